@@ -1,0 +1,98 @@
+// common.cuh -- shared definitions of the libbsgpu.so kernels (sm_100a).
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+
+#include "bsgpu.h"
+
+namespace bsg {
+
+constexpr uint32_t kRansL = 1u << 16;       // rANS lower bound, 16-bit renorm
+constexpr uint32_t kFull = 0xFFFFFFFFu;
+
+// ---- bf16_exp_chunked_v1 layout (little-endian; sections in this order, each
+// 16-byte aligned):
+//   0 "BSXC" | 4 u16 version=1 | 6 u8 coder (0 rANS, 1 tANS) | 7 u8 P
+//   8 u64 n | 16 u32 chunk_elems | 20 u32 n_chunks | 24 u32 lanes=32 | 28 u32 0
+//   32 u64 chunks_off | 40 u64 plane_off | 48 u64 blob_bytes | 56 u64 0
+//   64 u16 freq[256] | 576 u32 chunk_start[n_chunks+1] (16 B units)
+//   plane_off = rup16(576 + 4*(n_chunks+1)): n bytes of (sign << 7) | mantissa
+//   chunks_off = plane_off + rup16(n): per chunk [u32 init[32]][u16 words...]
+//   zero-padded to 16 B; blob_bytes = end of the last chunk record.
+constexpr uint32_t kXcMagic = 0x43585342u;  // "BSXC" little-endian
+constexpr uint32_t kXcFreqOff = 64;
+constexpr uint32_t kXcTabOff = 576;
+constexpr uint32_t kXcLanes = 32;
+constexpr uint32_t kXcMaxTable = 4096;      // 2^12 entries, the largest precision
+
+// Device-side tensor descriptor of a decode plan.  The host fills the first
+// block; the table-build kernel fills the parsed header fields.
+struct XcTensorDev {
+    const uint8_t *blob;
+    uint64_t blob_bytes;
+    uint16_t *out;
+    uint64_t n;
+    uint32_t chunk_elems;
+    uint32_t n_chunks;
+    // parsed from the blob header by xc_prepare_kernel
+    uint64_t chunks_off;
+    uint64_t plane_off;
+    uint32_t coder;
+    uint32_t prec;
+};
+
+// A work item: up to kXcWarps consecutive chunks of one tensor, one CTA.
+struct XcItem {
+    uint32_t tensor;
+    uint32_t first_chunk;
+    uint32_t n_chunks;
+    uint32_t pad;
+};
+
+// ---- bf16_parallel_v1 job descriptors --------------------------------------
+// One serial rANS stream (bigsmall/codecs/rans.py:165-207 semantics).
+struct ParJob {
+    uint64_t data_off;    // byte offset of the stream in the blob
+    uint32_t data_len;    // stream bytes actually present (python slice clamps)
+    uint32_t n_syms;      // symbols to decode
+    uint64_t out_off;     // element offset in the u16 (SE) or u8 (mantissa) scratch
+    uint32_t table;       // 0 = SE table, 1 + e = mantissa table of exponent e
+    uint32_t is_se;
+};
+
+// One PAR1 stream's merge parameters.
+struct ParStream {
+    uint64_t se_off;      // offset of its SE symbols in the u16 scratch
+    uint64_t mant_off;    // offset of its sorted mantissas in the u8 scratch
+    uint32_t n_in;        // elements in the stream
+    uint32_t k;           // stream index (element k + i * n_streams)
+    uint32_t bucket_first;// index of its first bucket count in ParPlan::bucket_counts
+    uint32_t n_buckets;
+};
+
+}  // namespace bsg
+
+// kernel launchers (host side, defined in the .cu files)
+namespace bsg {
+cudaError_t launch_xc_prepare(XcTensorDev *d_tens, int n_tensors, uint32_t *d_tables,
+                              uint32_t *d_errs, cudaStream_t s);
+cudaError_t launch_xc_decode(const XcTensorDev *d_tens, const XcItem *d_items, int n_items,
+                             const uint32_t *d_tables, uint32_t *d_errs, cudaStream_t s);
+int xc_warps_per_cta();
+
+cudaError_t launch_par_jobs(const uint8_t *d_blob, const ParJob *d_jobs, int n_jobs,
+                            const uint2 *d_se_tab, const uint2 *d_m_tabs, uint16_t *d_se_sym,
+                            uint8_t *d_mant, uint32_t *d_err, cudaStream_t s);
+cudaError_t launch_par_merge(const ParStream *d_streams, int n_streams_total,
+                             const uint32_t *d_bucket_exp_counts, const uint16_t *d_se_sym,
+                             const uint8_t *d_mant, uint16_t *d_out, uint32_t n_streams,
+                             uint32_t *d_err, cudaStream_t s);
+
+cudaError_t launch_xc_encode(const uint16_t *d_in, uint64_t n, int coder, int prec,
+                             uint32_t chunk_elems, uint8_t *d_out, uint64_t out_cap,
+                             uint64_t *d_out_len, uint8_t *d_ws, uint64_t ws_bytes,
+                             cudaStream_t s);
+uint64_t xc_encode_workspace(uint64_t n, uint32_t chunk_elems);
+uint64_t xc_encode_bound(uint64_t n, uint32_t chunk_elems);
+}  // namespace bsg

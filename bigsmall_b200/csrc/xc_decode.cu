@@ -1,0 +1,418 @@
+// xc_decode.cu -- sm_100a decoder of bf16_exp_chunked_v1 tensors.
+//
+// Format (this project's; the reference has no chunked codec -- its bf16
+// codecs code the joint (sign,exponent) symbol serially, e.g.
+// bigsmall/codecs/single_kernel.py:194-428):
+//   * the 8-bit exponent of every bf16 value is entropy coded, rANS (32-bit
+//     state, L = 2^16, 16-bit renorm, M = 2^P) or tANS (table of 2^P states);
+//   * sign and mantissa are kept raw as one byte per value, (s << 7) | m, in a
+//     byte plane that is merged back with 16-byte vector loads/stores;
+//   * the tensor is cut into chunks of chunk_elems values; each chunk is one
+//     "state group": 32 interleaved coder states (one per lane of a warp)
+//     sharing one u16 word stream stored in consumption order.  Lane l owns
+//     chunk elements g*256 + l*8 + j (group g, sub-step j < 8), so after 8
+//     steps a lane holds 8 consecutive values and writes them as one 16-byte
+//     store.  At each step the lanes needing a word take them in lane order:
+//     word index = base + popc(ballot & lanemask_lt)  (Giesen's interleaved
+//     rANS construction with a warp-shared stream).
+//
+// Kernels:
+//   xc_prepare_kernel  one CTA per tensor: validates the blob header against the
+//                      plan descriptor, builds the 2^P-entry decode table into
+//                      the plan's workspace and checks the chunk offset table.
+//   xc_decode_kernel   one CTA per work item (<= 8 chunks of one tensor): copies
+//                      the table into shared memory, then each warp decodes one
+//                      chunk.  Compressed words are staged per warp in a 2 KiB
+//                      shared-memory ring fed by 16-byte cp.async copies; the
+//                      sign/mantissa plane is read with 8-byte loads two groups
+//                      ahead; output leaves as 16-byte streaming stores.
+#include <cstdint>
+
+#include "common.cuh"
+
+namespace bsg {
+
+constexpr int kWarps = 8;                   // warps (= chunks) per CTA
+constexpr int kThreads = kWarps * 32;
+constexpr uint32_t kRingBytes = 2048;       // per-warp staging ring
+constexpr uint32_t kRingWords = kRingBytes / 2;
+constexpr uint32_t kFill = 512;             // bytes per refill: 32 lanes x 16 B
+
+int xc_warps_per_cta() { return kWarps; }
+
+__device__ __forceinline__ uint32_t lanemask_lt() {
+    uint32_t m;
+    asm("mov.u32 %0, %%lanemask_lt;" : "=r"(m));
+    return m;
+}
+
+__device__ __forceinline__ void cp_async16(void *smem, const void *gmem) {
+    uint32_t s = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(s), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;\n" ::: "memory"); }
+
+__device__ __forceinline__ uint2 ld_plane8(const uint8_t *p) {
+    uint2 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p));
+    return v;
+}
+
+__device__ __forceinline__ void st_out16(uint16_t *p, uint4 v) {
+    asm volatile("st.global.cs.v4.u32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(v.x), "r"(v.y), "r"(v.z),
+                 "r"(v.w)
+                 : "memory");
+}
+
+// Two bf16 words from two exponent symbols and two sign|mantissa bytes packed
+// as bytes 0 and 2 of `sm2` (bytes 1 and 3 zero).
+__device__ __forceinline__ uint32_t merge2(uint32_t e0, uint32_t e1, uint32_t sm2) {
+    uint32_t ep = __byte_perm(e0, e1, 0x5410);          // e0 | e1 << 16
+    return (sm2 & 0x007F007Fu) | ((sm2 << 8) & 0x80008000u) | (ep << 7);
+}
+
+__device__ __forceinline__ uint16_t merge1(uint32_t e, uint32_t sm) {
+    return static_cast<uint16_t>(((sm & 0x80u) << 8) | (e << 7) | (sm & 0x7Fu));
+}
+
+// --------------------------------------------------------------------------
+// table build
+// --------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) xc_prepare_kernel(XcTensorDev *tens, uint32_t *tables,
+                                                         uint32_t *errs) {
+    const int t = blockIdx.x;
+    const int tid = threadIdx.x;
+    XcTensorDev &T = tens[t];
+    __shared__ uint32_t s_err, s_prec, s_coder;
+    __shared__ uint64_t s_chunks_off, s_plane_off, s_total;
+    __shared__ uint32_t s_freq[256], s_cum[257];
+    __shared__ uint32_t s_next[256];
+    __shared__ uint8_t s_spread[kXcMaxTable];
+    const uint8_t *b = T.blob;
+    if (tid == 0) {
+        uint32_t err = 0;
+        if (T.blob_bytes < kXcTabOff || (reinterpret_cast<uintptr_t>(b) & 15)) {
+            err = BS_DEV_HEADER;
+        } else {
+            const uint32_t *h32 = reinterpret_cast<const uint32_t *>(b);
+            const uint64_t *h64 = reinterpret_cast<const uint64_t *>(b);
+            uint32_t ver_coder_prec = h32[1];
+            uint32_t ver = ver_coder_prec & 0xFFFF, coder = (ver_coder_prec >> 16) & 0xFF;
+            uint32_t prec = ver_coder_prec >> 24;
+            uint64_t n = h64[1];
+            uint32_t ce = h32[4], nc = h32[5], lanes = h32[6];
+            uint64_t co = h64[4], po = h64[5], total = h64[6];
+            const uint64_t po_want = (kXcTabOff + 4ull * (nc + 1ull) + 15) & ~15ull;
+            if (h32[0] != kXcMagic || ver != 1 || coder > 1 || prec < 8 || prec > 12 || n != T.n ||
+                ce != T.chunk_elems || nc != T.n_chunks || lanes != kXcLanes || po != po_want ||
+                co != po + ((n + 15) & ~15ull) || total < co || (total & 15) || total > T.blob_bytes)
+                err = BS_DEV_HEADER;
+            s_total = total;
+            s_prec = prec;
+            s_coder = coder;
+            s_chunks_off = co;
+            s_plane_off = po;
+        }
+        s_err = err;
+    }
+    __syncthreads();
+    if (s_err) {
+        if (tid == 0) {
+            errs[t] = s_err;
+            T.coder = 0xFFFFFFFFu;
+        }
+        return;
+    }
+    const uint32_t P = s_prec, M = 1u << P, coder = s_coder;
+    // frequencies and their exclusive prefix sum
+    const uint16_t *fr = reinterpret_cast<const uint16_t *>(b + kXcFreqOff);
+    uint32_t f = fr[tid];
+    s_freq[tid] = f;
+    __syncthreads();
+    if (tid < 32) {
+        // warp scan over 256 entries, 8 per lane
+        uint32_t loc[8], sum = 0;
+#pragma unroll
+        for (int k = 0; k < 8; k++) {
+            loc[k] = sum;
+            sum += s_freq[tid * 8 + k];
+        }
+        uint32_t incl = sum;
+#pragma unroll
+        for (int d = 1; d < 32; d <<= 1) {
+            uint32_t v = __shfl_up_sync(kFull, incl, d);
+            if (tid >= d) incl += v;
+        }
+        uint32_t excl = incl - sum;
+#pragma unroll
+        for (int k = 0; k < 8; k++) s_cum[tid * 8 + k] = excl + loc[k];
+        if (tid == 31) s_cum[256] = incl;
+    }
+    __syncthreads();
+    if (s_cum[256] != M || (coder == 0 && f >= M)) {
+        if (tid == 0 || f >= M) atomicOr(&s_err, BS_DEV_FREQ);
+    }
+    __syncthreads();
+    if (s_err) {
+        if (tid == 0) {
+            errs[t] = s_err;
+            T.coder = 0xFFFFFFFFu;
+        }
+        return;
+    }
+    uint32_t *tab = tables + static_cast<uint64_t>(t) * kXcMaxTable;
+    if (coder == 0) {
+        // rANS entry: sym | freq << 8 | (slot - cum) << 20; 16 slots per thread
+        const uint32_t per = (M + 255) / 256;
+        uint32_t s0 = tid * per;
+        if (s0 < M) {
+            int lo = 0, hi = 255;   // largest s with cum[s] <= s0
+            while (lo < hi) {
+                int mid = (lo + hi + 1) >> 1;
+                if (s_cum[mid] <= s0) lo = mid; else hi = mid - 1;
+            }
+            uint32_t s = lo;
+            for (uint32_t k = 0; k < per && s0 + k < M; k++) {
+                uint32_t slot = s0 + k;
+                while (s_cum[s + 1] <= slot) s++;
+                tab[slot] = s | (s_freq[s] << 8) | ((slot - s_cum[s]) << 20);
+            }
+        }
+    } else {
+        // tANS: spread symbol occurrences with Collet's step, then give each
+        // slot (in increasing order) its next state value x in [f, 2f)
+        const uint32_t step = (M >> 1) + (M >> 3) + 3, mask = M - 1;
+        for (uint32_t k = tid; k < M; k += blockDim.x) {
+            int lo = 0, hi = 255;
+            while (lo < hi) {
+                int mid = (lo + hi + 1) >> 1;
+                if (s_cum[mid] <= k) lo = mid; else hi = mid - 1;
+            }
+            s_spread[(k * step) & mask] = static_cast<uint8_t>(lo);
+        }
+        s_next[tid] = s_freq[tid];
+        __syncthreads();
+        if (tid < 32) {
+            const uint32_t lt = lanemask_lt();
+            for (uint32_t i0 = 0; i0 < M; i0 += 32) {
+                uint32_t i = i0 + tid;
+                uint32_t s = s_spread[i];
+                uint32_t grp = __match_any_sync(kFull, s);
+                uint32_t xs = s_next[s] + __popc(grp & lt);
+                __syncwarp();
+                if ((grp & lt) == 0) s_next[s] += __popc(grp);
+                __syncwarp();
+                uint32_t nb = P - (31 - __clz(xs));
+                uint32_t base = (xs << nb) - M;
+                tab[i] = s | (nb << 8) | (base << 12);
+            }
+        }
+    }
+    // chunk offset table: monotone, >= 128 B per record, inside [chunks_off, total)
+    const uint32_t *cs = reinterpret_cast<const uint32_t *>(b + kXcTabOff);
+    const uint64_t lim16 = (s_total - s_chunks_off) >> 4;
+    for (uint32_t c = tid; c < T.n_chunks; c += blockDim.x) {
+        uint32_t a = cs[c], z = cs[c + 1];
+        if (z < a + 8 || z > lim16) atomicOr(&s_err, BS_DEV_CHUNK_TABLE);
+    }
+    __syncthreads();
+    if (tid == 0) {
+        errs[t] = s_err;
+        T.coder = s_err ? 0xFFFFFFFFu : coder;
+        T.prec = P;
+        T.chunks_off = s_chunks_off;
+        T.plane_off = s_plane_off;
+    }
+}
+
+// --------------------------------------------------------------------------
+// chunk decode
+// --------------------------------------------------------------------------
+struct Ring {
+    uint8_t *buf;            // this warp's kRingBytes of shared memory
+    const uint8_t *src;      // first renorm word of the chunk record
+    uint32_t bytes;          // renorm bytes in the record (multiple of 16)
+    uint32_t fetched;        // bytes requested so far (multiple of kFill)
+    uint32_t landed;         // bytes known to be in shared memory
+};
+
+__device__ __forceinline__ void ring_issue(Ring &r, uint32_t lane) {
+    uint32_t off = r.fetched + 16 * lane;
+    if (off < r.bytes) cp_async16(r.buf + (off & (kRingBytes - 1)), r.src + off);
+    cp_async_commit();
+    r.fetched += kFill;
+}
+
+// make bytes [0, min(bytes, consumed + kFill)) visible to the whole warp
+__device__ __forceinline__ void ring_ensure(Ring &r, uint32_t consumed_bytes) {
+    uint32_t need = consumed_bytes + kFill;
+    if (need > r.bytes) need = r.bytes;
+    if (need > r.landed) {
+        cp_async_wait_all();
+        __syncwarp();
+        r.landed = r.fetched;
+    }
+}
+
+// top up the ring after a group: one kFill refill if its slot is consumed
+__device__ __forceinline__ void ring_refill(Ring &r, uint32_t consumed_bytes, uint32_t lane) {
+    if (r.fetched < r.bytes && r.fetched + kFill - consumed_bytes <= kRingBytes) {
+        __syncwarp();
+        ring_issue(r, lane);
+    }
+}
+
+template <int CODER>
+__device__ __forceinline__ void decode_chunk(const uint32_t *__restrict__ s_tab, uint8_t *ring_buf,
+                                             const uint8_t *__restrict__ rec, uint32_t rec_bytes,
+                                             const uint8_t *__restrict__ plane,
+                                             uint16_t *__restrict__ out, uint32_t cn, uint32_t P,
+                                             uint32_t *err) {
+    const uint32_t lane = threadIdx.x & 31;
+    const uint32_t lt = lanemask_lt();
+    const uint32_t smask = (1u << P) - 1;
+    const uint16_t *ring16 = reinterpret_cast<const uint16_t *>(ring_buf);
+
+    uint32_t init = reinterpret_cast<const uint32_t *>(rec)[lane];
+    // coder state: rANS x; tANS (st, buf, cnt)
+    uint32_t x = init, st = init & 0xFFFF, bits = init >> 16, cnt = 16;
+    (void)st; (void)bits; (void)cnt;
+
+    Ring r{ring_buf, rec + 128, rec_bytes - 128, 0, 0};
+#pragma unroll
+    for (int k = 0; k < (int)(kRingBytes / kFill); k++) ring_issue(r, lane);
+
+    uint32_t base = 0;   // words consumed by the warp (uniform)
+    const uint32_t G = cn >> 8, rem = cn & 255;
+
+    auto step = [&](bool active) -> uint32_t {
+        uint32_t sym;
+        if (CODER == 0) {
+            uint32_t t = active ? s_tab[x & smask] : 0u;
+            sym = t & 0xFF;
+            uint32_t nx = ((t >> 8) & 0xFFF) * (x >> P) + (t >> 20);
+            if (active) x = nx;
+            bool need = active && (x < kRansL);
+            uint32_t m = __ballot_sync(kFull, need);
+            if (need) x = (x << 16) | ring16[(base + __popc(m & lt)) & (kRingWords - 1)];
+            base += __popc(m);
+        } else {
+            bool need = active && (cnt < P);
+            uint32_t m = __ballot_sync(kFull, need);
+            if (need) {
+                bits |= static_cast<uint32_t>(ring16[(base + __popc(m & lt)) & (kRingWords - 1)]) << cnt;
+                cnt += 16;
+            }
+            base += __popc(m);
+            uint32_t t = active ? s_tab[st] : 0u;
+            sym = t & 0xFF;
+            if (active) {
+                uint32_t nb = (t >> 8) & 0xF;
+                st = (t >> 12) + (bits & ((1u << nb) - 1));
+                bits >>= nb;
+                cnt -= nb;
+            }
+        }
+        return sym;
+    };
+
+    uint2 sm_a = make_uint2(0, 0), sm_b = make_uint2(0, 0);
+    if (G > 0) sm_a = ld_plane8(plane + lane * 8);
+    if (G > 1) sm_b = ld_plane8(plane + 256 + lane * 8);
+    for (uint32_t g = 0; g < G; g++) {
+        ring_ensure(r, base * 2);
+        uint2 sm = sm_a;
+        sm_a = sm_b;
+        if (g + 2 < G) sm_b = ld_plane8(plane + (g + 2) * 256 + lane * 8);
+        uint32_t e0 = step(true), e1 = step(true), e2 = step(true), e3 = step(true);
+        uint32_t e4 = step(true), e5 = step(true), e6 = step(true), e7 = step(true);
+        uint4 v;
+        v.x = merge2(e0, e1, __byte_perm(sm.x, 0, 0x4140));
+        v.y = merge2(e2, e3, __byte_perm(sm.x, 0, 0x4342));
+        v.z = merge2(e4, e5, __byte_perm(sm.y, 0, 0x4140));
+        v.w = merge2(e6, e7, __byte_perm(sm.y, 0, 0x4342));
+        st_out16(out + g * 256 + lane * 8, v);
+        ring_refill(r, base * 2, lane);
+    }
+    if (rem) {
+        ring_ensure(r, base * 2);
+        const uint32_t e_base = G * 256 + lane * 8;
+#pragma unroll 1
+        for (uint32_t j = 0; j < 8; j++) {
+            bool active = (lane * 8 + j) < rem;
+            uint32_t sym = step(active);
+            if (active) out[e_base + j] = merge1(sym, plane[e_base + j]);
+        }
+    }
+    cp_async_wait_all();
+    __syncwarp();
+    bool bad_state = CODER == 0 ? (x != kRansL) : (st != 0);
+    uint32_t used = base * 2;
+    bool bad_stream = used > r.bytes || (r.bytes - used) >= 16;
+    uint32_t code = (bad_state ? BS_DEV_FINAL_STATE : 0u) | (bad_stream ? BS_DEV_STREAM : 0u);
+    code = __reduce_or_sync(kFull, code);
+    if (code && lane == 0) atomicOr(err, code);
+}
+
+__global__ void __launch_bounds__(kThreads) xc_decode_kernel(const XcTensorDev *__restrict__ tens,
+                                                             const XcItem *__restrict__ items,
+                                                             const uint32_t *__restrict__ tables,
+                                                             uint32_t *errs) {
+    extern __shared__ __align__(16) uint8_t smem[];
+    uint32_t *s_tab = reinterpret_cast<uint32_t *>(smem);
+    uint8_t *s_ring = smem + kXcMaxTable * 4;
+
+    const XcItem it = items[blockIdx.x];
+    const XcTensorDev &T = tens[it.tensor];
+    const uint32_t coder = T.coder;
+    if (coder > 1) return;   // the table build flagged this tensor
+    const uint32_t P = T.prec;
+    const uint32_t M = 1u << P;
+    const uint4 *src = reinterpret_cast<const uint4 *>(tables + static_cast<uint64_t>(it.tensor) * kXcMaxTable);
+    for (uint32_t i = threadIdx.x; i < M / 4; i += kThreads) reinterpret_cast<uint4 *>(s_tab)[i] = src[i];
+    __syncthreads();
+
+    const uint32_t warp = threadIdx.x >> 5;
+    if (warp >= it.n_chunks) return;
+    const uint32_t c = it.first_chunk + warp;
+    const uint8_t *blob = T.blob;
+    const uint32_t *cs = reinterpret_cast<const uint32_t *>(blob + kXcTabOff);
+    const uint32_t a = cs[c], z = cs[c + 1];
+    const uint8_t *rec = blob + T.chunks_off + 16ull * a;
+    const uint32_t rec_bytes = 16u * (z - a);
+    const uint64_t e0 = static_cast<uint64_t>(c) * T.chunk_elems;
+    const uint64_t left = T.n - e0;
+    const uint32_t cn = left < T.chunk_elems ? static_cast<uint32_t>(left) : T.chunk_elems;
+    uint8_t *ring = s_ring + warp * kRingBytes;
+    const uint8_t *plane = blob + T.plane_off + e0;
+    uint16_t *out = T.out + e0;
+    if (coder == 0)
+        decode_chunk<0>(s_tab, ring, rec, rec_bytes, plane, out, cn, P, &errs[it.tensor]);
+    else
+        decode_chunk<1>(s_tab, ring, rec, rec_bytes, plane, out, cn, P, &errs[it.tensor]);
+}
+
+cudaError_t launch_xc_prepare(XcTensorDev *d_tens, int n_tensors, uint32_t *d_tables, uint32_t *d_errs,
+                              cudaStream_t s) {
+    if (n_tensors <= 0) return cudaSuccess;
+    xc_prepare_kernel<<<n_tensors, 256, 0, s>>>(d_tens, d_tables, d_errs);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_xc_decode(const XcTensorDev *d_tens, const XcItem *d_items, int n_items,
+                             const uint32_t *d_tables, uint32_t *d_errs, cudaStream_t s) {
+    if (n_items <= 0) return cudaSuccess;
+    const size_t smem = kXcMaxTable * 4 + kWarps * kRingBytes;
+    static bool attr_set = false;   // idempotent; a benign race
+    if (!attr_set) {
+        cudaError_t e = cudaFuncSetAttribute(xc_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             static_cast<int>(smem));
+        if (e != cudaSuccess) return e;
+        attr_set = true;
+    }
+    xc_decode_kernel<<<n_items, kThreads, smem, s>>>(d_tens, d_items, d_tables, d_errs);
+    return cudaGetLastError();
+}
+
+}  // namespace bsg

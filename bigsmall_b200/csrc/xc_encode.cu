@@ -1,0 +1,322 @@
+// xc_encode.cu -- sm_100a encoder of bf16_exp_chunked_v1 (used for KV-cache
+// compression and to build containers on the device).
+//
+// The reference compresses KV entries on the CPU after a device->host copy
+// (bigsmall/codecs/kv_cache.py:24-29, :64-69).  Here the bf16 tensor never
+// leaves HBM:
+//   1. xc_enc_hist_kernel    exponent histogram (per-warp shared-memory bins)
+//                            and the sign|mantissa byte plane, one pass.
+//   2. xc_enc_setup_kernel   deterministic frequency quantisation (the same
+//                            rule as the CPU reference encoder), blob header,
+//                            per-symbol encode table.
+//   3. xc_enc_chunks_kernel  one warp per chunk: the 32 interleaved rANS states
+//                            run backwards over the chunk; renorm words are
+//                            written from the end of a per-chunk scratch slot
+//                            downwards so they land in decode order.
+//   4. xc_enc_scan_kernel    exclusive scan of record sizes -> chunk table and
+//                            blob length.
+//   5. xc_enc_compact_kernel copy every record from its scratch slot into the
+//                            blob.
+// Output bytes equal the CPU reference encoder's for the same input.
+#include <cstdint>
+
+#include "common.cuh"
+
+namespace bsg {
+
+namespace {
+constexpr int kEncWarps = 8;
+constexpr uint64_t kWsCounts = 0;       // u64[256]
+constexpr uint64_t kWsTab = 2048;       // u32[256]: freq | cum << 16
+constexpr uint64_t kWsFlags = 3072;     // u32 flags
+constexpr uint64_t kWsRec = 4096;       // u32[n_chunks]: words per record
+
+inline uint64_t rup(uint64_t x, uint64_t a) { return (x + a - 1) / a * a; }
+inline uint64_t slot_bytes(uint32_t ce) { return rup(128 + 2ull * ce, 16); }
+inline uint64_t slots_off(uint64_t nc) { return rup(kWsRec + 4 * nc, 256); }
+}  // namespace
+
+uint64_t xc_encode_workspace(uint64_t n, uint32_t ce) {
+    uint64_t nc = (n + ce - 1) / ce;
+    return slots_off(nc) + nc * slot_bytes(ce);
+}
+
+uint64_t xc_encode_bound(uint64_t n, uint32_t ce) {
+    uint64_t nc = (n + ce - 1) / ce;
+    uint64_t plane_off = rup(kXcTabOff + 4 * (nc + 1), 16);
+    return plane_off + rup(n, 16) + nc * slot_bytes(ce);
+}
+
+__device__ __forceinline__ uint32_t lanemask_gt_e() {
+    uint32_t m;
+    asm("mov.u32 %0, %%lanemask_gt;" : "=r"(m));
+    return m;
+}
+
+// 1. histogram + plane ------------------------------------------------------
+__global__ void __launch_bounds__(256) xc_enc_hist_kernel(const uint16_t *__restrict__ in, uint64_t n,
+                                                          unsigned long long *counts,
+                                                          uint8_t *__restrict__ plane) {
+    __shared__ uint32_t h[8][256];
+    const uint32_t w = threadIdx.x >> 5;
+    for (int i = threadIdx.x; i < 8 * 256; i += 256) (&h[0][0])[i] = 0;
+    __syncthreads();
+    const uint64_t n8 = n / 8;
+    const uint64_t stride = static_cast<uint64_t>(gridDim.x) * blockDim.x;
+    for (uint64_t q = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; q < n8; q += stride) {
+        uint4 v = reinterpret_cast<const uint4 *>(in)[q];
+        uint32_t wv[4] = {v.x, v.y, v.z, v.w};
+        uint32_t pl[2] = {0, 0};
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            uint32_t lo = wv[k] & 0xFFFF, hi = wv[k] >> 16;
+            atomicAdd(&h[w][(lo >> 7) & 0xFF], 1u);
+            atomicAdd(&h[w][(hi >> 7) & 0xFF], 1u);
+            uint32_t b0 = ((lo >> 8) & 0x80) | (lo & 0x7F), b1 = ((hi >> 8) & 0x80) | (hi & 0x7F);
+            pl[k >> 1] |= (b0 | (b1 << 8)) << ((k & 1) * 16);
+        }
+        reinterpret_cast<uint2 *>(plane)[q] = make_uint2(pl[0], pl[1]);
+    }
+    if (blockIdx.x == 0) {
+        for (uint64_t i = n8 * 8 + threadIdx.x; i < n; i += blockDim.x) {
+            uint32_t v = in[i];
+            atomicAdd(&h[w][(v >> 7) & 0xFF], 1u);
+            plane[i] = static_cast<uint8_t>(((v >> 8) & 0x80) | (v & 0x7F));
+        }
+    }
+    __syncthreads();
+    uint32_t s = 0;
+#pragma unroll
+    for (int k = 0; k < 8; k++) s += h[k][threadIdx.x];
+    if (s) atomicAdd(&counts[threadIdx.x], static_cast<unsigned long long>(s));
+}
+
+// 2. quantise + header -----------------------------------------------------
+// Same rule as the CPU reference encoder of the format: f = max(1, c*M/total)
+// for present symbols; a positive remainder goes to the most frequent symbol
+// (lowest index on ties); an excess is taken from the most frequent symbols,
+// never below 1; a single present symbol gets M-1 plus a phantom neighbour.
+__global__ void __launch_bounds__(256) xc_enc_setup_kernel(const unsigned long long *counts, uint64_t n,
+                                                           int coder, int prec, uint32_t ce, uint32_t nc,
+                                                           uint8_t *out, uint32_t *enc_tab) {
+    __shared__ int64_t f[256];
+    __shared__ uint32_t s_cum[256];
+    const int tid = threadIdx.x;
+    const int64_t M = 1ll << prec;
+    if (tid == 0) {
+        int nnz = 0, first = -1;
+        unsigned long long total = 0;
+        for (int s = 0; s < 256; s++)
+            if (counts[s]) { nnz++; total += counts[s]; if (first < 0) first = s; }
+        for (int s = 0; s < 256; s++) f[s] = 0;
+        if (nnz <= 1) {
+            int s = first < 0 ? 0 : first;
+            f[s] = M - 1;
+            f[(s + 1) & 255] = 1;
+        } else {
+            int64_t sum = 0;
+            for (int s = 0; s < 256; s++) {
+                unsigned long long cs = counts[s];
+                // cs < 2^51 for any tensor that fits in memory, so cs*M fits in 64 bits
+                int64_t v = cs ? static_cast<int64_t>((cs * static_cast<unsigned long long>(M)) / total) : 0;
+                if (cs && v == 0) v = 1;
+                f[s] = v;
+                sum += v;
+            }
+            int64_t diff = M - sum;
+            if (diff > 0) {
+                int best = 0;
+                for (int s = 1; s < 256; s++) if (f[s] > f[best]) best = s;
+                f[best] += diff;
+            }
+            while (diff < 0) {
+                int best = 0;
+                for (int s = 1; s < 256; s++) if (f[s] > f[best]) best = s;
+                int64_t take = f[best] - 1 < -diff ? f[best] - 1 : -diff;
+                f[best] -= take;
+                diff += take;
+            }
+        }
+        uint32_t cum = 0;
+        for (int s = 0; s < 256; s++) { s_cum[s] = cum; cum += static_cast<uint32_t>(f[s]); }
+    }
+    __syncthreads();
+    // header
+    const uint64_t plane_off = (kXcTabOff + 4ull * (nc + 1ull) + 15) & ~15ull;
+    const uint64_t chunks_off = plane_off + ((n + 15) & ~15ull);
+    if (tid == 0) {
+        uint32_t *h32 = reinterpret_cast<uint32_t *>(out);
+        uint64_t *h64 = reinterpret_cast<uint64_t *>(out);
+        h32[0] = kXcMagic;
+        h32[1] = 1u | (static_cast<uint32_t>(coder) << 16) | (static_cast<uint32_t>(prec) << 24);
+        h64[1] = n;
+        h32[4] = ce;
+        h32[5] = nc;
+        h32[6] = kXcLanes;
+        h32[7] = 0;
+        h64[4] = chunks_off;
+        h64[5] = plane_off;
+        h64[7] = 0;
+    }
+    reinterpret_cast<uint16_t *>(out + kXcFreqOff)[tid] = static_cast<uint16_t>(f[tid]);
+    // zero the two alignment pads
+    const uint64_t tab_end = kXcTabOff + 4ull * (nc + 1ull);
+    if (tab_end + tid < plane_off) out[tab_end + tid] = 0;
+    if (plane_off + n + tid < chunks_off) out[plane_off + n + tid] = 0;
+    enc_tab[tid] = static_cast<uint32_t>(f[tid]) | (s_cum[tid] << 16);
+}
+
+// 3. per-chunk reverse rANS ---------------------------------------------------
+__global__ void __launch_bounds__(kEncWarps * 32) xc_enc_chunks_kernel(
+    const uint16_t *__restrict__ in, uint64_t n, uint32_t ce, uint32_t nc, int prec,
+    const uint32_t *__restrict__ enc_tab, uint8_t *__restrict__ slots, uint64_t slot_b,
+    uint32_t *__restrict__ rec_words) {
+    __shared__ uint32_t s_tab[256];
+    s_tab[threadIdx.x] = enc_tab[threadIdx.x];
+    __syncthreads();
+    const uint32_t lane = threadIdx.x & 31;
+    const uint32_t c = blockIdx.x * kEncWarps + (threadIdx.x >> 5);
+    if (c >= nc) return;
+    const uint32_t P = static_cast<uint32_t>(prec);
+    const uint64_t e0 = static_cast<uint64_t>(c) * ce;
+    const uint32_t cn = (n - e0) < ce ? static_cast<uint32_t>(n - e0) : ce;
+    const uint16_t *src = in + e0;
+    uint8_t *slot = slots + static_cast<uint64_t>(c) * slot_b;
+    uint16_t *wend = reinterpret_cast<uint16_t *>(slot + slot_b);   // words grow downwards
+    const uint32_t gt = lanemask_gt_e();
+    uint32_t x = kRansL;
+    uint32_t cur = 0;
+    const uint32_t G = cn >> 8, rem = cn & 255;
+
+    auto enc = [&](uint32_t v, bool active) {
+        const uint32_t sym = (v >> 7) & 0xFF;
+        const uint32_t t = s_tab[sym];
+        const uint32_t f = t & 0xFFFF, cf = t >> 16;
+        const bool emit = active && (static_cast<uint64_t>(x) >= (static_cast<uint64_t>(f) << (32 - P)));
+        const uint32_t m = __ballot_sync(kFull, emit);
+        if (emit) {
+            wend[-1 - static_cast<int64_t>(cur + __popc(m & gt))] = static_cast<uint16_t>(x & 0xFFFF);
+            x >>= 16;
+        }
+        cur += __popc(m);
+        if (active) {
+            const uint32_t q = x / f;
+            x = (q << P) + (x - q * f) + cf;
+        }
+    };
+
+    if (rem) {
+        const uint32_t eb = G * 256 + lane * 8;
+        uint32_t v[8];
+#pragma unroll
+        for (int j = 0; j < 8; j++) v[j] = (lane * 8 + j < rem) ? src[eb + j] : 0u;
+#pragma unroll
+        for (int j = 7; j >= 0; j--) enc(v[j], lane * 8 + j < rem);
+    }
+    uint4 nxt = make_uint4(0, 0, 0, 0);
+    if (G > 0) nxt = reinterpret_cast<const uint4 *>(src + (G - 1) * 256 + lane * 8)[0];
+    for (int g = static_cast<int>(G) - 1; g >= 0; g--) {
+        const uint4 v = nxt;
+        if (g > 0) nxt = reinterpret_cast<const uint4 *>(src + (g - 1) * 256 + lane * 8)[0];
+        enc(v.w >> 16, true);
+        enc(v.w & 0xFFFF, true);
+        enc(v.z >> 16, true);
+        enc(v.z & 0xFFFF, true);
+        enc(v.y >> 16, true);
+        enc(v.y & 0xFFFF, true);
+        enc(v.x >> 16, true);
+        enc(v.x & 0xFFFF, true);
+    }
+    reinterpret_cast<uint32_t *>(slot)[lane] = x;
+    if (lane == 0) rec_words[c] = cur;
+}
+
+// 4. record offsets -----------------------------------------------------------
+__global__ void __launch_bounds__(1024) xc_enc_scan_kernel(const uint32_t *__restrict__ rec_words, uint32_t nc,
+                                                           uint8_t *out, uint64_t chunks_off, uint64_t out_cap,
+                                                           unsigned long long *out_len, uint32_t *flags) {
+    __shared__ uint64_t s_part[1024];
+    const uint32_t tid = threadIdx.x;
+    const uint32_t per = (nc + 1023) / 1024;
+    const uint32_t lo = tid * per, hi = min(nc, lo + per);
+    uint64_t sum = 0;
+    for (uint32_t c = lo; c < hi; c++) sum += (128u + 2u * rec_words[c] + 15u) >> 4;
+    s_part[tid] = sum;
+    __syncthreads();
+    for (uint32_t d = 1; d < 1024; d <<= 1) {
+        uint64_t v = tid >= d ? s_part[tid - d] : 0;
+        __syncthreads();
+        s_part[tid] += v;
+        __syncthreads();
+    }
+    uint64_t run = s_part[tid] - sum;   // exclusive
+    uint32_t *tab = reinterpret_cast<uint32_t *>(out + kXcTabOff);
+    for (uint32_t c = lo; c < hi; c++) {
+        tab[c] = static_cast<uint32_t>(run);
+        run += (128u + 2u * rec_words[c] + 15u) >> 4;
+    }
+    if (tid == 1023) {
+        const uint64_t total16 = s_part[1023];
+        tab[nc] = static_cast<uint32_t>(total16);
+        const uint64_t total = chunks_off + 16 * total16;
+        if (total > out_cap) {
+            *flags = 1;
+            *out_len = 0;
+        } else {
+            *flags = 0;
+            reinterpret_cast<uint64_t *>(out)[6] = total;
+            *out_len = total;
+        }
+    }
+}
+
+// 5. compaction -----------------------------------------------------------------
+__global__ void __launch_bounds__(256) xc_enc_compact_kernel(const uint8_t *__restrict__ slots, uint64_t slot_b,
+                                                             const uint32_t *__restrict__ rec_words,
+                                                             uint8_t *out, uint64_t chunks_off,
+                                                             const uint32_t *flags) {
+    if (*flags) return;
+    const uint32_t c = blockIdx.x;
+    const uint32_t W = rec_words[c];
+    const uint32_t start16 = reinterpret_cast<const uint32_t *>(out + kXcTabOff)[c];
+    uint8_t *dst = out + chunks_off + 16ull * start16;
+    const uint8_t *slot = slots + static_cast<uint64_t>(c) * slot_b;
+    if (threadIdx.x < 32)
+        reinterpret_cast<uint32_t *>(dst)[threadIdx.x] = reinterpret_cast<const uint32_t *>(slot)[threadIdx.x];
+    const uint16_t *ws = reinterpret_cast<const uint16_t *>(slot + slot_b) - W;
+    uint16_t *wd = reinterpret_cast<uint16_t *>(dst + 128);
+    const uint32_t padded = ((128u + 2u * W + 15u) & ~15u) - 128u;   // bytes incl. zero pad
+    for (uint32_t i = threadIdx.x; i < padded / 2; i += blockDim.x) wd[i] = i < W ? ws[i] : 0;
+}
+
+cudaError_t launch_xc_encode(const uint16_t *d_in, uint64_t n, int coder, int prec, uint32_t ce,
+                             uint8_t *d_out, uint64_t out_cap, uint64_t *d_out_len, uint8_t *d_ws,
+                             uint64_t ws_bytes, cudaStream_t s) {
+    const uint64_t nc = (n + ce - 1) / ce;
+    auto *counts = reinterpret_cast<unsigned long long *>(d_ws + kWsCounts);
+    auto *tab = reinterpret_cast<uint32_t *>(d_ws + kWsTab);
+    auto *flags = reinterpret_cast<uint32_t *>(d_ws + kWsFlags);
+    auto *recw = reinterpret_cast<uint32_t *>(d_ws + kWsRec);
+    uint8_t *slots = d_ws + slots_off(nc);
+    const uint64_t sb = slot_bytes(ce);
+    const uint64_t plane_off = rup(kXcTabOff + 4 * (nc + 1), 16);
+    const uint64_t chunks_off = plane_off + rup(n, 16);
+    cudaError_t e = cudaMemsetAsync(counts, 0, 2048, s);
+    if (e != cudaSuccess) return e;
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    uint64_t want = (n / 8 + 255) / 256;
+    int grid = static_cast<int>(want < static_cast<uint64_t>(sms) * 8 ? (want ? want : 1) : static_cast<uint64_t>(sms) * 8);
+    xc_enc_hist_kernel<<<grid, 256, 0, s>>>(d_in, n, counts, d_out + plane_off);
+    xc_enc_setup_kernel<<<1, 256, 0, s>>>(counts, n, coder, prec, ce, static_cast<uint32_t>(nc), d_out, tab);
+    xc_enc_chunks_kernel<<<static_cast<unsigned>((nc + kEncWarps - 1) / kEncWarps), kEncWarps * 32, 0, s>>>(
+        d_in, n, ce, static_cast<uint32_t>(nc), prec, tab, slots, sb, recw);
+    xc_enc_scan_kernel<<<1, 1024, 0, s>>>(recw, static_cast<uint32_t>(nc), d_out, chunks_off, out_cap,
+                                          reinterpret_cast<unsigned long long *>(d_out_len), flags);
+    xc_enc_compact_kernel<<<static_cast<unsigned>(nc), 256, 0, s>>>(slots, sb, recw, d_out, chunks_off, flags);
+    (void)ws_bytes;
+    return cudaGetLastError();
+}
+
+}  // namespace bsg

@@ -1,0 +1,256 @@
+"""Device-resident API over libbsgpu.so (PyTorch supplies memory and streams).
+
+Everything here runs on the CUDA device through the C ABI declared in
+``include/bsgpu.h``; there is no CPU decode path.  Tensors handed to these
+functions must be CUDA tensors; compressed blobs are ``torch.uint8`` device
+tensors, decoded outputs ``torch.bfloat16`` (or a same-size 16-bit view).
+
+Reference counterparts (BigSmall):
+  * ``bigsmall/kernels/__init__.py:89-111`` decode_bf16_parallel  -> :func:`decode_par_into`
+  * ``bigsmall/kernels/ac_triton.py:112-262`` (Triton SE + CPU mantissa) -> :class:`ParPlan`
+  * ``bigsmall/decoder.py:128-136`` per-tensor decode loop -> :class:`XcPlan` (batched)
+  * ``bigsmall/codecs/kv_cache.py:41-83`` CPU encode -> :func:`encode_xc`
+"""
+from __future__ import annotations
+
+import ctypes
+from typing import Iterable, Optional, Sequence
+
+import torch
+
+from . import _lib
+
+DEFAULT_CHUNK_ELEMS = 65536   # 128 KiB of bf16 per chunk (one warp-state group)
+DEFAULT_PREC = 12             # M = 4096
+
+CODERS = {"rans": _lib.CODER_RANS, "tans": _lib.CODER_TANS}
+
+
+def _as_cuda(t: torch.Tensor, name: str) -> torch.Tensor:
+    if not isinstance(t, torch.Tensor) or not t.is_cuda:
+        raise TypeError(f"{name} must be a CUDA tensor")
+    if not t.is_contiguous():
+        raise ValueError(f"{name} must be contiguous")
+    return t
+
+
+def _stream_ptr(stream, device) -> ctypes.c_void_p:
+    if stream is None:
+        stream = torch.cuda.current_stream(device)
+    return ctypes.c_void_p(stream.cuda_stream)
+
+
+def _dev_index(t: torch.Tensor) -> int:
+    return t.device.index if t.device.index is not None else torch.cuda.current_device()
+
+
+class _Plan:
+    """Owns a ``bs_plan*``; keeps the tensors it points at alive."""
+
+    def __init__(self, handle: ctypes.c_void_p, device: int, keep: list, n: int):
+        self._h = handle
+        self.device = device
+        self._keep = keep
+        self.n_tensors = n
+
+    def decode(self, stream: Optional[torch.cuda.Stream] = None) -> None:
+        """Enqueue the decode on `stream` (default: current stream).  Async."""
+        L = _lib.load()
+        _lib.check(L.bs_plan_decode(self._h, _stream_ptr(stream, self.device)), "bs_plan_decode")
+
+    def check(self, stream: Optional[torch.cuda.Stream] = None) -> list[int]:
+        """Synchronise `stream` and raise BsCorruptError if any tensor failed."""
+        L = _lib.load()
+        st = (ctypes.c_uint32 * max(1, self.n_tensors))()
+        rc = L.bs_plan_check(self._h, _stream_ptr(stream, self.device), st)
+        words = [int(st[i]) for i in range(self.n_tensors)]
+        if rc != _lib.BS_OK:
+            bad = [(i, _lib.describe_device_status(w)) for i, w in enumerate(words) if w]
+            _lib.check(rc, f"decode failed {bad}", words)
+        return words
+
+    def run(self, stream=None) -> None:
+        self.decode(stream)
+        self.check(stream)
+
+    def close(self) -> None:
+        if self._h:
+            _lib.load().bs_plan_destroy(self._h)
+            self._h = None
+            self._keep = []
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+
+class XcPlan(_Plan):
+    """Decode plan for a batch of bf16_exp_chunked_v1 tensors.
+
+    ``entries``: iterable of ``(blob, out, chunk_elems)`` with ``blob`` a
+    1-D uint8 CUDA tensor (16-byte aligned) and ``out`` a contiguous 16-bit
+    CUDA tensor receiving ``out.numel()`` values.  One plan decodes all of
+    them with two kernel launches; it can be re-run any number of times.
+    """
+
+    def __init__(self, entries: Iterable[tuple], device: Optional[int] = None):
+        entries = list(entries)
+        keep = []
+        arr = (_lib.XcTensor * max(1, len(entries)))()
+        dev = device
+        for i, (blob, out, ce) in enumerate(entries):
+            _as_cuda(blob, "blob")
+            _as_cuda(out, "out")
+            if blob.dtype != torch.uint8:
+                raise TypeError("blob must be torch.uint8")
+            if out.element_size() != 2:
+                raise TypeError("out must be a 16-bit tensor (bfloat16)")
+            d = _dev_index(out)
+            if dev is None:
+                dev = d
+            if d != dev or _dev_index(blob) != dev:
+                raise ValueError("all tensors of a plan must live on one device")
+            arr[i].d_blob = blob.data_ptr() if blob.numel() else None
+            arr[i].blob_bytes = blob.numel()
+            arr[i].d_out = out.data_ptr() if out.numel() else None
+            arr[i].n_elems = out.numel()
+            arr[i].chunk_elems = int(ce)
+            arr[i].reserved = 0
+            keep += [blob, out]
+        if dev is None:
+            dev = torch.cuda.current_device()
+        h = ctypes.c_void_p()
+        L = _lib.load()
+        _lib.check(L.bs_xc_plan_create(arr, len(entries), dev, ctypes.byref(h)), "bs_xc_plan_create")
+        super().__init__(h, dev, keep, len(entries))
+
+
+class ParPlan(_Plan):
+    """Decode plan for one bf16_parallel_v1 blob (the reference's GPU format).
+
+    The framing is parsed from ``host_blob`` (bytes identical to ``d_blob``).
+    """
+
+    def __init__(self, host_blob: bytes, d_blob: torch.Tensor, out: torch.Tensor, n_weights: int):
+        _as_cuda(out, "out")
+        if n_weights and len(host_blob):
+            _as_cuda(d_blob, "d_blob")
+        if out.numel() < n_weights:
+            raise ValueError("out is smaller than n_weights")
+        dev = _dev_index(out)
+        hb = ctypes.create_string_buffer(bytes(host_blob), len(host_blob)) if len(host_blob) else None
+        h = ctypes.c_void_p()
+        L = _lib.load()
+        rc = L.bs_par_plan_create(hb, len(host_blob), int(n_weights),
+                                  d_blob.data_ptr() if d_blob is not None and d_blob.numel() else None,
+                                  out.data_ptr() if out.numel() else None, dev, ctypes.byref(h))
+        _lib.check(rc, "bs_par_plan_create")
+        super().__init__(h, dev, [d_blob, out], 1)
+
+
+def decode_xc_into(blob: torch.Tensor, out: torch.Tensor, chunk_elems: int,
+                   stream=None, check: bool = True) -> torch.Tensor:
+    """Decode one bf16_exp_chunked_v1 blob (device) into ``out`` (device)."""
+    with XcPlan([(blob, out, chunk_elems)]) as p:
+        p.decode(stream)
+        if check:
+            p.check(stream)
+    return out
+
+
+def decode_par_into(host_blob: bytes, d_blob: torch.Tensor, out: torch.Tensor, n_weights: int,
+                    stream=None) -> torch.Tensor:
+    with ParPlan(host_blob, d_blob, out, n_weights) as p:
+        p.run(stream)
+    return out
+
+
+# ---------------------------------------------------------------------------
+# encoder
+# ---------------------------------------------------------------------------
+def encode_bound(n: int, chunk_elems: int = DEFAULT_CHUNK_ELEMS) -> int:
+    v = ctypes.c_uint64()
+    _lib.check(_lib.load().bs_xc_encode_bound(n, chunk_elems, ctypes.byref(v)), "bs_xc_encode_bound")
+    return int(v.value)
+
+
+def encode_workspace(n: int, chunk_elems: int = DEFAULT_CHUNK_ELEMS) -> int:
+    v = ctypes.c_uint64()
+    _lib.check(_lib.load().bs_xc_encode_workspace(n, chunk_elems, ctypes.byref(v)), "bs_xc_encode_workspace")
+    return int(v.value)
+
+
+class XcEncoder:
+    """Reusable device encoder: owns an output buffer and a workspace sized for
+    tensors of up to ``max_elems`` values (no allocation per call)."""
+
+    def __init__(self, max_elems: int, chunk_elems: int = DEFAULT_CHUNK_ELEMS, coder: str = "rans",
+                 prec: int = DEFAULT_PREC, device=None):
+        self.chunk_elems = int(chunk_elems)
+        self.coder = CODERS[coder] if isinstance(coder, str) else int(coder)
+        self.prec = int(prec)
+        self.max_elems = int(max_elems)
+        dev = torch.device("cuda", device if device is not None else torch.cuda.current_device())
+        self.device = dev
+        self.out = torch.empty(max(16, encode_bound(max_elems, chunk_elems)), dtype=torch.uint8, device=dev)
+        self.ws = torch.empty(max(16, encode_workspace(max_elems, chunk_elems)), dtype=torch.uint8, device=dev)
+        self.out_len = torch.zeros(2, dtype=torch.int64, device=dev)
+
+    def encode_async(self, x: torch.Tensor, stream=None) -> None:
+        """Enqueue the encode of ``x``; the blob is ``self.out[:self.out_len[0]]``."""
+        _as_cuda(x, "x")
+        if x.element_size() != 2:
+            raise TypeError("x must be a 16-bit tensor (bfloat16)")
+        n = x.numel()
+        if n > self.max_elems:
+            raise ValueError(f"tensor of {n} values exceeds encoder capacity {self.max_elems}")
+        L = _lib.load()
+        rc = L.bs_xc_encode(x.data_ptr() if n else None, n, self.coder, self.prec, self.chunk_elems,
+                            self.out.data_ptr(), self.out.numel(), self.out_len.data_ptr(),
+                            self.ws.data_ptr(), self.ws.numel(), _stream_ptr(stream, self.device))
+        _lib.check(rc, "bs_xc_encode")
+
+    def encode(self, x: torch.Tensor, stream=None) -> torch.Tensor:
+        """Encode ``x`` and return a right-sized device copy of the blob."""
+        self.encode_async(x, stream)
+        n = int(self.out_len[0].item())
+        return self.out[:n].clone()
+
+
+def encode_xc(x: torch.Tensor, coder: str = "rans", prec: int = DEFAULT_PREC,
+              chunk_elems: int = DEFAULT_CHUNK_ELEMS, stream=None) -> torch.Tensor:
+    """Encode a bf16 CUDA tensor into a bf16_exp_chunked_v1 blob on the device."""
+    enc = XcEncoder(max(1, x.numel()), chunk_elems, coder, prec, device=_dev_index(x))
+    return enc.encode(x.reshape(-1), stream)
+
+
+def xc_extras(chunk_elems: int = DEFAULT_CHUNK_ELEMS, coder: str = "rans", prec: int = DEFAULT_PREC) -> dict:
+    """The per-tensor ``extra`` dict the container header stores for the codec."""
+    return {"chunk_elems": int(chunk_elems), "coder": coder, "prec": int(prec)}
+
+
+def aligned_view(buf: torch.Tensor, offset: int, nbytes: int) -> torch.Tensor:
+    """A 16-byte aligned device view of buf[offset:offset+nbytes] (a copy if the
+    slice is misaligned)."""
+    v = buf[offset:offset + nbytes]
+    if nbytes and v.data_ptr() % 16:
+        v = v.clone()
+    return v
+
+
+def sync(device=None) -> None:
+    torch.cuda.synchronize(device)
+
+
+__all__: Sequence[str] = [
+    "DEFAULT_CHUNK_ELEMS", "DEFAULT_PREC", "XcPlan", "ParPlan", "XcEncoder", "decode_xc_into",
+    "decode_par_into", "encode_xc", "encode_bound", "encode_workspace", "xc_extras", "aligned_view",
+]

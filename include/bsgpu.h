@@ -1,0 +1,124 @@
+/*
+ * bsgpu.h -- C ABI of libbsgpu.so, the B200 (sm_100a) decode/encode engine
+ * behind BigSmall's bf16 codec path.
+ *
+ * Plain pointers and sizes only: device pointers are CUDA device addresses,
+ * `stream` is a cudaStream_t passed as void*.  Every entry point returns an
+ * int status (BS_OK == 0); bs_last_error() gives a message for the calling
+ * thread.  Nothing here falls back to the CPU: a device failure is reported,
+ * never hidden.
+ *
+ * Reference interfaces replaced (paths are within the BigSmall project):
+ *   bigsmall/kernels/__init__.py:56-64   the missing `ac_cuda` backend slot,
+ *                                        contract decode(blob, extras, n)->bytes
+ *   bigsmall/kernels/__init__.py:89-111  decode_bf16_parallel dispatch
+ *   bigsmall/kernels/ac_triton.py:112-262 Triton SE kernel + CPU mantissa path
+ *   bigsmall/codecs/bf16_parallel.py:262-352  bf16_parallel_v1 decode
+ *   bigsmall/codecs/kv_cache.py:41-117   KV blob encode/decode (CPU today)
+ *   bigsmall/decoder.py:49-97            per-tensor codec dispatch (GPU branch)
+ */
+#ifndef BSGPU_H
+#define BSGPU_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ------------------------------------------------------- */
+#define BS_OK                0
+#define BS_E_INVALID_ARG     1   /* bad pointer/size/alignment/parameter      */
+#define BS_E_BAD_MAGIC       2   /* blob does not start with its format magic */
+#define BS_E_COUNT_MISMATCH  3   /* header n != caller's n_weights            */
+#define BS_E_TRUNCATED       4   /* blob shorter than its own framing says    */
+#define BS_E_CORRUPT         5   /* device decoder flagged a stream error     */
+#define BS_E_CUDA            6   /* a CUDA runtime call failed                */
+#define BS_E_UNSUPPORTED     7   /* format version / precision not supported  */
+#define BS_E_NOMEM           8   /* allocation failed (plan creation only)    */
+#define BS_E_PRECISION       9   /* bf16_parallel_v1 precision mismatch       */
+
+/* per-tensor device status bits (bs_plan_check out array) */
+#define BS_DEV_HEADER        0x01u  /* header disagrees with the descriptor   */
+#define BS_DEV_FREQ          0x02u  /* frequency table does not sum to 2^P    */
+#define BS_DEV_CHUNK_TABLE   0x04u  /* chunk offsets out of range/unordered   */
+#define BS_DEV_STREAM        0x08u  /* renorm words over- or under-consumed   */
+#define BS_DEV_FINAL_STATE   0x10u  /* coder state did not return to its seed */
+#define BS_DEV_COUNT         0x20u  /* bucket/stream symbol counts disagree   */
+
+/* bf16_exp_chunked_v1 coders */
+#define BS_CODER_RANS        0
+#define BS_CODER_TANS        1
+
+typedef struct bs_plan bs_plan;
+
+/* One bf16_exp_chunked_v1 tensor to decode.  Both pointers must be 16-byte
+ * aligned device addresses on the plan's device.  chunk_elems comes from the
+ * container header's per-tensor "extra" dict (bigsmall/container.py:17-38
+ * keeps codec extras there) and must match the blob header. */
+typedef struct bs_xc_tensor {
+    const void *d_blob;
+    uint64_t    blob_bytes;
+    void       *d_out;         /* n_elems bf16 values */
+    uint64_t    n_elems;
+    uint32_t    chunk_elems;
+    uint32_t    reserved;      /* must be 0 */
+} bs_xc_tensor;
+
+/* ---- library ------------------------------------------------------------ */
+int         bs_version(void);                 /* 100*major + minor           */
+const char *bs_last_error(void);              /* thread-local, never NULL    */
+const char *bs_status_string(int status);
+
+/* ---- bf16_exp_chunked_v1 decode (the hot path) -------------------------- */
+/* Build a reusable decode plan for a batch of tensors (any mix of coders and
+ * precisions).  Allocates the plan's device memory (work list, per-tensor
+ * decode tables, status words); decoding itself allocates nothing.
+ * Replaces: bigsmall/decoder.py:128-136 per-tensor decode loop (GPU branch). */
+int bs_xc_plan_create(const bs_xc_tensor *tensors, int n_tensors, int device,
+                      bs_plan **out_plan);
+
+/* Enqueue the decode of every tensor in the plan on `stream` (cudaStream_t).
+ * Asynchronous; stream-ordered; launches a table-build kernel and the decode
+ * kernel.  The plan may be decoded any number of times. */
+int bs_plan_decode(bs_plan *plan, void *stream);
+
+/* Synchronise `stream`, read the per-tensor device status words into
+ * `status_out` (may be NULL; else n_tensors entries) and return BS_OK or
+ * BS_E_CORRUPT. */
+int bs_plan_check(bs_plan *plan, void *stream, uint32_t *status_out);
+
+int bs_plan_n_tensors(const bs_plan *plan);
+int bs_plan_destroy(bs_plan *plan);
+
+/* ---- bf16_parallel_v1 decode (the reference's GPU format) --------------- */
+/* Parse a PAR1 blob's framing on the host (`h_blob`, the same bytes as at
+ * `d_blob` on the device) and build a decode plan writing n_weights bf16
+ * values to d_out.  Errors mirror bigsmall/codecs/bf16_parallel.py:153-163,
+ * :274-276 (bad magic, precision mismatch, count mismatch).
+ * Replaces: bigsmall/kernels/ac_triton.py:112-262 and
+ *           bigsmall/codecs/bf16_parallel.py:262-352. */
+int bs_par_plan_create(const uint8_t *h_blob, uint64_t blob_bytes,
+                       uint64_t n_weights, const void *d_blob, void *d_out,
+                       int device, bs_plan **out_plan);
+
+/* ---- bf16_exp_chunked_v1 encode (KV-cache compression) ------------------ */
+/* Worst-case blob size and scratch size for one tensor. */
+int bs_xc_encode_bound(uint64_t n_elems, uint32_t chunk_elems, uint64_t *bytes);
+int bs_xc_encode_workspace(uint64_t n_elems, uint32_t chunk_elems, uint64_t *bytes);
+
+/* Encode n_elems bf16 values at d_in into a bf16_exp_chunked_v1 blob at d_out
+ * (capacity out_cap >= bs_xc_encode_bound).  The exact blob length is written
+ * to the device u64 at d_out_len.  Deterministic: the bytes equal the CPU
+ * reference encoder's.  Asynchronous on `stream`.
+ * Replaces: bigsmall/codecs/kv_cache.py:41-83 compress_kv_entry's CPU encode. */
+int bs_xc_encode(const void *d_in, uint64_t n_elems, int coder, int prec,
+                 uint32_t chunk_elems, void *d_out, uint64_t out_cap,
+                 uint64_t *d_out_len, void *d_workspace, uint64_t ws_bytes,
+                 void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* BSGPU_H */

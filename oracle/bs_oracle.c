@@ -854,13 +854,16 @@ int bso_tans_decode(const uint8_t *blob, int64_t len, int64_t n_weights, uint16_
 
 /* ======================================================================== */
 /* bf16_exp_chunked_v1 -- this project's chunked format (no reference       */
-/* counterpart).  Layout (little-endian, every section 16-byte aligned):    */
+/* counterpart).  Layout (little-endian; sections in this fixed order, each  */
+/* 16-byte aligned):                                                         */
 /*   0   "BSXC"   4 u16 version=1   6 u8 coder (0 rANS, 1 tANS)   7 u8 P     */
 /*   8   u64 n    16 u32 chunk_elems   20 u32 n_chunks   24 u32 lanes=32     */
 /*   28  u32 flags=0  32 u64 chunks_off  40 u64 plane_off  48 u64 blob_bytes */
-/*   56  u64 0    64 u16 freq[256]   576 u32 chunk_start[n_chunks+1] (16 B   */
-/*   units from chunks_off)   chunks_off: per chunk [u32 init[32]][u16 words]*/
-/*   zero-padded to 16 B   plane_off: n bytes (sign<<7 | mantissa), padded. */
+/*   56  u64 0    64 u16 freq[256]                                           */
+/*   576 u32 chunk_start[n_chunks+1] (16-byte units from chunks_off)         */
+/*   plane_off  = rup16(576 + 4*(n_chunks+1)): n bytes (sign<<7 | mantissa)  */
+/*   chunks_off = plane_off + rup16(n): per chunk [u32 init[32]][u16 words]  */
+/*                zero-padded to 16 bytes; blob_bytes = end of last record.  */
 /* Element e of a chunk belongs to lane (e%256)/8 at step (e/256)*8 + e%8.  */
 /* ======================================================================== */
 #define XC_HDR 64
@@ -1072,9 +1075,11 @@ int64_t bso_xc_encode(const uint16_t *w, int64_t n, int coder, int prec, uint32_
         uint32_t cum2[256];
         xc_tans_tables(freq, prec, dec, slot_list, cum2);
     }
-    int64_t chunks_off = rup16(XC_TAB_OFF + 4 * ((int64_t)nc + 1));
+    int64_t plane_off = rup16(XC_TAB_OFF + 4 * ((int64_t)nc + 1));
+    int64_t chunks_off = plane_off + rup16(n);
     if (chunks_off > cap) { free(ex); free(slot_list); free(dec); return BSO_E_CAP; }
     memset(out, 0, (size_t)chunks_off);
+    for (int64_t i = 0; i < n; i++) out[plane_off + i] = (uint8_t)(((w[i] >> 8) & 0x80) | (w[i] & 0x7F));
     int64_t pos = chunks_off;
     int rc = 0;
     for (uint32_t k = 0; k < nc; k++) {
@@ -1088,11 +1093,7 @@ int64_t bso_xc_encode(const uint16_t *w, int64_t n, int coder, int prec, uint32_
     free(ex); free(slot_list); free(dec);
     if (rc) return rc;
     wr32(out + XC_TAB_OFF + 4 * nc, (uint32_t)((pos - chunks_off) / 16));
-    int64_t plane_off = pos;
-    int64_t total = plane_off + rup16(n);
-    if (total > cap) return BSO_E_CAP;
-    memset(out + plane_off, 0, (size_t)(total - plane_off));
-    for (int64_t i = 0; i < n; i++) out[plane_off + i] = (uint8_t)(((w[i] >> 8) & 0x80) | (w[i] & 0x7F));
+    int64_t total = pos;
     memcpy(out, "BSXC", 4);
     wr16(out + 4, 1);
     out[6] = (uint8_t)coder;
@@ -1124,9 +1125,10 @@ int bso_xc_decode(const uint8_t *blob, int64_t len, int64_t n_weights, uint16_t 
     if ((coder != 0 && coder != 1) || P < 8 || P > 12 || lanes != XC_LANES || ce == 0 || (ce & 255))
         return BSO_E_CORRUPT;
     if ((int64_t)nc != (n + ce - 1) / ce) return BSO_E_CORRUPT;
-    if (total > len || chunks_off < XC_TAB_OFF + 4 * ((int64_t)nc + 1) || plane_off + n > total ||
-        (chunks_off & 15) || (plane_off & 15))
-        return BSO_E_TRUNC;
+    if (plane_off != rup16(XC_TAB_OFF + 4 * ((int64_t)nc + 1)) || chunks_off != plane_off + rup16(n) ||
+        (total & 15) || total < chunks_off)
+        return BSO_E_CORRUPT;
+    if (total > len) return BSO_E_TRUNC;
     const uint32_t M = 1u << P;
     uint16_t freq[256];
     uint32_t cum[256], sum = 0;
@@ -1150,7 +1152,7 @@ int bso_xc_decode(const uint8_t *blob, int64_t len, int64_t n_weights, uint16_t 
     for (uint32_t k = 0; k < nc && !rc; k++) {
         int64_t a = chunks_off + 16 * (int64_t)rd32(blob + XC_TAB_OFF + 4 * k);
         int64_t b = chunks_off + 16 * (int64_t)rd32(blob + XC_TAB_OFF + 4 * (k + 1));
-        if (b < a + 128 || b > plane_off) { rc = BSO_E_CORRUPT; break; }
+        if (b < a + 128 || b > total) { rc = BSO_E_CORRUPT; break; }
         const uint8_t *rec = blob + a;
         const int64_t navail = (b - a - 128) / 2;
         const uint8_t *wd = rec + 128;

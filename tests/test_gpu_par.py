@@ -1,0 +1,66 @@
+"""GPU parity of the bf16_parallel_v1 decoder against the reference's own blobs.
+
+tests/golden holds blobs minted by the reference encoder
+(bigsmall/codecs/bf16_parallel.py:186-259); the device decode must equal the
+reference decode (bigsmall/codecs/bf16_parallel.py:262-352) byte for byte, as
+the reference's only GPU test demands of its Triton path
+(tests/test_gpu_kernel.py:37-51).
+"""
+from __future__ import annotations
+
+import hashlib
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+from oracle import oracle as O  # noqa: E402
+from tests.conftest import golden_bytes  # noqa: E402
+
+
+def md5(b):
+    return hashlib.md5(b).hexdigest()
+
+
+def _gpu_par(blob: bytes, n: int) -> bytes:
+    from bigsmall_b200 import gpu
+    d = torch.from_numpy(np.frombuffer(blob, dtype=np.uint8).copy()).cuda() if blob else torch.empty(0, dtype=torch.uint8, device="cuda")
+    out = torch.empty(max(n, 1), dtype=torch.bfloat16, device="cuda")
+    gpu.decode_par_into(blob, d, out, n)
+    return out[:n].cpu().view(torch.uint8).numpy().tobytes()
+
+
+@pytest.mark.parametrize("key", ["par1", "par32", "par128"])
+def test_reference_blobs(manifest, key):
+    for name, c in manifest["cases"].items():
+        b = c["blobs"][key]
+        got = _gpu_par(golden_bytes(b["file"]), c["n"])
+        assert md5(got) == b["decoded_md5"], (name, key)
+
+
+@pytest.mark.parametrize("n,ns", [(1 << 18, 64), (1 << 20, 128), (1 << 20, 1), (300_001, 256)])
+def test_gaussian(n, ns):
+    """reference tests/test_gpu_kernel.py:37-51 shape (n=2^18, N=64) and more"""
+    g = torch.Generator().manual_seed(ns)
+    raw = (torch.randn(n, generator=g) * 0.02).to(torch.bfloat16).view(torch.uint8).numpy().tobytes()
+    blob = O.par_encode(raw, ns)
+    assert _gpu_par(blob, n) == raw == O.par_decode(blob, n)
+
+
+def test_errors_mirror_reference():
+    from bigsmall_b200.exceptions import BsCorruptError
+    raw = golden_bytes("gauss_8k.raw")
+    blob = O.par_encode(raw, 32)
+    with pytest.raises(BsCorruptError, match="bad magic"):
+        _gpu_par(b"XXXX" + blob[4:], 8192)
+    with pytest.raises(BsCorruptError, match="count mismatch"):
+        _gpu_par(blob, 8191)
+    bad = bytearray(blob)
+    bad[10] = 13    # precision_se field
+    with pytest.raises(BsCorruptError, match="precision"):
+        _gpu_par(bytes(bad), 8192)
+    with pytest.raises(BsCorruptError):
+        _gpu_par(blob[:100], 8192)
+    assert _gpu_par(b"", 0) == b""

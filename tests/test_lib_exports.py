@@ -1,0 +1,47 @@
+"""The C-ABI library builds, loads without a GPU, and exports exactly the
+symbols include/bsgpu.h declares (no compute calls here)."""
+from __future__ import annotations
+
+import os
+import re
+import subprocess
+
+from tests.conftest import ROOT
+
+
+def _declared():
+    hdr = open(os.path.join(ROOT, "include", "bsgpu.h")).read()
+    return set(re.findall(r"^(?:int|const char \*)\s*(bs_\w+)\(", hdr, re.M))
+
+
+def test_header_declarations_match_binding():
+    from bigsmall_b200 import _lib
+    assert _declared() == set(_lib.SIGNATURES)
+
+
+def test_library_loads_and_exports_every_symbol():
+    from bigsmall_b200 import _lib
+    lib = _lib.load()
+    for name in _declared():
+        assert hasattr(lib, name), name
+    assert lib.bs_version() == 100
+    assert lib.bs_status_string(5) == b"corrupt stream"
+    out = subprocess.run(["nm", "-D", "--defined-only", _lib.LIB_PATH], capture_output=True, text=True).stdout
+    exported = set(re.findall(r" T (bs_\w+)", out))
+    assert _declared() <= exported
+
+
+def test_host_side_validation_without_gpu():
+    """Argument checks run before any device work."""
+    import ctypes
+    from bigsmall_b200 import _lib
+    lib = _lib.load()
+    v = ctypes.c_uint64()
+    assert lib.bs_xc_encode_bound(1000, 100, ctypes.byref(v)) == _lib.BS_E_INVALID_ARG
+    assert lib.bs_xc_encode_bound(1000, 256, ctypes.byref(v)) == 0 and v.value > 2000
+    h = ctypes.c_void_p()
+    # no CUDA device in a CPU-only container: creation must fail cleanly
+    rc = lib.bs_xc_plan_create(None, 0, 0, ctypes.byref(h))
+    assert rc in (_lib.BS_OK, _lib.BS_E_INVALID_ARG)
+    if rc == _lib.BS_OK:
+        lib.bs_plan_destroy(h)
