@@ -1,0 +1,444 @@
+"""Benchmark: full-container bf16 decode on B200.
+
+Workload: a Llama-3-8B-shaped random-init bf16 container (32 layers, hidden
+4096, q/o 4096x4096, k/v 1024x4096, gate/up 14336x4096, down 4096x14336,
+embed + lm_head 128256x4096, RMSNorm 1.0+N(0,0.01), linear N(0, 1/sqrt(fan_in)),
+one CUDA generator seeded 0, tensors generated in name order), ~8.03 G values
+(16.06 GB of bf16), encoded on the device with bf16_exp_chunked_v1 (rANS).
+
+One step = decode the whole container (this rank's share of it) into HBM.
+  value : decoded bf16 GB/s with the compressed bytes already in HBM
+          (one decode plan: table build + decode kernel per step)
+  e2e   : the same through the public loader (bigsmall_b200.loader.DeviceLoader):
+          pinned host -> device copy of the compressed bytes, overlapped group by
+          group with the decode, plus the device->host read of the status words.
+With torchrun (N ranks) the container is partitioned by tensor / chunk-range
+ownership (contiguous chunk spans); there is no collective on the decode path.
+
+``--impl reference`` times the reference's fastest CPU decoder
+(bf16_se_single_kernel, ported to C in oracle/ because the reference is
+Python/Numba) on the host cores, on a bounded sample of the same tensors.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "decoded bf16 GB/s per GPU and per box at 1/2/4/8 B200; % of HBM roofline"
+FALLBACK_HBM_GBS = 6650.0
+
+
+# ---------------------------------------------------------------------------
+# workload
+# ---------------------------------------------------------------------------
+def llama3_8b_tensors():
+    """(name, shape, kind) in generation order."""
+    H, I, KV, V, L = 4096, 14336, 1024, 128256, 32
+    out = [("model.embed_tokens.weight", (V, H), "linear")]
+    for i in range(L):
+        p = f"model.layers.{i}."
+        out += [
+            (p + "input_layernorm.weight", (H,), "norm"),
+            (p + "self_attn.q_proj.weight", (H, H), "linear"),
+            (p + "self_attn.k_proj.weight", (KV, H), "linear"),
+            (p + "self_attn.v_proj.weight", (KV, H), "linear"),
+            (p + "self_attn.o_proj.weight", (H, H), "linear"),
+            (p + "post_attention_layernorm.weight", (H,), "norm"),
+            (p + "mlp.gate_proj.weight", (I, H), "linear"),
+            (p + "mlp.up_proj.weight", (I, H), "linear"),
+            (p + "mlp.down_proj.weight", (H, I), "linear"),
+        ]
+    out += [("model.norm.weight", (H,), "norm"), ("lm_head.weight", (V, H), "linear")]
+    return out
+
+
+def gen_tensor(torch, g, shape, kind, device):
+    if kind == "norm":
+        return (1.0 + torch.randn(shape, generator=g, device=device) * 0.01).to(torch.bfloat16)
+    fan_in = shape[-1]
+    return (torch.randn(shape, generator=g, device=device) * (1.0 / math.sqrt(fan_in))).to(torch.bfloat16)
+
+
+def partition(tensors, world, chunk_elems):
+    """Ownership: cut the container's chunk sequence (tensors in name order)
+    into `world` contiguous spans of equal element count.  Each rank owns a few
+    whole tensors plus at most two chunk ranges of the tensors at its span
+    ends; loads differ by at most one chunk."""
+    spans = []          # (name, n, n_chunks)
+    for name, shape, _ in tensors:
+        n = math.prod(shape)
+        spans.append((name, n, -(-n // chunk_elems)))
+    total = sum(n for _, n, _ in spans)
+    owned = [[] for _ in range(world)]
+    load = [0] * world
+    r, acc = 0, 0
+    for name, n, nc in spans:
+        c = 0
+        while c < nc:
+            target = total * (r + 1) / world
+            # chunks of this tensor that still fit into rank r's span
+            take = nc - c
+            if r < world - 1:
+                room = target - acc
+                fit = max(1, int(round(room / chunk_elems))) if room > 0 else 0
+                take = min(take, fit) if fit else 0
+            if take == 0:
+                r += 1
+                continue
+            e = min(n, (c + take) * chunk_elems) - c * chunk_elems
+            owned[r].append((name, c, take) if (c, take) != (0, nc) else (name, 0, 0))
+            load[r] += e
+            acc += e
+            c += take
+            if r < world - 1 and acc >= target - chunk_elems / 2:
+                r += 1
+    return owned, load
+
+
+# ---------------------------------------------------------------------------
+# clocks (NVML polled during the timed region)
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    REASONS = {
+        0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap", 0x8: "hw_slowdown",
+        0x10: "sync_boost", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+        0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting",
+    }
+
+    def __init__(self, index: int, period: float = 0.005):
+        self.samples, self.reasons = [], 0
+        self.ok = False
+        self.period = period
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            self.ok = True
+        except Exception as e:   # no NVML: record why
+            self.err = repr(e)
+        self._stop = threading.Event()
+
+    def _poll(self):
+        nv = self.nv
+        while not self._stop.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM))
+                fn = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or nv.nvmlDeviceGetCurrentClocksThrottleReasons
+                self.reasons |= int(fn(self.h))
+            except Exception:
+                pass
+            time.sleep(self.period)
+
+    def __enter__(self):
+        if self.ok:
+            self._t = threading.Thread(target=self._poll, daemon=True)
+            self._t.start()
+        return self
+
+    def __exit__(self, *a):
+        if self.ok:
+            self._stop.set()
+            self._t.join()
+
+    def summary(self):
+        if not self.ok:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "note": getattr(self, "err", "")}
+        r = [name for bit, name in self.REASONS.items() if self.reasons & bit and bit != 0x1]
+        return {"sm_mhz": statistics.median(self.samples) if self.samples else None,
+                "sm_max_mhz": self.max_mhz, "reasons": r, "samples": len(self.samples)}
+
+
+def measured_peak():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def profile_traffic():
+    """dram bytes per decode launch from the committed ncu summary, if any."""
+    p = os.path.join(ROOT, "profiles", "xc_decode_c2.json")
+    try:
+        with open(p) as f:
+            return json.load(f)
+    except Exception:
+        return None
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline: the reference's fastest CPU decoder (oracle C port)
+# ---------------------------------------------------------------------------
+def cpu_baseline(torch, seconds: float = 8.0, threads=None, device="cuda:0"):
+    from oracle import oracle as O
+    from concurrent.futures import ThreadPoolExecutor
+    threads = threads or os.cpu_count() or 1
+    # sample: k/v-projection shaped tensors of the same container distribution
+    n_tensors = max(8, 2 * threads)
+    g = torch.Generator(device=device).manual_seed(1)
+    raws = []
+    for _ in range(n_tensors):
+        x = gen_tensor(torch, g, (1024, 4096), "linear", device)
+        raws.append(x.view(torch.int16).cpu().numpy().tobytes())
+    with ThreadPoolExecutor(threads) as ex:
+        blobs = list(ex.map(O.sk_encode, raws))
+    nw = [len(r) // 2 for r in raws]
+    # warm up, then time whole rounds until `seconds` elapsed
+    O.decode_many("sk", blobs[:threads], nw[:threads], threads)
+    t0 = time.perf_counter()
+    rounds = 0
+    while True:
+        outs = O.decode_many("sk", blobs, nw, threads)
+        rounds += 1
+        if time.perf_counter() - t0 >= seconds:
+            break
+    dt = time.perf_counter() - t0
+    assert outs[0].tobytes() == raws[0], "CPU baseline decode mismatch"
+    decoded = rounds * sum(2 * n for n in nw)
+    return {"value": decoded / dt / 1e9, "unit": "GB/s", "cores": threads, "kind": "port",
+            "sample": f"{n_tensors} tensors of 1024x4096 bf16 (config-2 k/v shape and init), "
+                      f"bf16_se_single_kernel blobs, {rounds} round(s) in {dt:.1f} s, "
+                      f"{threads} host threads"}
+
+
+# ---------------------------------------------------------------------------
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--chunk-elems", type=int, default=None)
+    ap.add_argument("--coder", default="rans")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=8.0)
+    a = ap.parse_args()
+    a.warmup = max(3, a.warmup)
+
+    import torch
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+
+    from bigsmall_b200 import gpu
+    from bigsmall_b200.container import ContainerWriter
+    from bigsmall_b200.loader import ContainerImage, DeviceLoader
+
+    ce = a.chunk_elems or gpu.DEFAULT_CHUNK_ELEMS
+    config = {"workload": "llama3-8b-shaped bf16 container (BASELINE config 2), full-container decode",
+              "codec": "bf16_exp_chunked_v1", "coder": a.coder, "chunk_elems": ce, "prec": gpu.DEFAULT_PREC,
+              "partition": "contiguous chunk-span ownership, no collective", "ranks": world,
+              "l2": "inputs (~10.6 GB compressed) far larger than the 126 MB L2; no flush"}
+
+    if a.impl == "reference":
+        if rank != 0:
+            if dist: dist.destroy_process_group()
+            return
+        res = cpu_baseline(torch, seconds=a.cpu_seconds)
+        # steps of the bounded sample, as the timed unit
+        line = {"metric": METRIC, "value": round(res["value"], 4), "unit": "GB/s", "n_gpus": world,
+                "steps": a.steps, "warmup": a.warmup, "ms_per_step": None, "higher_is_better": True,
+                "scaling": "strong", "vs_baseline": None, "dtype": "u16", "data": "synthetic",
+                "config": config, "impl": "reference",
+                "cpu_baseline": {"value": round(res["value"], 4), "unit": "GB/s", "cores": res["cores"],
+                                 "kind": res["kind"], "sample": res["sample"]},
+                "e2e": {"value": round(res["value"], 4), "unit": "GB/s", "h2d_bytes_per_step": 0,
+                        "d2h_bytes_per_step": 0},
+                "note": "reference is Python/Numba; timed through its C port in oracle/ on host cores"}
+        print(json.dumps(line), flush=True)
+        if dist: dist.destroy_process_group()
+        return
+
+    tensors = llama3_8b_tensors()
+    owned_all, load = partition(tensors, world, ce)
+    owned = owned_all[rank]
+    owned_names = {n for n, _, _ in owned}
+
+    # generate (every rank walks the same generator sequence) and encode owned tensors
+    t_setup = time.time()
+    g = torch.Generator(device=dev).manual_seed(0)
+    originals, blobs = {}, {}
+    max_n = max(math.prod(s) for n, s, _ in tensors if n in owned_names)
+    enc = gpu.XcEncoder(max_n, ce, a.coder, gpu.DEFAULT_PREC, device=local)
+    for name, shape, kind in tensors:
+        x = gen_tensor(torch, g, shape, kind, dev)
+        if name in owned_names:
+            originals[name] = x
+            blobs[name] = enc.encode(x.reshape(-1))
+        else:
+            del x
+    del enc
+    # container image in pinned host memory (blobs 16-byte aligned)
+    offs, pos = {}, 0
+    for name in blobs:
+        offs[name] = pos
+        pos += (blobs[name].numel() + 15) // 16 * 16
+    host = torch.zeros(max(16, pos), dtype=torch.uint8, pin_memory=True)
+    metas = []
+    for name, shape, kind in tensors:
+        if name not in blobs:
+            continue
+        b = blobs[name]
+        host[offs[name]:offs[name] + b.numel()].copy_(b)
+        metas.append({"name": name, "shape": list(shape), "dtype": "BF16", "codec": "bf16_exp_chunked_v1",
+                      "special": None, "compressed_bytes": int(b.numel()), "offset": offs[name], "md5": "",
+                      "extra": gpu.xc_extras(ce, a.coder, gpu.DEFAULT_PREC)})
+    header = {"format": "bf16", "mode": "balanced", "model_type": "llm", "base_model": None,
+              "tensor_count": len(metas), "tensors": metas}
+    image = ContainerImage(header, host, pin=True)
+    comp_bytes = sum(int(b.numel()) for b in blobs.values())
+    del blobs
+    torch.cuda.synchronize()
+    loader = DeviceLoader(image, device=local, owned=owned)
+    # elements / compressed bytes this rank decodes per step
+    dec_elems, algo_bytes = 0, 0
+    for name, c0, cc in owned:
+        m = image.tensors[name]
+        n = math.prod(m["shape"])
+        e = (min(n, (c0 + cc) * ce) - c0 * ce) if cc else n
+        dec_elems += e
+        algo_bytes += int(m["compressed_bytes"] * e / n) + 2 * e
+    setup_s = time.time() - t_setup
+
+    def barrier():
+        if dist:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(v):
+        if not dist:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def sum_over_ranks(v):
+        if not dist:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.SUM)
+        return float(t.item())
+
+    stream = torch.cuda.current_stream(dev)
+
+    # ---- e2e through the public loader: H2D of compressed bytes + decode ------
+    e2e_ms = None
+    n_groups = len(loader.groups)
+    if not a.no_e2e:
+        for _ in range(a.warmup):
+            loader.run_async(stream)
+        loader.check(stream)
+        barrier()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record(stream)
+        for _ in range(a.steps):
+            loader.run_async(stream)
+        e.record(stream)
+        loader.check(stream)
+        barrier()
+        e2e_ms = max_over_ranks(s.elapsed_time(e) / a.steps)
+
+    # ---- device-resident decode: one plan over everything this rank owns -----
+    loader.upload()
+    entries = []
+    for name, c0, cc in owned:
+        m = image.tensors[name]
+        _, d, nb = loader.layout[name]
+        entries.append((loader.dev_data[d:d + nb], loader.out[name].reshape(-1).view(torch.int16), ce,
+                        math.prod(m["shape"]), c0, cc))
+    plan = gpu.XcPlan(entries, device=local)
+    for _ in range(a.warmup):
+        plan.decode(stream)
+    plan.check(stream)
+    barrier()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        s.record(stream)
+        for _ in range(a.steps):
+            plan.decode(stream)
+        e.record(stream)
+        torch.cuda.synchronize()
+    plan.check(stream)
+    local_ms = s.elapsed_time(e) / a.steps
+    barrier()
+    ms = max_over_ranks(local_ms)
+
+    # ---- verification: bitwise equality of every owned part (device) ---------
+    bad = []
+    for name, c0, cc in owned:
+        ref = originals[name].reshape(-1)
+        if cc:
+            ref = ref[c0 * ce: min(ref.numel(), (c0 + cc) * ce)]
+        if not torch.equal(ref.view(torch.int16), loader.out[name].reshape(-1).view(torch.int16)):
+            bad.append(name)
+    n_bad = int(sum_over_ranks(len(bad)))
+    total_elems = sum_over_ranks(dec_elems)
+    total_comp = sum_over_ranks(sum(int(image.tensors[n]["compressed_bytes"]) for n in image.tensors))
+    h2d = loader.h2d_bytes()
+    if rank == 0:
+        peak, peak_kind = measured_peak()
+        value = 2 * total_elems / (ms * 1e-3) / 1e9
+        achieved = algo_bytes / (local_ms * 1e-3) / 1e9
+        prof = profile_traffic()
+        traffic = None
+        if prof and prof.get("chunk_elems") == ce and world == 1:
+            traffic = prof.get("traffic_bytes_per_launch")
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": a.steps,
+            "warmup": a.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "u16", "data": "synthetic (random-init Llama-3-8B shapes, seed 0)",
+            "config": config,
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "peak_source": f"hbm_gbs of {peak_kind}",
+                         "traffic": traffic,
+                         "kernel": "xc_prepare_kernel + xc_decode_kernel (one plan launch pair per step)",
+                         "algorithmic_bytes_per_step": algo_bytes},
+            "e2e": None if e2e_ms is None else {
+                "value": round(2 * total_elems / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4 * len(owned),
+                "ms_per_step": round(e2e_ms, 3),
+                "path": "bigsmall_b200.loader.DeviceLoader.run_async (pinned H2D of compressed blobs "
+                        f"in {n_groups} groups overlapped with decode) + status check"},
+            "gpu_launches": 2 * a.steps,
+            "clocks": clk.summary(),
+            "verified": f"bitwise equal on device for all {len(tensors)} tensors" if n_bad == 0 else f"MISMATCH in {n_bad} parts",
+            "compression_ratio": round(total_comp / (2 * sum(math.prod(s) for _, s, _ in tensors)), 5)
+            if world == 1 else None,
+            "decoded_bytes_per_step": int(2 * total_elems),
+            "setup_s": round(setup_s, 1),
+        }
+        if world == 1 and not a.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline(torch, seconds=a.cpu_seconds, device=dev)
+        print(json.dumps(line), flush=True)
+    plan.close()
+    loader.close()
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+    if n_bad:
+        sys.exit(1)
+
+
+if __name__ == "__main__":
+    main()

@@ -42,6 +42,8 @@ class XcTensor(ctypes.Structure):
         ("d_out", ctypes.c_void_p),
         ("n_elems", ctypes.c_uint64),
         ("chunk_elems", ctypes.c_uint32),
+        ("chunk_begin", ctypes.c_uint32),
+        ("chunk_count", ctypes.c_uint32),
         ("reserved", ctypes.c_uint32),
     ]
 

@@ -173,6 +173,7 @@ int bs_xc_plan_create(const bs_xc_tensor *tensors, int n_tensors, int device, bs
     }
     DeviceGuard guard(device);
     std::vector<XcTensorDev> ht;
+    std::vector<std::pair<uint32_t, uint32_t>> ranges;   // chunk range per internal tensor
     std::vector<int> u2i(n_tensors, -1);
     for (int i = 0; i < n_tensors; i++) {
         const bs_xc_tensor &t = tensors[i];
@@ -186,6 +187,9 @@ int bs_xc_plan_create(const bs_xc_tensor *tensors, int n_tensors, int device, bs
             return fail(BS_E_INVALID_ARG, who + "chunk_elems must be a positive multiple of 256");
         uint64_t nc = (t.n_elems + t.chunk_elems - 1) / t.chunk_elems;
         if (nc > 0x7FFFFFFFull) return fail(BS_E_INVALID_ARG, who + "too many chunks");
+        if (t.chunk_begin >= nc) return fail(BS_E_INVALID_ARG, who + "chunk_begin beyond the last chunk");
+        const uint64_t cnt = t.chunk_count ? t.chunk_count : nc - t.chunk_begin;
+        if (t.chunk_begin + cnt > nc) return fail(BS_E_INVALID_ARG, who + "chunk range beyond the last chunk");
         uint64_t min_bytes = rup(kXcTabOff + 4 * (nc + 1), 16) + rup(t.n_elems, 16) + 128 * nc;
         if (t.blob_bytes < min_bytes) return fail(BS_E_TRUNCATED, who + "blob shorter than its framing");
         if (!on_device(t.d_blob, device) || !on_device(t.d_out, device))
@@ -197,20 +201,24 @@ int bs_xc_plan_create(const bs_xc_tensor *tensors, int n_tensors, int device, bs
         d.n = t.n_elems;
         d.chunk_elems = t.chunk_elems;
         d.n_chunks = static_cast<uint32_t>(nc);
+        d.chunk_begin = t.chunk_begin;
         d.coder = 0xFFFFFFFFu;
         u2i[i] = static_cast<int>(ht.size());
         ht.push_back(d);
+        ranges.push_back({t.chunk_begin, static_cast<uint32_t>(cnt)});
     }
     // work items: <= warps-per-CTA chunks of one tensor; big tensors first so
     // small ones fill the tail of the grid
     const uint32_t W = static_cast<uint32_t>(xc_warps_per_cta());
     std::vector<int> order(ht.size());
     for (size_t i = 0; i < ht.size(); i++) order[i] = static_cast<int>(i);
-    std::stable_sort(order.begin(), order.end(), [&](int a, int b) { return ht[a].n > ht[b].n; });
+    std::stable_sort(order.begin(), order.end(),
+                     [&](int a, int b) { return ranges[a].second > ranges[b].second; });
     std::vector<XcItem> items;
     for (int ti : order) {
-        for (uint32_t c = 0; c < ht[ti].n_chunks; c += W) {
-            XcItem it{static_cast<uint32_t>(ti), c, std::min(W, ht[ti].n_chunks - c), 0};
+        const uint32_t c0 = ranges[ti].first, c1 = ranges[ti].first + ranges[ti].second;
+        for (uint32_t c = c0; c < c1; c += W) {
+            XcItem it{static_cast<uint32_t>(ti), c, std::min(W, c1 - c), 0};
             items.push_back(it);
         }
     }

@@ -35,6 +35,8 @@ struct XcTensorDev {
     uint64_t n;
     uint32_t chunk_elems;
     uint32_t n_chunks;
+    uint32_t chunk_begin;     // d_out holds element chunk_begin * chunk_elems first
+    uint32_t pad0;
     // parsed from the blob header by xc_prepare_kernel
     uint64_t chunks_off;
     uint64_t plane_off;

@@ -386,7 +386,7 @@ __global__ void __launch_bounds__(kThreads) xc_decode_kernel(const XcTensorDev *
     const uint32_t cn = left < T.chunk_elems ? static_cast<uint32_t>(left) : T.chunk_elems;
     uint8_t *ring = s_ring + warp * kRingBytes;
     const uint8_t *plane = blob + T.plane_off + e0;
-    uint16_t *out = T.out + e0;
+    uint16_t *out = T.out + (e0 - static_cast<uint64_t>(T.chunk_begin) * T.chunk_elems);
     if (coder == 0)
         decode_chunk<0>(s_tab, ring, rec, rec_bytes, plane, out, cn, P, &errs[it.tensor]);
     else

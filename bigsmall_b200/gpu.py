@@ -97,8 +97,12 @@ class XcPlan(_Plan):
 
     ``entries``: iterable of ``(blob, out, chunk_elems)`` with ``blob`` a
     1-D uint8 CUDA tensor (16-byte aligned) and ``out`` a contiguous 16-bit
-    CUDA tensor receiving ``out.numel()`` values.  One plan decodes all of
-    them with two kernel launches; it can be re-run any number of times.
+    CUDA tensor receiving ``out.numel()`` values; or of
+    ``(blob, out, chunk_elems, n_total, chunk_begin, chunk_count)`` to decode
+    only chunks [chunk_begin, chunk_begin + chunk_count) of a tensor of
+    ``n_total`` values into ``out`` (element chunk_begin * chunk_elems first).
+    One plan decodes all entries with two kernel launches; it can be re-run
+    any number of times.
     """
 
     def __init__(self, entries: Iterable[tuple], device: Optional[int] = None):
@@ -106,7 +110,9 @@ class XcPlan(_Plan):
         keep = []
         arr = (_lib.XcTensor * max(1, len(entries)))()
         dev = device
-        for i, (blob, out, ce) in enumerate(entries):
+        for i, ent in enumerate(entries):
+            blob, out, ce = ent[:3]
+            n_total, c0, cc = (ent[3], ent[4], ent[5]) if len(ent) > 3 else (out.numel(), 0, 0)
             _as_cuda(blob, "blob")
             _as_cuda(out, "out")
             if blob.dtype != torch.uint8:
@@ -121,8 +127,10 @@ class XcPlan(_Plan):
             arr[i].d_blob = blob.data_ptr() if blob.numel() else None
             arr[i].blob_bytes = blob.numel()
             arr[i].d_out = out.data_ptr() if out.numel() else None
-            arr[i].n_elems = out.numel()
+            arr[i].n_elems = int(n_total)
             arr[i].chunk_elems = int(ce)
+            arr[i].chunk_begin = int(c0)
+            arr[i].chunk_count = int(cc)
             arr[i].reserved = 0
             keep += [blob, out]
         if dev is None:

@@ -53,16 +53,21 @@ extern "C" {
 
 typedef struct bs_plan bs_plan;
 
-/* One bf16_exp_chunked_v1 tensor to decode.  Both pointers must be 16-byte
- * aligned device addresses on the plan's device.  chunk_elems comes from the
- * container header's per-tensor "extra" dict (bigsmall/container.py:17-38
- * keeps codec extras there) and must match the blob header. */
+/* One bf16_exp_chunked_v1 tensor (or a chunk range of one) to decode.  Both
+ * pointers must be 16-byte aligned device addresses on the plan's device.
+ * chunk_elems comes from the container header's per-tensor "extra" dict
+ * (bigsmall/container.py:17-38 keeps codec extras there) and must match the
+ * blob header.  Chunks [chunk_begin, chunk_begin + chunk_count) are decoded
+ * (chunk_count 0: through the last chunk); d_out receives the value of element
+ * chunk_begin * chunk_elems first.  Ranges let several GPUs share one tensor. */
 typedef struct bs_xc_tensor {
     const void *d_blob;
     uint64_t    blob_bytes;
-    void       *d_out;         /* n_elems bf16 values */
-    uint64_t    n_elems;
+    void       *d_out;
+    uint64_t    n_elems;       /* elements of the whole tensor */
     uint32_t    chunk_elems;
+    uint32_t    chunk_begin;
+    uint32_t    chunk_count;
     uint32_t    reserved;      /* must be 0 */
 } bs_xc_tensor;
 
