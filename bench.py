@@ -226,6 +226,9 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=8.0)
+    ap.add_argument("--config", default="c2", choices=["c2", "small"],
+                    help="c2: the benchmark workload; small: one 2^27-value tensor of the same "
+                         "distribution (compressed ~170 MB, above L2) for ncu captures")
     a = ap.parse_args()
     a.warmup = max(3, a.warmup)
 
@@ -270,7 +273,11 @@ def main():
         if dist: dist.destroy_process_group()
         return
 
-    tensors = llama3_8b_tensors()
+    if a.config == "small":
+        tensors = [("model.layers.0.mlp.small_proj.weight", (1 << 15, 4096), "linear")]
+        config["workload"] = "one 2^27-value bf16 tensor, config-2 distribution (profiling case)"
+    else:
+        tensors = llama3_8b_tensors()
     owned_all, load = partition(tensors, world, ce)
     owned = owned_all[rank]
     owned_names = {n for n, _, _ in owned}
