@@ -311,6 +311,79 @@ int bs_plan_check(bs_plan *p, void *stream, uint32_t *status_out) {
 }
 
 // --------------------------------------------------------------------------
+// allocation-free decode: same validation as bs_xc_plan_create, scratch in a
+// static device array (xc_decode.cu), no cudaMalloc/cudaFree anywhere
+// --------------------------------------------------------------------------
+int bs_xc_decode_noalloc(const bs_xc_tensor *tensors, int n_tensors, void *stream, uint32_t *status_out) {
+    if (n_tensors < 0 || n_tensors > BS_NOALLOC_MAX_TENSORS)
+        return fail(BS_E_INVALID_ARG, "bs_xc_decode_noalloc decodes at most " +
+                                          std::to_string(BS_NOALLOC_MAX_TENSORS) + " tensors per call (got " +
+                                          std::to_string(n_tensors) + ")");
+    if (n_tensors > 0 && !tensors) return fail(BS_E_INVALID_ARG, "tensors is NULL");
+    int device = 0;
+    if (cudaGetDevice(&device) != cudaSuccess) {
+        cudaGetLastError();
+        return fail(BS_E_CUDA, "no current CUDA device");
+    }
+    XcTensorDev ht[BS_NOALLOC_MAX_TENSORS];
+    uint32_t rc_count[BS_NOALLOC_MAX_TENSORS];
+    int u2i[BS_NOALLOC_MAX_TENSORS];
+    int n = 0;
+    for (int i = 0; i < n_tensors; i++) {
+        const bs_xc_tensor &t = tensors[i];
+        u2i[i] = -1;
+        if (t.n_elems == 0) continue;
+        const std::string who = "tensor " + std::to_string(i) + ": ";
+        if (t.reserved != 0) return fail(BS_E_INVALID_ARG, who + "reserved field must be 0");
+        if (!t.d_blob || !t.d_out) return fail(BS_E_INVALID_ARG, who + "NULL pointer");
+        if ((reinterpret_cast<uintptr_t>(t.d_blob) | reinterpret_cast<uintptr_t>(t.d_out)) & 15)
+            return fail(BS_E_INVALID_ARG, who + "blob and output must be 16-byte aligned");
+        if (t.chunk_elems < 256 || (t.chunk_elems & 255))
+            return fail(BS_E_INVALID_ARG, who + "chunk_elems must be a positive multiple of 256");
+        const uint64_t nc = (t.n_elems + t.chunk_elems - 1) / t.chunk_elems;
+        if (nc > 0x7FFFFFFFull) return fail(BS_E_INVALID_ARG, who + "too many chunks");
+        if (t.chunk_begin >= nc) return fail(BS_E_INVALID_ARG, who + "chunk_begin beyond the last chunk");
+        const uint64_t cnt = t.chunk_count ? t.chunk_count : nc - t.chunk_begin;
+        if (t.chunk_begin + cnt > nc) return fail(BS_E_INVALID_ARG, who + "chunk range beyond the last chunk");
+        const uint64_t min_bytes = rup(kXcTabOff + 4 * (nc + 1), 16) + rup(t.n_elems, 16) + 128 * nc;
+        if (t.blob_bytes < min_bytes) return fail(BS_E_TRUNCATED, who + "blob shorter than its framing");
+        if (!on_device(t.d_blob, device) || !on_device(t.d_out, device))
+            return fail(BS_E_INVALID_ARG, who + "pointers must be device memory of the current device");
+        XcTensorDev d{};
+        d.blob = static_cast<const uint8_t *>(t.d_blob);
+        d.blob_bytes = t.blob_bytes;
+        d.out = static_cast<uint16_t *>(t.d_out);
+        d.n = t.n_elems;
+        d.chunk_elems = t.chunk_elems;
+        d.n_chunks = static_cast<uint32_t>(nc);
+        d.chunk_begin = t.chunk_begin;
+        d.coder = 0xFFFFFFFFu;
+        ht[n] = d;
+        rc_count[n] = static_cast<uint32_t>(cnt);
+        u2i[i] = n++;
+    }
+    uint32_t st[BS_NOALLOC_MAX_TENSORS] = {};
+    if (n > 0) {
+        cudaError_t e = launch_xc_noalloc(ht, rc_count, n, static_cast<cudaStream_t>(stream), st);
+        if (e != cudaSuccess) return cuda_fail(e, "bs_xc_decode_noalloc");
+    }
+    bool bad = false;
+    std::string msg;
+    for (int i = 0; i < n_tensors; i++) {
+        const uint32_t w = u2i[i] >= 0 ? st[u2i[i]] : 0u;
+        if (status_out) status_out[i] = w;
+        if (w && !bad) {
+            char b[16];
+            snprintf(b, sizeof b, "%x", w);
+            msg = "tensor " + std::to_string(i) + " device status 0x" + b;
+            bad = true;
+        }
+    }
+    if (bad) return fail(BS_E_CORRUPT, msg);
+    return BS_OK;
+}
+
+// --------------------------------------------------------------------------
 // bf16_parallel_v1 (bigsmall/codecs/bf16_parallel.py:15-52 layout)
 // --------------------------------------------------------------------------
 int bs_par_plan_create(const uint8_t *h, uint64_t len, uint64_t n_weights, const void *d_blob, void *d_out,

@@ -82,6 +82,9 @@ cudaError_t launch_xc_prepare(XcTensorDev *d_tens, int n_tensors, uint32_t *d_ta
 cudaError_t launch_xc_decode(const XcTensorDev *d_tens, const XcItem *d_items, int n_items,
                              const uint32_t *d_tables, uint32_t *d_errs, cudaStream_t s);
 int xc_warps_per_cta();
+cudaError_t launch_xc_noalloc(const XcTensorDev *h_tens, const uint32_t *range_count, int n, cudaStream_t s,
+                              uint32_t *h_status);
+uint64_t xc_noalloc_scratch_bytes();
 
 cudaError_t launch_par_jobs(const uint8_t *d_blob, const ParJob *d_jobs, int n_jobs,
                             const uint2 *d_se_tab, const uint2 *d_m_tabs, uint16_t *d_se_sym,

@@ -27,6 +27,7 @@
 //                      sign/mantissa plane is read with 8-byte loads two groups
 //                      ahead; output leaves as 16-byte streaming stores.
 #include <cstdint>
+#include <mutex>
 
 #include "common.cuh"
 
@@ -414,5 +415,131 @@ cudaError_t launch_xc_decode(const XcTensorDev *d_tens, const XcItem *d_items, i
     xc_decode_kernel<<<n_items, kThreads, smem, s>>>(d_tens, d_items, d_tables, d_errs);
     return cudaGetLastError();
 }
+
+// --------------------------------------------------------------------------
+// Allocation-free decode (bs_xc_decode_noalloc).
+//
+// For callers that must not allocate device memory: the per-call scratch (the
+// tensors' descriptors, their decode tables and status words) lives in this
+// file-scope array instead of plan memory.  Every GPU that loads the library
+// holds it (kNoallocScratchBytes) until the process exits.  All calls share
+// it, so calls whose GPU work overlaps race; each call rewrites every field it
+// reads (descriptors by the stage kernel, tables and status words by
+// xc_prepare_kernel), so a call never depends on what the previous one left.
+// --------------------------------------------------------------------------
+constexpr int kNoallocMaxTensors = BS_NOALLOC_MAX_TENSORS;
+constexpr uint64_t kNoallocTablesOff = 0;
+constexpr uint64_t kNoallocTensOff = kNoallocTablesOff + 4ull * kXcMaxTable * kNoallocMaxTensors;
+constexpr uint64_t kNoallocErrsOff = kNoallocTensOff + 256ull * ((sizeof(XcTensorDev) * kNoallocMaxTensors + 255) / 256);
+constexpr uint64_t kNoallocScratchBytes = kNoallocErrsOff + 256;
+
+static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoallocScratchBytes];
+
+// by-value kernel arguments: descriptors and the per-tensor CTA prefix
+struct NoallocArgs {
+    XcTensorDev tens[kNoallocMaxTensors];
+    uint32_t range_count[kNoallocMaxTensors];        // chunks decoded per tensor
+    uint32_t cta_prefix[kNoallocMaxTensors + 1];     // first CTA of each tensor
+    int n;
+};
+
+__global__ void xc_noalloc_stage_kernel(const NoallocArgs a, XcTensorDev *tens) {
+    const int t = threadIdx.x;
+    if (t < a.n) tens[t] = a.tens[t];
+}
+
+__global__ void __launch_bounds__(kThreads) xc_decode_noalloc_kernel(const NoallocArgs a,
+                                                                     const XcTensorDev *__restrict__ tens,
+                                                                     const uint32_t *__restrict__ tables,
+                                                                     uint32_t *errs) {
+    extern __shared__ __align__(16) uint8_t smem[];
+    uint32_t *s_tab = reinterpret_cast<uint32_t *>(smem);
+    uint8_t *s_ring = smem + kXcMaxTable * 4;
+    int ti = 0;
+    while (ti + 1 < a.n && blockIdx.x >= a.cta_prefix[ti + 1]) ti++;
+    const XcTensorDev &T = tens[ti];
+    const uint32_t coder = T.coder;
+    if (coder > 1) return;   // xc_prepare_kernel flagged this tensor
+    const uint32_t P = T.prec;
+    const uint32_t M = 1u << P;
+    const uint4 *src = reinterpret_cast<const uint4 *>(tables + static_cast<uint64_t>(ti) * kXcMaxTable);
+    for (uint32_t i = threadIdx.x; i < M / 4; i += kThreads) reinterpret_cast<uint4 *>(s_tab)[i] = src[i];
+    __syncthreads();
+    const uint32_t warp = threadIdx.x >> 5;
+    const uint32_t c0 = a.tens[ti].chunk_begin;
+    const uint32_t c = c0 + (blockIdx.x - a.cta_prefix[ti]) * kWarps + warp;
+    if (c >= c0 + a.range_count[ti]) return;
+    const uint8_t *blob = T.blob;
+    const uint32_t *cs = reinterpret_cast<const uint32_t *>(blob + kXcTabOff);
+    const uint32_t ca = cs[c], cz = cs[c + 1];
+    const uint8_t *rec = blob + T.chunks_off + 16ull * ca;
+    const uint32_t rec_bytes = 16u * (cz - ca);
+    const uint64_t e0 = static_cast<uint64_t>(c) * T.chunk_elems;
+    const uint64_t left = T.n - e0;
+    const uint32_t cn = left < T.chunk_elems ? static_cast<uint32_t>(left) : T.chunk_elems;
+    uint8_t *ring = s_ring + warp * kRingBytes;
+    const uint8_t *plane = blob + T.plane_off + e0;
+    uint16_t *out = T.out + (e0 - static_cast<uint64_t>(T.chunk_begin) * T.chunk_elems);
+    if (coder == 0)
+        decode_chunk<0>(s_tab, ring, rec, rec_bytes, plane, out, cn, P, &errs[ti]);
+    else
+        decode_chunk<1>(s_tab, ring, rec, rec_bytes, plane, out, cn, P, &errs[ti]);
+}
+
+namespace {
+std::mutex g_noalloc_mu;
+uint8_t *g_noalloc_ptr[128] = {};   // device address of g_noalloc_scratch, per device
+}  // namespace
+
+// Set-up (first call on a device, with that device current): resolve the
+// scratch array's device address.  In host code the symbol is only a host-side
+// stand-in, so kernels receive this address instead.
+static cudaError_t noalloc_scratch(int dev, uint8_t **out) {
+    if (dev < 0 || dev >= 128) return cudaErrorInvalidDevice;
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    if (!g_noalloc_ptr[dev]) {
+        void *p = nullptr;
+        cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess) return e;
+        g_noalloc_ptr[dev] = static_cast<uint8_t *>(p);
+    }
+    *out = g_noalloc_ptr[dev];
+    return cudaSuccess;
+}
+
+cudaError_t launch_xc_noalloc(const XcTensorDev *h_tens, const uint32_t *range_count, int n, cudaStream_t s,
+                              uint32_t *h_status) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    uint8_t *scr = nullptr;
+    e = noalloc_scratch(dev, &scr);
+    if (e != cudaSuccess) return e;
+    XcTensorDev *d_tens = reinterpret_cast<XcTensorDev *>(scr + kNoallocTensOff);
+    uint32_t *d_tables = reinterpret_cast<uint32_t *>(scr + kNoallocTablesOff);
+    uint32_t *d_errs = reinterpret_cast<uint32_t *>(scr + kNoallocErrsOff);
+    NoallocArgs a{};
+    a.n = n;
+    a.cta_prefix[0] = 0;
+    for (int i = 0; i < n; i++) {
+        a.tens[i] = h_tens[i];
+        a.range_count[i] = range_count[i];
+        a.cta_prefix[i + 1] = a.cta_prefix[i] + (range_count[i] + kWarps - 1) / kWarps;
+    }
+    for (int i = n; i < kNoallocMaxTensors; i++) a.cta_prefix[i + 1] = a.cta_prefix[n];
+    xc_noalloc_stage_kernel<<<1, kNoallocMaxTensors, 0, s>>>(a, d_tens);
+    e = cudaGetLastError();
+    if (e == cudaSuccess) e = launch_xc_prepare(d_tens, n, d_tables, d_errs, s);
+    if (e == cudaSuccess && a.cta_prefix[n] > 0) {
+        const size_t smem = kXcMaxTable * 4 + kWarps * kRingBytes;
+        xc_decode_noalloc_kernel<<<a.cta_prefix[n], kThreads, smem, s>>>(a, d_tens, d_tables, d_errs);
+        e = cudaGetLastError();
+    }
+    if (e == cudaSuccess) e = cudaMemcpyAsync(h_status, d_errs, 4ull * n, cudaMemcpyDeviceToHost, s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    return e;
+}
+
+uint64_t xc_noalloc_scratch_bytes() { return kNoallocScratchBytes; }
 
 }  // namespace bsg

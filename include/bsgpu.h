@@ -97,6 +97,26 @@ int bs_plan_check(bs_plan *plan, void *stream, uint32_t *status_out);
 int bs_plan_n_tensors(const bs_plan *plan);
 int bs_plan_destroy(bs_plan *plan);
 
+/* ---- allocation-free decode -------------------------------------------- */
+/* No counterpart in the reference.  Decodes up to BS_NOALLOC_MAX_TENSORS
+ * bf16_exp_chunked_v1 tensors (descriptors as for bs_xc_plan_create) on
+ * `stream` without allocating any device memory: for callers that cannot call
+ * cudaMalloc -- e.g. a serving engine that has already reserved nearly all of
+ * HBM for its own arena or KV cache (a fresh cudaMalloc can fail there), or a
+ * latency-critical path where cudaMalloc/cudaFree would synchronise the whole
+ * device.  Its scratch (descriptors, decode tables, status words; about
+ * 130 KiB) is a static device array that every GPU loading the library holds
+ * until the process exits.  The first call on a device resolves that array's
+ * address (with the device current); make that first call before any stream
+ * capture.  All calls share the array, so calls whose GPU work overlaps race:
+ * serialise them.  Synchronous: returns after `stream` has finished the
+ * decode, with the per-tensor device status words in `status_out` (may be
+ * NULL; else n_tensors entries).  More than BS_NOALLOC_MAX_TENSORS tensors is
+ * BS_E_INVALID_ARG. */
+#define BS_NOALLOC_MAX_TENSORS 8
+int bs_xc_decode_noalloc(const bs_xc_tensor *tensors, int n_tensors, void *stream,
+                         uint32_t *status_out);
+
 /* ---- bf16_parallel_v1 decode (the reference's GPU format) --------------- */
 /* Parse a PAR1 blob's framing on the host (`h_blob`, the same bytes as at
  * `d_blob` on the device) and build a decode plan writing n_weights bf16
