@@ -23,9 +23,10 @@
 //   xc_decode_kernel   one CTA per work item (<= 8 chunks of one tensor): copies
 //                      the table into shared memory, then each warp decodes one
 //                      chunk.  Compressed words are staged per warp in a 2 KiB
-//                      shared-memory ring fed by 16-byte cp.async copies; the
-//                      sign/mantissa plane is read with 8-byte loads two groups
-//                      ahead; output leaves as 16-byte streaming stores.
+//                      shared-memory ring (plus a 1 KiB mirror of its head)
+//                      fed by 16-byte cp.async copies; the sign/mantissa plane
+//                      is read with 8-byte loads two groups ahead; output
+//                      leaves as 16-byte streaming stores.
 #include <cstdint>
 #include <mutex>
 
@@ -36,7 +37,6 @@ namespace bsg {
 constexpr int kWarps = 8;                   // warps (= chunks) per CTA
 constexpr int kThreads = kWarps * 32;
 constexpr uint32_t kRingBytes = 2048;       // per-warp staging ring
-constexpr uint32_t kRingWords = kRingBytes / 2;
 constexpr uint32_t kFill = 512;             // bytes per refill: 32 lanes x 16 B
 
 int xc_warps_per_cta() { return kWarps; }
@@ -51,6 +51,16 @@ __device__ __forceinline__ void cp_async16(void *smem, const void *gmem) {
     uint32_t s = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(s), "l"(gmem) : "memory");
 }
+__device__ __forceinline__ uint32_t lds_u16(uint32_t a) {
+    unsigned short v;
+    asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(a));
+    return v;
+}
+__device__ __forceinline__ uint32_t lds_u32(uint32_t a) {
+    uint32_t v;
+    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(a));
+    return v;
+}
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;\n" ::: "memory"); }
 
@@ -64,17 +74,6 @@ __device__ __forceinline__ void st_out16(uint16_t *p, uint4 v) {
     asm volatile("st.global.cs.v4.u32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(v.x), "r"(v.y), "r"(v.z),
                  "r"(v.w)
                  : "memory");
-}
-
-// Two bf16 words from two exponent symbols and two sign|mantissa bytes packed
-// as bytes 0 and 2 of `sm2` (bytes 1 and 3 zero).
-__device__ __forceinline__ uint32_t merge2(uint32_t e0, uint32_t e1, uint32_t sm2) {
-    uint32_t ep = __byte_perm(e0, e1, 0x5410);          // e0 | e1 << 16
-    return (sm2 & 0x007F007Fu) | ((sm2 << 8) & 0x80008000u) | (ep << 7);
-}
-
-__device__ __forceinline__ uint16_t merge1(uint32_t e, uint32_t sm) {
-    return static_cast<uint16_t>(((sm & 0x80u) << 8) | (e << 7) | (sm & 0x7Fu));
 }
 
 // --------------------------------------------------------------------------
@@ -164,7 +163,7 @@ __global__ void __launch_bounds__(256) xc_prepare_kernel(XcTensorDev *tens, uint
     }
     uint32_t *tab = tables + static_cast<uint64_t>(t) * kXcMaxTable;
     if (coder == 0) {
-        // rANS entry: sym | freq << 8 | (slot - cum) << 20; 16 slots per thread
+        // rANS entry: (slot - cum) | sym << 12 | freq << 20; 16 slots per thread
         const uint32_t per = (M + 255) / 256;
         uint32_t s0 = tid * per;
         if (s0 < M) {
@@ -177,7 +176,7 @@ __global__ void __launch_bounds__(256) xc_prepare_kernel(XcTensorDev *tens, uint
             for (uint32_t k = 0; k < per && s0 + k < M; k++) {
                 uint32_t slot = s0 + k;
                 while (s_cum[s + 1] <= slot) s++;
-                tab[slot] = s | (s_freq[s] << 8) | ((slot - s_cum[s]) << 20);
+                tab[slot] = (slot - s_cum[s]) | (s << 12) | (s_freq[s] << 20);
             }
         }
     } else {
@@ -206,7 +205,7 @@ __global__ void __launch_bounds__(256) xc_prepare_kernel(XcTensorDev *tens, uint
                 __syncwarp();
                 uint32_t nb = P - (31 - __clz(xs));
                 uint32_t base = (xs << nb) - M;
-                tab[i] = s | (nb << 8) | (base << 12);
+                tab[i] = base | (s << 12) | (nb << 20);
             }
         }
     }
@@ -230,8 +229,16 @@ __global__ void __launch_bounds__(256) xc_prepare_kernel(XcTensorDev *tens, uint
 // --------------------------------------------------------------------------
 // chunk decode
 // --------------------------------------------------------------------------
+// Per-warp staging ring: kRingBytes of compressed words followed by a kMirror
+// copy of the ring's first two kFill blocks.  One loop iteration (two groups of
+// 8 steps) consumes at most 16 x 32 words = 1024 bytes, so reading from the
+// iteration's start offset onwards never needs a wrap mask: offsets past
+// kRingBytes land in the mirror.
+constexpr uint32_t kMirror = 2 * kFill;
+constexpr uint32_t kWarpRing = kRingBytes + kMirror;
+
 struct Ring {
-    uint8_t *buf;            // this warp's kRingBytes of shared memory
+    uint8_t *buf;            // this warp's kWarpRing bytes of shared memory
     const uint8_t *src;      // first renorm word of the chunk record
     uint32_t bytes;          // renorm bytes in the record (multiple of 16)
     uint32_t fetched;        // bytes requested so far (multiple of kFill)
@@ -239,15 +246,19 @@ struct Ring {
 };
 
 __device__ __forceinline__ void ring_issue(Ring &r, uint32_t lane) {
-    uint32_t off = r.fetched + 16 * lane;
-    if (off < r.bytes) cp_async16(r.buf + (off & (kRingBytes - 1)), r.src + off);
+    const uint32_t off = r.fetched + 16 * lane;
+    if (off < r.bytes) {
+        const uint32_t pos = off & (kRingBytes - 1);
+        cp_async16(r.buf + pos, r.src + off);
+        if (pos < kMirror) cp_async16(r.buf + kRingBytes + pos, r.src + off);
+    }
     cp_async_commit();
     r.fetched += kFill;
 }
 
-// make bytes [0, min(bytes, consumed + kFill)) visible to the whole warp
+// make bytes [0, min(bytes, consumed + kMirror)) visible to the whole warp
 __device__ __forceinline__ void ring_ensure(Ring &r, uint32_t consumed_bytes) {
-    uint32_t need = consumed_bytes + kFill;
+    uint32_t need = consumed_bytes + kMirror;
     if (need > r.bytes) need = r.bytes;
     if (need > r.landed) {
         cp_async_wait_all();
@@ -264,6 +275,21 @@ __device__ __forceinline__ void ring_refill(Ring &r, uint32_t consumed_bytes, ui
     }
 }
 
+// Decode-table entries keep the exponent symbol in bits 12..19:
+//   rANS: (slot - cum) | sym << 12 | freq << 20
+//   tANS: next-state base | sym << 12 | bits << 20
+// Two bf16 words from two entries and the pair's sign|mantissa bytes given
+// duplicated as [c0, c0, c1, c1]: bit 15/31 and bits 0-6/16-22 come from the
+// plane bytes, bits 7-14/23-30 from the symbols.
+__device__ __forceinline__ uint32_t merge_pair(uint32_t t0, uint32_t t1, uint32_t cc) {
+    const uint32_t e7 = __byte_perm(t0, t1, 0x6521) << 3;
+    return (cc & 0x807F807Fu) | (e7 & 0x7F807F80u);
+}
+
+__device__ __forceinline__ uint16_t merge_one(uint32_t t, uint32_t c) {
+    return static_cast<uint16_t>(((c & 0x80u) << 8) | (((t >> 12) & 0xFFu) << 7) | (c & 0x7Fu));
+}
+
 template <int CODER>
 __device__ __forceinline__ void decode_chunk(const uint32_t *__restrict__ s_tab, uint8_t *ring_buf,
                                              const uint8_t *__restrict__ rec, uint32_t rec_bytes,
@@ -273,10 +299,11 @@ __device__ __forceinline__ void decode_chunk(const uint32_t *__restrict__ s_tab,
     const uint32_t lane = threadIdx.x & 31;
     const uint32_t lt = lanemask_lt();
     const uint32_t smask = (1u << P) - 1;
-    const uint16_t *ring16 = reinterpret_cast<const uint16_t *>(ring_buf);
 
-    uint32_t init = reinterpret_cast<const uint32_t *>(rec)[lane];
-    // coder state: rANS x; tANS (st, buf, cnt)
+    const uint32_t ring_s = static_cast<uint32_t>(__cvta_generic_to_shared(ring_buf));
+    const uint32_t tab_s = static_cast<uint32_t>(__cvta_generic_to_shared(s_tab));
+    const uint32_t init = reinterpret_cast<const uint32_t *>(rec)[lane];
+    // coder state: rANS x; tANS (st, bits, cnt)
     uint32_t x = init, st = init & 0xFFFF, bits = init >> 16, cnt = 16;
     (void)st; (void)bits; (void)cnt;
 
@@ -284,73 +311,98 @@ __device__ __forceinline__ void decode_chunk(const uint32_t *__restrict__ s_tab,
 #pragma unroll
     for (int k = 0; k < (int)(kRingBytes / kFill); k++) ring_issue(r, lane);
 
-    uint32_t base = 0;   // words consumed by the warp (uniform)
+    uint32_t raddr = ring_s;  // shared address of the next unconsumed word (uniform)
+    uint32_t consumed = 0;    // renorm bytes consumed so far (uniform)
     const uint32_t G = cn >> 8, rem = cn & 255;
 
+    // One step for the whole warp; returns the lane's decode-table entry.  The
+    // renorm word is read by every lane (inside the ring + mirror) and used
+    // only where needed, so the step has no divergent branch.  Shared loads use
+    // 32-bit shared-window addresses.
     auto step = [&](bool active) -> uint32_t {
-        uint32_t sym;
+        uint32_t t;
         if (CODER == 0) {
-            uint32_t t = active ? s_tab[x & smask] : 0u;
-            sym = t & 0xFF;
-            uint32_t nx = ((t >> 8) & 0xFFF) * (x >> P) + (t >> 20);
+            t = lds_u32(tab_s + ((x & smask) << 2));
+            const uint32_t nx = (t >> 20) * (x >> P) + (t & 0xFFFu);
             if (active) x = nx;
-            bool need = active && (x < kRansL);
-            uint32_t m = __ballot_sync(kFull, need);
-            if (need) x = (x << 16) | ring16[(base + __popc(m & lt)) & (kRingWords - 1)];
-            base += __popc(m);
+            const bool need = active && (x < kRansL);
+            const uint32_t m = __ballot_sync(kFull, need);
+            const uint32_t w = lds_u16(raddr + 2 * __popc(m & lt));
+            if (need) x = x * 65536u + w;
+            raddr += 2 * __popc(m);
         } else {
-            bool need = active && (cnt < P);
-            uint32_t m = __ballot_sync(kFull, need);
+            const bool need = active && (cnt < P);
+            const uint32_t m = __ballot_sync(kFull, need);
+            const uint32_t w = lds_u16(raddr + 2 * __popc(m & lt));
             if (need) {
-                bits |= static_cast<uint32_t>(ring16[(base + __popc(m & lt)) & (kRingWords - 1)]) << cnt;
+                bits |= w << cnt;
                 cnt += 16;
             }
-            base += __popc(m);
-            uint32_t t = active ? s_tab[st] : 0u;
-            sym = t & 0xFF;
+            raddr += 2 * __popc(m);
+            t = lds_u32(tab_s + (st << 2));
             if (active) {
-                uint32_t nb = (t >> 8) & 0xF;
-                st = (t >> 12) + (bits & ((1u << nb) - 1));
+                const uint32_t nb = t >> 20;
+                st = (t & 0xFFFu) + (bits & ((1u << nb) - 1));
                 bits >>= nb;
                 cnt -= nb;
             }
         }
-        return sym;
+        return t;
     };
-
-    uint2 sm_a = make_uint2(0, 0), sm_b = make_uint2(0, 0);
-    if (G > 0) sm_a = ld_plane8(plane + lane * 8);
-    if (G > 1) sm_b = ld_plane8(plane + 256 + lane * 8);
-    for (uint32_t g = 0; g < G; g++) {
-        ring_ensure(r, base * 2);
-        uint2 sm = sm_a;
-        sm_a = sm_b;
-        if (g + 2 < G) sm_b = ld_plane8(plane + (g + 2) * 256 + lane * 8);
-        uint32_t e0 = step(true), e1 = step(true), e2 = step(true), e3 = step(true);
-        uint32_t e4 = step(true), e5 = step(true), e6 = step(true), e7 = step(true);
+    auto group = [&](uint32_t g, uint2 sm) {
+        const uint32_t t0 = step(true), t1 = step(true), t2 = step(true), t3 = step(true);
+        const uint32_t t4 = step(true), t5 = step(true), t6 = step(true), t7 = step(true);
         uint4 v;
-        v.x = merge2(e0, e1, __byte_perm(sm.x, 0, 0x4140));
-        v.y = merge2(e2, e3, __byte_perm(sm.x, 0, 0x4342));
-        v.z = merge2(e4, e5, __byte_perm(sm.y, 0, 0x4140));
-        v.w = merge2(e6, e7, __byte_perm(sm.y, 0, 0x4342));
+        v.x = merge_pair(t0, t1, __byte_perm(sm.x, 0, 0x1100));
+        v.y = merge_pair(t2, t3, __byte_perm(sm.x, 0, 0x3322));
+        v.z = merge_pair(t4, t5, __byte_perm(sm.y, 0, 0x1100));
+        v.w = merge_pair(t6, t7, __byte_perm(sm.y, 0, 0x3322));
         st_out16(out + g * 256 + lane * 8, v);
-        ring_refill(r, base * 2, lane);
+    };
+    const uint32_t ring_end = ring_s + kRingBytes;
+    const uint8_t *pl = plane + lane * 8;
+    uint2 sm_a = make_uint2(0, 0), sm_b = make_uint2(0, 0);
+    if (G > 0) sm_a = ld_plane8(pl);
+    if (G > 1) sm_b = ld_plane8(pl + 256);
+    uint32_t g = 0;
+    for (; g + 1 < G; g += 2) {
+        ring_ensure(r, consumed);
+        if (raddr >= ring_end) raddr -= kRingBytes;
+        const uint32_t rstart = raddr;
+        const uint2 s0 = sm_a, s1 = sm_b;
+        // next two groups' plane bytes (clamped to the last full group)
+        sm_a = ld_plane8(pl + min(g + 2, G - 1) * 256);
+        sm_b = ld_plane8(pl + min(g + 3, G - 1) * 256);
+        group(g, s0);
+        group(g + 1, s1);
+        consumed += raddr - rstart;
+        ring_refill(r, consumed, lane);
+        ring_refill(r, consumed, lane);
+    }
+    if (g < G) {
+        ring_ensure(r, consumed);
+        if (raddr >= ring_end) raddr -= kRingBytes;
+        const uint32_t rstart = raddr;
+        group(g, sm_a);
+        consumed += raddr - rstart;
     }
     if (rem) {
-        ring_ensure(r, base * 2);
+        ring_ensure(r, consumed);
+        if (raddr >= ring_end) raddr -= kRingBytes;
+        const uint32_t rstart = raddr;
         const uint32_t e_base = G * 256 + lane * 8;
 #pragma unroll 1
         for (uint32_t j = 0; j < 8; j++) {
-            bool active = (lane * 8 + j) < rem;
-            uint32_t sym = step(active);
-            if (active) out[e_base + j] = merge1(sym, plane[e_base + j]);
+            const bool active = (lane * 8 + j) < rem;
+            const uint32_t t = step(active);
+            if (active) out[e_base + j] = merge_one(t, plane[e_base + j]);
         }
+        consumed += raddr - rstart;
     }
     cp_async_wait_all();
     __syncwarp();
-    bool bad_state = CODER == 0 ? (x != kRansL) : (st != 0);
-    uint32_t used = base * 2;
-    bool bad_stream = used > r.bytes || (r.bytes - used) >= 16;
+    const bool bad_state = CODER == 0 ? (x != kRansL) : (st != 0);
+    const bool bad_stream = consumed > r.bytes || (r.bytes - consumed) >= 16;
     uint32_t code = (bad_state ? BS_DEV_FINAL_STATE : 0u) | (bad_stream ? BS_DEV_STREAM : 0u);
     code = __reduce_or_sync(kFull, code);
     if (code && lane == 0) atomicOr(err, code);
@@ -385,7 +437,7 @@ __global__ void __launch_bounds__(kThreads) xc_decode_kernel(const XcTensorDev *
     const uint64_t e0 = static_cast<uint64_t>(c) * T.chunk_elems;
     const uint64_t left = T.n - e0;
     const uint32_t cn = left < T.chunk_elems ? static_cast<uint32_t>(left) : T.chunk_elems;
-    uint8_t *ring = s_ring + warp * kRingBytes;
+    uint8_t *ring = s_ring + warp * kWarpRing;
     const uint8_t *plane = blob + T.plane_off + e0;
     uint16_t *out = T.out + (e0 - static_cast<uint64_t>(T.chunk_begin) * T.chunk_elems);
     if (coder == 0)
@@ -404,7 +456,7 @@ cudaError_t launch_xc_prepare(XcTensorDev *d_tens, int n_tensors, uint32_t *d_ta
 cudaError_t launch_xc_decode(const XcTensorDev *d_tens, const XcItem *d_items, int n_items,
                              const uint32_t *d_tables, uint32_t *d_errs, cudaStream_t s) {
     if (n_items <= 0) return cudaSuccess;
-    const size_t smem = kXcMaxTable * 4 + kWarps * kRingBytes;
+    const size_t smem = kXcMaxTable * 4 + kWarps * kWarpRing;
     static bool attr_set = false;   // idempotent; a benign race
     if (!attr_set) {
         cudaError_t e = cudaFuncSetAttribute(xc_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -477,7 +529,7 @@ __global__ void __launch_bounds__(kThreads) xc_decode_noalloc_kernel(const Noall
     const uint64_t e0 = static_cast<uint64_t>(c) * T.chunk_elems;
     const uint64_t left = T.n - e0;
     const uint32_t cn = left < T.chunk_elems ? static_cast<uint32_t>(left) : T.chunk_elems;
-    uint8_t *ring = s_ring + warp * kRingBytes;
+    uint8_t *ring = s_ring + warp * kWarpRing;
     const uint8_t *plane = blob + T.plane_off + e0;
     uint16_t *out = T.out + (e0 - static_cast<uint64_t>(T.chunk_begin) * T.chunk_elems);
     if (coder == 0)
@@ -531,7 +583,7 @@ cudaError_t launch_xc_noalloc(const XcTensorDev *h_tens, const uint32_t *range_c
     e = cudaGetLastError();
     if (e == cudaSuccess) e = launch_xc_prepare(d_tens, n, d_tables, d_errs, s);
     if (e == cudaSuccess && a.cta_prefix[n] > 0) {
-        const size_t smem = kXcMaxTable * 4 + kWarps * kRingBytes;
+        const size_t smem = kXcMaxTable * 4 + kWarps * kWarpRing;
         xc_decode_noalloc_kernel<<<a.cta_prefix[n], kThreads, smem, s>>>(a, d_tens, d_tables, d_errs);
         e = cudaGetLastError();
     }
