@@ -226,9 +226,10 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=8.0)
-    ap.add_argument("--config", default="c2", choices=["c2", "small"],
+    ap.add_argument("--config", default="c2", choices=["c2", "small", "kv", "sweep"],
                     help="c2: the benchmark workload; small: one 2^27-value tensor of the same "
-                         "distribution (compressed ~170 MB, above L2) for ncu captures")
+                         "distribution (compressed ~170 MB, above L2) for ncu captures; kv: BASELINE "
+                         "config 5 (KV cache encode+decode); sweep: config 3 (rANS vs tANS x chunk size)")
     a = ap.parse_args()
     a.warmup = max(3, a.warmup)
 
@@ -273,6 +274,10 @@ def main():
         if dist: dist.destroy_process_group()
         return
 
+    if a.config == "kv":
+        return bench_kv(a, torch, dev, world, rank, dist, local)
+    if a.config == "sweep":
+        return bench_sweep(a, torch, dev, world, rank, dist, local)
     if a.config == "small":
         tensors = [("model.layers.0.mlp.small_proj.weight", (1 << 15, 4096), "linear")]
         config["workload"] = "one 2^27-value bf16 tensor, config-2 distribution (profiling case)"
@@ -446,6 +451,128 @@ def main():
     if n_bad:
         sys.exit(1)
 
+
+
+# ---------------------------------------------------------------------------
+# config 5: KV cache (batch sharded across ranks)
+# ---------------------------------------------------------------------------
+def _timed(torch, fn, steps, warmup, stream):
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record(stream)
+    for _ in range(steps):
+        fn()
+    e.record(stream)
+    torch.cuda.synchronize()
+    return s.elapsed_time(e) / steps
+
+
+def bench_kv(a, torch, dev, world, rank, dist, local):
+    """32 layers x {K, V} of [16, 8, 8192, 128] bf16, N(0,1) x per-channel scale
+    log-normal(0,1) [1,8,1,128], seed 0; this rank encodes and decodes its batch slice."""
+    from bigsmall_b200 import gpu
+    B, H, T, D, L = 16, 8, 8192, 128, 32
+    b0, b1 = rank * B // world, (rank + 1) * B // world
+    g = torch.Generator(device=dev).manual_seed(0)
+    kv = []
+    for _ in range(L):
+        for _kvi in range(2):
+            scale = torch.exp(torch.randn(1, H, 1, D, generator=g, device=dev))
+            x = (torch.randn(B, H, T, D, generator=g, device=dev) * scale).to(torch.bfloat16)
+            kv.append(x[b0:b1].contiguous().reshape(-1))
+            del x
+    ce = a.chunk_elems or gpu.DEFAULT_CHUNK_ELEMS
+    n = kv[0].numel()
+    enc = gpu.XcEncoder(n, ce, a.coder, gpu.DEFAULT_PREC, device=local)
+    bound = gpu.encode_bound(n, ce)
+    outs = [torch.empty(bound, dtype=torch.uint8, device=dev) for _ in kv]
+    lens = torch.zeros(len(kv), 2, dtype=torch.int64, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def encode_all():
+        for i, x in enumerate(kv):
+            enc.encode_into(x, outs[i], lens[i], stream)
+
+    enc_ms = _timed(torch, encode_all, a.steps, a.warmup, stream)
+    ln = lens[:, 0].tolist()
+    blobs = [o[:int(l)] for o, l in zip(outs, ln)]
+    dec = [torch.empty_like(x) for x in kv]
+    plan = gpu.XcPlan([(bl, d.view(torch.int16), ce) for bl, d in zip(blobs, dec)], device=local)
+    dec_ms = _timed(torch, lambda: plan.decode(stream), a.steps, a.warmup, stream)
+    plan.check(stream)
+    ok = all(torch.equal(x.view(torch.int16), d.view(torch.int16)) for x, d in zip(kv, dec))
+    raw = sum(2 * x.numel() for x in kv)
+    comp = sum(int(l) for l in ln)
+
+    def agg(v, op):
+        if not dist:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=op)
+        return float(t.item())
+
+    enc_ms_max = agg(enc_ms, dist.ReduceOp.MAX if dist else None)
+    dec_ms_max = agg(dec_ms, dist.ReduceOp.MAX if dist else None)
+    raw_all = agg(raw, dist.ReduceOp.SUM if dist else None)
+    comp_all = agg(comp, dist.ReduceOp.SUM if dist else None)
+    bad = agg(0 if ok else 1, dist.ReduceOp.SUM if dist else None)
+    if rank == 0:
+        print(json.dumps({
+            "metric": "KV cache GPU decode GB/s (BASELINE config 5), whole job", "unit": "GB/s",
+            "value": round(raw_all / (dec_ms_max * 1e-3) / 1e9, 2),
+            "encode_GBs": round(raw_all / (enc_ms_max * 1e-3) / 1e9, 2),
+            "ratio": round(comp_all / raw_all, 5), "n_gpus": world, "steps": a.steps, "warmup": a.warmup,
+            "decode_ms_per_step": round(dec_ms_max, 3), "encode_ms_per_step": round(enc_ms_max, 3),
+            "higher_is_better": True, "scaling": "strong", "dtype": "u16", "data": "synthetic",
+            "config": {"workload": "32 layers x {K,V} [16,8,8192,128] bf16, N(0,1) x log-normal per-channel "
+                                   "scale, seed 0; batch sharded across ranks", "chunk_elems": ce, "coder": a.coder},
+            "verified": "bitwise equal" if bad == 0 else f"MISMATCH on {int(bad)} ranks"}), flush=True)
+    plan.close()
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+# ---------------------------------------------------------------------------
+# config 3: codec sweep
+# ---------------------------------------------------------------------------
+def bench_sweep(a, torch, dev, world, rank, dist, local):
+    """2^30 Laplace(0, b) values, b in {0.005, 0.02, 0.1}; rANS vs tANS; chunks
+    of 64 KiB / 256 KiB / 1 MiB / 4 MiB of bf16.  One JSON line per case."""
+    from bigsmall_b200 import gpu
+    n = int(os.environ.get("BS_SWEEP_N", str(1 << 30)))
+    peak, peak_kind = measured_peak()
+    stream = torch.cuda.current_stream(dev)
+    for bscale in (0.005, 0.02, 0.1):
+        g = torch.Generator(device=dev).manual_seed(0)
+        u = torch.rand(n, generator=g, device=dev) - 0.5
+        x = (-bscale * torch.sign(u) * torch.log1p(-2 * u.abs())).to(torch.bfloat16)
+        del u
+        hist = torch.bincount(((x.view(torch.int16).to(torch.int32) >> 7) & 0xFF), minlength=256).double()
+        pr = hist[hist > 0] / n
+        h_exp = float(-(pr * pr.log2()).sum())
+        for coder in ("rans", "tans"):
+            for cbytes in (64 << 10, 256 << 10, 1 << 20, 4 << 20):
+                ce = cbytes // 2
+                blob = gpu.encode_xc(x, coder=coder, chunk_elems=ce)
+                out = torch.empty_like(x)
+                plan = gpu.XcPlan([(blob, out.view(torch.int16), ce)], device=local)
+                ms = _timed(torch, lambda: plan.decode(stream), a.steps, a.warmup, stream)
+                plan.check(stream)
+                ok = torch.equal(out.view(torch.int16), x.view(torch.int16))
+                algo = blob.numel() + 2 * n
+                print(json.dumps({"config": "BASELINE config 3 sweep", "laplace_b": bscale, "H_exp_bits": round(h_exp, 3),
+                                  "coder": coder, "chunk_bytes": cbytes, "values": n,
+                                  "ratio": round(blob.numel() / (2 * n), 5), "decode_ms": round(ms, 4),
+                                  "decoded_GBs": round(2 * n / ms / 1e6, 1),
+                                  "hbm_frac": round(algo / ms / 1e6 / peak, 4), "peak": f"{peak} ({peak_kind})",
+                                  "verified": ok}), flush=True)
+                plan.close()
+                del blob, out
+        del x
+        torch.cuda.empty_cache()
 
 if __name__ == "__main__":
     main()

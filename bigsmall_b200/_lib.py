@@ -62,7 +62,7 @@ SIGNATURES = {
     "bs_xc_decode_noalloc": (_I, [ctypes.POINTER(XcTensor), _I, _P, ctypes.POINTER(_U32)]),
     "bs_par_plan_create": (_I, [_P, _U64, _U64, _P, _P, _I, ctypes.POINTER(_P)]),
     "bs_xc_encode_bound": (_I, [_U64, _U32, ctypes.POINTER(_U64)]),
-    "bs_xc_encode_workspace": (_I, [_U64, _U32, ctypes.POINTER(_U64)]),
+    "bs_xc_encode_workspace": (_I, [_U64, _U32, _I, ctypes.POINTER(_U64)]),
     "bs_xc_encode": (_I, [_P, _U64, _I, _I, _U32, _P, _U64, _P, _P, _U64, _P]),
 }
 

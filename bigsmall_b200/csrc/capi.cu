@@ -625,9 +625,10 @@ int bs_xc_encode_bound(uint64_t n, uint32_t ce, uint64_t *bytes) {
     return BS_OK;
 }
 
-int bs_xc_encode_workspace(uint64_t n, uint32_t ce, uint64_t *bytes) {
-    if (!bytes || ce < 256 || (ce & 255)) return fail(BS_E_INVALID_ARG, "bad encode_workspace arguments");
-    *bytes = n ? xc_encode_workspace(n, ce) : 0;
+int bs_xc_encode_workspace(uint64_t n, uint32_t ce, int coder, uint64_t *bytes) {
+    if (!bytes || ce < 256 || (ce & 255) || (coder != BS_CODER_RANS && coder != BS_CODER_TANS))
+        return fail(BS_E_INVALID_ARG, "bad encode_workspace arguments");
+    *bytes = n ? xc_encode_workspace(n, ce, coder) : 0;
     return BS_OK;
 }
 
@@ -636,7 +637,7 @@ int bs_xc_encode(const void *d_in, uint64_t n, int coder, int prec, uint32_t ce,
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     if (ce < 256 || (ce & 255)) return fail(BS_E_INVALID_ARG, "chunk_elems must be a positive multiple of 256");
     if (prec < 8 || prec > 12) return fail(BS_E_INVALID_ARG, "precision must be in [8, 12]");
-    if (coder != BS_CODER_RANS) return fail(BS_E_UNSUPPORTED, "the device encoder supports the rANS coder only");
+    if (coder != BS_CODER_RANS && coder != BS_CODER_TANS) return fail(BS_E_INVALID_ARG, "coder must be 0 (rANS) or 1 (tANS)");
     if (!d_out_len) return fail(BS_E_INVALID_ARG, "d_out_len is NULL");
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) return fail(BS_E_CUDA, "no current device");
@@ -653,7 +654,7 @@ int bs_xc_encode(const void *d_in, uint64_t n, int coder, int prec, uint32_t ce,
         return fail(BS_E_INVALID_ARG, "pointers must be device memory of the current device");
     if ((n + ce - 1) / ce > 0x7FFFFFFFull) return fail(BS_E_INVALID_ARG, "too many chunks");
     if (out_cap < xc_encode_bound(n, ce)) return fail(BS_E_INVALID_ARG, "out_cap below bs_xc_encode_bound");
-    if (ws_bytes < xc_encode_workspace(n, ce)) return fail(BS_E_INVALID_ARG, "workspace below bs_xc_encode_workspace");
+    if (ws_bytes < xc_encode_workspace(n, ce, coder)) return fail(BS_E_INVALID_ARG, "workspace below bs_xc_encode_workspace");
     cudaError_t e = launch_xc_encode(static_cast<const uint16_t *>(d_in), n, coder, prec, ce,
                                      static_cast<uint8_t *>(d_out), out_cap, d_out_len,
                                      static_cast<uint8_t *>(d_ws), ws_bytes, s);

@@ -98,6 +98,6 @@ cudaError_t launch_xc_encode(const uint16_t *d_in, uint64_t n, int coder, int pr
                              uint32_t chunk_elems, uint8_t *d_out, uint64_t out_cap,
                              uint64_t *d_out_len, uint8_t *d_ws, uint64_t ws_bytes,
                              cudaStream_t s);
-uint64_t xc_encode_workspace(uint64_t n, uint32_t chunk_elems);
+uint64_t xc_encode_workspace(uint64_t n, uint32_t chunk_elems, int coder);
 uint64_t xc_encode_bound(uint64_t n, uint32_t chunk_elems);
 }  // namespace bsg

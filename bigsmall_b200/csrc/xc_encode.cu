@@ -13,6 +13,8 @@
 //                            run backwards over the chunk; renorm words are
 //                            written from the end of a per-chunk scratch slot
 //                            downwards so they land in decode order.
+//      xc_enc_chunks_tans_kernel  the tANS coder: a backward pass per lane, then
+//                            a forward replay of the decoder's refills.
 //   4. xc_enc_scan_kernel    exclusive scan of record sizes -> chunk table and
 //                            blob length.
 //   5. xc_enc_compact_kernel copy every record from its scratch slot into the
@@ -33,12 +35,17 @@ constexpr uint64_t kWsRec = 4096;       // u32[n_chunks]: words per record
 
 inline uint64_t rup(uint64_t x, uint64_t a) { return (x + a - 1) / a * a; }
 inline uint64_t slot_bytes(uint32_t ce) { return rup(128 + 2ull * ce, 16); }
-inline uint64_t slots_off(uint64_t nc) { return rup(kWsRec + 4 * nc, 256); }
+inline uint64_t slotlist_off(uint64_t nc) { return rup(kWsRec + 4 * nc, 256); }   // u16[4096] (tANS)
+inline uint64_t slots_off(uint64_t nc) { return slotlist_off(nc) + 2 * kXcMaxTable; }
+// tANS: one u32 (bits | nbits << 16) per lane and step, rup(chunk, 256) per chunk
+inline uint64_t tans_scratch_off(uint64_t nc, uint32_t ce) { return slots_off(nc) + nc * slot_bytes(ce); }
 }  // namespace
 
-uint64_t xc_encode_workspace(uint64_t n, uint32_t ce) {
+uint64_t xc_encode_workspace(uint64_t n, uint32_t ce, int coder) {
     uint64_t nc = (n + ce - 1) / ce;
-    return slots_off(nc) + nc * slot_bytes(ce);
+    uint64_t b = slots_off(nc) + nc * slot_bytes(ce);
+    if (coder == BS_CODER_TANS) b += nc * 4ull * rup(ce, 256);
+    return b;
 }
 
 uint64_t xc_encode_bound(uint64_t n, uint32_t ce) {
@@ -98,9 +105,11 @@ __global__ void __launch_bounds__(256) xc_enc_hist_kernel(const uint16_t *__rest
 // never below 1; a single present symbol gets M-1 plus a phantom neighbour.
 __global__ void __launch_bounds__(256) xc_enc_setup_kernel(const unsigned long long *counts, uint64_t n,
                                                            int coder, int prec, uint32_t ce, uint32_t nc,
-                                                           uint8_t *out, uint32_t *enc_tab) {
+                                                           uint8_t *out, uint32_t *enc_tab, uint16_t *slot_list) {
     __shared__ int64_t f[256];
     __shared__ uint32_t s_cum[256];
+    __shared__ uint8_t s_spread[kXcMaxTable];
+    __shared__ uint32_t s_occ[256];
     const int tid = threadIdx.x;
     const int64_t M = 1ll << prec;
     if (tid == 0) {
@@ -164,6 +173,34 @@ __global__ void __launch_bounds__(256) xc_enc_setup_kernel(const unsigned long l
     if (tab_end + tid < plane_off) out[tab_end + tid] = 0;
     if (plane_off + n + tid < chunks_off) out[plane_off + n + tid] = 0;
     enc_tab[tid] = static_cast<uint32_t>(f[tid]) | (s_cum[tid] << 16);
+    if (coder != BS_CODER_TANS) return;
+    // tANS: spread the symbols over the 2^P states with Collet's step (the k-th
+    // placement in symbol order lands on (k * step) mod M), then list each
+    // symbol's states in increasing order (the encoder's next-state table)
+    const uint32_t Mu = static_cast<uint32_t>(M), step = (Mu >> 1) + (Mu >> 3) + 3;
+    for (uint32_t k = tid; k < Mu; k += blockDim.x) {
+        int lo = 0, hi = 255;   // largest symbol with cum <= k (it has f > 0)
+        while (lo < hi) {
+            const int mid = (lo + hi + 1) >> 1;
+            if (s_cum[mid] <= k) lo = mid; else hi = mid - 1;
+        }
+        s_spread[(k * step) & (Mu - 1)] = static_cast<uint8_t>(lo);
+    }
+    s_occ[tid] = 0;
+    __syncthreads();
+    if (tid < 32) {
+        uint32_t lt;
+        asm("mov.u32 %0, %%lanemask_lt;" : "=r"(lt));
+        for (uint32_t i0 = 0; i0 < Mu; i0 += 32) {
+            const uint32_t i = i0 + tid;
+            const uint32_t sym = s_spread[i];
+            const uint32_t grp = __match_any_sync(0xFFFFFFFFu, sym);
+            slot_list[s_cum[sym] + s_occ[sym] + __popc(grp & lt)] = static_cast<uint16_t>(i);
+            __syncwarp();
+            if ((grp & lt) == 0) s_occ[sym] += __popc(grp);
+            __syncwarp();
+        }
+    }
 }
 
 // 3. per-chunk reverse rANS ---------------------------------------------------
@@ -231,6 +268,101 @@ __global__ void __launch_bounds__(kEncWarps * 32) xc_enc_chunks_kernel(
     if (lane == 0) rec_words[c] = cur;
 }
 
+// 3b. per-chunk tANS ------------------------------------------------------------
+// Phase 1 runs each lane's tANS state backwards over its symbols and records
+// (bits, nbits) per step; phase 2 replays the decoder forwards: before a step,
+// lanes holding fewer than P bits take their next 16-bit word of their own
+// LSB-first bit string, in lane order, into the shared word stream.
+__global__ void __launch_bounds__(kEncWarps * 32) xc_enc_chunks_tans_kernel(
+    const uint16_t *__restrict__ in, uint64_t n, uint32_t ce, uint32_t nc, int prec,
+    const uint32_t *__restrict__ enc_tab, const uint16_t *__restrict__ slot_list, uint8_t *__restrict__ slots,
+    uint64_t slot_b, uint32_t *__restrict__ scratch, uint32_t *__restrict__ rec_words) {
+    __shared__ uint32_t s_tab[256];
+    __shared__ uint16_t s_sl[kXcMaxTable];
+    const uint32_t M = 1u << prec;
+    s_tab[threadIdx.x] = enc_tab[threadIdx.x];
+    for (uint32_t i = threadIdx.x; i < M; i += blockDim.x) s_sl[i] = slot_list[i];
+    __syncthreads();
+    const uint32_t lane = threadIdx.x & 31;
+    const uint32_t c = blockIdx.x * kEncWarps + (threadIdx.x >> 5);
+    if (c >= nc) return;
+    const uint32_t P = static_cast<uint32_t>(prec);
+    const uint64_t e0 = static_cast<uint64_t>(c) * ce;
+    const uint32_t cn = (n - e0) < ce ? static_cast<uint32_t>(n - e0) : ce;
+    const uint16_t *src = in + e0;
+    uint8_t *slot = slots + static_cast<uint64_t>(c) * slot_b;
+    uint32_t *sc = scratch + static_cast<uint64_t>(c) * ((ce + 255) & ~255u);
+    const uint32_t G = cn >> 8, rem = cn & 255;
+    const uint32_t S = (G + (rem ? 1u : 0u)) * 8;
+
+    uint32_t X = M;
+    auto enc1 = [&](uint32_t s, uint32_t v, bool active) {
+        uint32_t r = 0;
+        if (active) {
+            const uint32_t t = s_tab[(v >> 7) & 0xFF];
+            const uint32_t f = t & 0xFFFF, cf = t >> 16;
+            int nb = (31 - __clz(X)) - (31 - __clz(f));
+            if ((X >> nb) < f) nb--;
+            const uint32_t bits = X & ((1u << nb) - 1);
+            X = M + s_sl[cf + (X >> nb) - f];
+            r = bits | (static_cast<uint32_t>(nb) << 16);
+        }
+        sc[s * 32 + lane] = r;
+    };
+    if (rem) {
+        const uint32_t eb = G * 256 + lane * 8;
+        for (int j = 7; j >= 0; j--) {
+            const bool act = lane * 8 + j < rem;
+            enc1(G * 8 + j, act ? src[eb + j] : 0u, act);
+        }
+    }
+    for (int g = static_cast<int>(G) - 1; g >= 0; g--) {
+        const uint4 v = reinterpret_cast<const uint4 *>(src + g * 256 + lane * 8)[0];
+        enc1(g * 8 + 7, v.w >> 16, true);
+        enc1(g * 8 + 6, v.w & 0xFFFF, true);
+        enc1(g * 8 + 5, v.z >> 16, true);
+        enc1(g * 8 + 4, v.z & 0xFFFF, true);
+        enc1(g * 8 + 3, v.y >> 16, true);
+        enc1(g * 8 + 2, v.y & 0xFFFF, true);
+        enc1(g * 8 + 1, v.x >> 16, true);
+        enc1(g * 8 + 0, v.x & 0xFFFF, true);
+    }
+    // phase 2
+    uint64_t acc = 0;
+    uint32_t accn = 0, p = 0;
+    auto pull16 = [&]() -> uint32_t {
+        while (accn < 16 && p < S) {
+            const uint32_t r = sc[p * 32 + lane];
+            acc |= static_cast<uint64_t>(r & 0xFFFF) << accn;
+            accn += r >> 16;
+            p++;
+        }
+        const uint32_t w = static_cast<uint32_t>(acc & 0xFFFF);
+        acc >>= 16;
+        accn = accn > 16 ? accn - 16 : 0;
+        return w;
+    };
+    const uint32_t first = pull16();
+    const uint32_t init = (X - M) | (first << 16);
+    uint16_t *wout = reinterpret_cast<uint16_t *>(slot + 128);
+    uint32_t lt;
+    asm("mov.u32 %0, %%lanemask_lt;" : "=r"(lt));
+    uint32_t cnt = 16, base = 0;
+    for (uint32_t s = 0; s < S; s++) {
+        const bool active = (s >> 3) < G || (lane * 8 + (s & 7)) < rem;
+        const bool need = active && cnt < P;
+        const uint32_t m = __ballot_sync(kFull, need);
+        if (need) {
+            wout[base + __popc(m & lt)] = static_cast<uint16_t>(pull16());
+            cnt += 16;
+        }
+        base += __popc(m);
+        if (active) cnt -= sc[s * 32 + lane] >> 16;
+    }
+    reinterpret_cast<uint32_t *>(slot)[lane] = init;
+    if (lane == 0) rec_words[c] = base;
+}
+
 // 4. record offsets -----------------------------------------------------------
 __global__ void __launch_bounds__(1024) xc_enc_scan_kernel(const uint32_t *__restrict__ rec_words, uint32_t nc,
                                                            uint8_t *out, uint64_t chunks_off, uint64_t out_cap,
@@ -274,7 +406,7 @@ __global__ void __launch_bounds__(1024) xc_enc_scan_kernel(const uint32_t *__res
 __global__ void __launch_bounds__(256) xc_enc_compact_kernel(const uint8_t *__restrict__ slots, uint64_t slot_b,
                                                              const uint32_t *__restrict__ rec_words,
                                                              uint8_t *out, uint64_t chunks_off,
-                                                             const uint32_t *flags) {
+                                                             const uint32_t *flags, int coder) {
     if (*flags) return;
     const uint32_t c = blockIdx.x;
     const uint32_t W = rec_words[c];
@@ -283,7 +415,10 @@ __global__ void __launch_bounds__(256) xc_enc_compact_kernel(const uint8_t *__re
     const uint8_t *slot = slots + static_cast<uint64_t>(c) * slot_b;
     if (threadIdx.x < 32)
         reinterpret_cast<uint32_t *>(dst)[threadIdx.x] = reinterpret_cast<const uint32_t *>(slot)[threadIdx.x];
-    const uint16_t *ws = reinterpret_cast<const uint16_t *>(slot + slot_b) - W;
+    // rANS records hold their words at the end of the slot (written backwards),
+    // tANS records right after the lane states (written forwards)
+    const uint16_t *ws = coder == BS_CODER_TANS ? reinterpret_cast<const uint16_t *>(slot + 128)
+                                                : reinterpret_cast<const uint16_t *>(slot + slot_b) - W;
     uint16_t *wd = reinterpret_cast<uint16_t *>(dst + 128);
     const uint32_t padded = ((128u + 2u * W + 15u) & ~15u) - 128u;   // bytes incl. zero pad
     for (uint32_t i = threadIdx.x; i < padded / 2; i += blockDim.x) wd[i] = i < W ? ws[i] : 0;
@@ -309,12 +444,22 @@ cudaError_t launch_xc_encode(const uint16_t *d_in, uint64_t n, int coder, int pr
     uint64_t want = (n / 8 + 255) / 256;
     int grid = static_cast<int>(want < static_cast<uint64_t>(sms) * 8 ? (want ? want : 1) : static_cast<uint64_t>(sms) * 8);
     xc_enc_hist_kernel<<<grid, 256, 0, s>>>(d_in, n, counts, d_out + plane_off);
-    xc_enc_setup_kernel<<<1, 256, 0, s>>>(counts, n, coder, prec, ce, static_cast<uint32_t>(nc), d_out, tab);
-    xc_enc_chunks_kernel<<<static_cast<unsigned>((nc + kEncWarps - 1) / kEncWarps), kEncWarps * 32, 0, s>>>(
-        d_in, n, ce, static_cast<uint32_t>(nc), prec, tab, slots, sb, recw);
+    uint16_t *slot_list = reinterpret_cast<uint16_t *>(d_ws + slotlist_off(nc));
+    xc_enc_setup_kernel<<<1, 256, 0, s>>>(counts, n, coder, prec, ce, static_cast<uint32_t>(nc), d_out, tab,
+                                          slot_list);
+    const unsigned enc_blocks = static_cast<unsigned>((nc + kEncWarps - 1) / kEncWarps);
+    if (coder == BS_CODER_TANS) {
+        auto *scr = reinterpret_cast<uint32_t *>(d_ws + tans_scratch_off(nc, ce));
+        xc_enc_chunks_tans_kernel<<<enc_blocks, kEncWarps * 32, 0, s>>>(d_in, n, ce, static_cast<uint32_t>(nc), prec,
+                                                                       tab, slot_list, slots, sb, scr, recw);
+    } else {
+        xc_enc_chunks_kernel<<<enc_blocks, kEncWarps * 32, 0, s>>>(d_in, n, ce, static_cast<uint32_t>(nc), prec,
+                                                                  tab, slots, sb, recw);
+    }
     xc_enc_scan_kernel<<<1, 1024, 0, s>>>(recw, static_cast<uint32_t>(nc), d_out, chunks_off, out_cap,
                                           reinterpret_cast<unsigned long long *>(d_out_len), flags);
-    xc_enc_compact_kernel<<<static_cast<unsigned>(nc), 256, 0, s>>>(slots, sb, recw, d_out, chunks_off, flags);
+    xc_enc_compact_kernel<<<static_cast<unsigned>(nc), 256, 0, s>>>(slots, sb, recw, d_out, chunks_off, flags,
+                                                                    coder);
     (void)ws_bytes;
     return cudaGetLastError();
 }

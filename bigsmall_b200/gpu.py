@@ -190,9 +190,10 @@ def encode_bound(n: int, chunk_elems: int = DEFAULT_CHUNK_ELEMS) -> int:
     return int(v.value)
 
 
-def encode_workspace(n: int, chunk_elems: int = DEFAULT_CHUNK_ELEMS) -> int:
+def encode_workspace(n: int, chunk_elems: int = DEFAULT_CHUNK_ELEMS, coder: str = "rans") -> int:
     v = ctypes.c_uint64()
-    _lib.check(_lib.load().bs_xc_encode_workspace(n, chunk_elems, ctypes.byref(v)), "bs_xc_encode_workspace")
+    c = CODERS[coder] if isinstance(coder, str) else int(coder)
+    _lib.check(_lib.load().bs_xc_encode_workspace(n, chunk_elems, c, ctypes.byref(v)), "bs_xc_encode_workspace")
     return int(v.value)
 
 
@@ -209,7 +210,8 @@ class XcEncoder:
         dev = torch.device("cuda", device if device is not None else torch.cuda.current_device())
         self.device = dev
         self.out = torch.empty(max(16, encode_bound(max_elems, chunk_elems)), dtype=torch.uint8, device=dev)
-        self.ws = torch.empty(max(16, encode_workspace(max_elems, chunk_elems)), dtype=torch.uint8, device=dev)
+        self.ws = torch.empty(max(16, encode_workspace(max_elems, chunk_elems, self.coder)), dtype=torch.uint8,
+                              device=dev)
         self.out_len = torch.zeros(2, dtype=torch.int64, device=dev)
 
     def encode_async(self, x: torch.Tensor, stream=None) -> None:
@@ -224,6 +226,21 @@ class XcEncoder:
         rc = L.bs_xc_encode(x.data_ptr() if n else None, n, self.coder, self.prec, self.chunk_elems,
                             self.out.data_ptr(), self.out.numel(), self.out_len.data_ptr(),
                             self.ws.data_ptr(), self.ws.numel(), _stream_ptr(stream, self.device))
+        _lib.check(rc, "bs_xc_encode")
+
+    def encode_into(self, x: torch.Tensor, out: torch.Tensor, out_len: torch.Tensor, stream=None) -> None:
+        """Enqueue the encode of ``x`` into ``out`` (uint8, >= encode_bound bytes);
+        the blob length lands in ``out_len[0]`` (int64 device tensor).  Uses this
+        encoder's workspace, so calls on one stream must not overlap others."""
+        _as_cuda(x, "x")
+        _as_cuda(out, "out")
+        n = x.numel()
+        if n > self.max_elems:
+            raise ValueError(f"tensor of {n} values exceeds encoder capacity {self.max_elems}")
+        L = _lib.load()
+        rc = L.bs_xc_encode(x.data_ptr() if n else None, n, self.coder, self.prec, self.chunk_elems,
+                            out.data_ptr(), out.numel(), out_len.data_ptr(), self.ws.data_ptr(), self.ws.numel(),
+                            _stream_ptr(stream, self.device))
         _lib.check(rc, "bs_xc_encode")
 
     def encode(self, x: torch.Tensor, stream=None) -> torch.Tensor:

@@ -55,6 +55,8 @@ class ContainerImage:
             host = data.reshape(-1).view(torch.uint8)
         else:
             arr = np.frombuffer(data, dtype=np.uint8) if not isinstance(data, np.ndarray) else data.reshape(-1).view(np.uint8)
+            if not arr.flags.writeable:
+                arr = arr.copy()
             host = torch.from_numpy(arr)
         if pin and not host.is_pinned():
             pinned = torch.empty(host.numel(), dtype=torch.uint8, pin_memory=True)

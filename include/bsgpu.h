@@ -129,9 +129,9 @@ int bs_par_plan_create(const uint8_t *h_blob, uint64_t blob_bytes,
                        int device, bs_plan **out_plan);
 
 /* ---- bf16_exp_chunked_v1 encode (KV-cache compression) ------------------ */
-/* Worst-case blob size and scratch size for one tensor. */
+/* Worst-case blob size, and scratch size for one tensor with a given coder. */
 int bs_xc_encode_bound(uint64_t n_elems, uint32_t chunk_elems, uint64_t *bytes);
-int bs_xc_encode_workspace(uint64_t n_elems, uint32_t chunk_elems, uint64_t *bytes);
+int bs_xc_encode_workspace(uint64_t n_elems, uint32_t chunk_elems, int coder, uint64_t *bytes);
 
 /* Encode n_elems bf16 values at d_in into a bf16_exp_chunked_v1 blob at d_out
  * (capacity out_cap >= bs_xc_encode_bound).  The exact blob length is written

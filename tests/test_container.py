@@ -1,0 +1,78 @@
+"""Container format (BigSmall bigsmall/container.py layout) and partitioning, CPU only."""
+from __future__ import annotations
+
+import json
+import math
+import struct
+
+import pytest
+
+from bigsmall_b200 import container as C
+from bigsmall_b200.exceptions import BigSmallVersionError
+
+
+def test_writer_roundtrip_and_alignment(tmp_path):
+    w = C.ContainerWriter()
+    w.add("a", [3], "BF16", "raw", b"\x01\x02" * 3, "m1")
+    w.add("b", [5], "BF16", "bf16_exp_chunked_v1", b"x" * 37, "m2", {"chunk_elems": 256})
+    w.add("c", [5], "BF16", "tied_ref", b"", "m2", {"tied_to": "b"})
+    w.add("d", [2, 2], "F32", "raw", b"\0" * 16, "m3")
+    buf = w.to_bytes()
+    header, off = C.parse_header(buf)
+    assert buf[:4] == b"BGSM" and struct.unpack_from("<H", buf, 4)[0] == 2   # v2: new codec present
+    assert header["tensor_count"] == 4 and header["_format_version"] == 2
+    for t in header["tensors"]:
+        if t["codec"] != "tied_ref":
+            assert t["offset"] % 16 == 0
+    data = memoryview(buf)[off:]
+    blobs = {t["name"]: bytes(b) for t, b in C.iter_blobs(header, data)}
+    assert blobs["a"] == b"\x01\x02" * 3 and blobs["b"] == b"x" * 37 and blobs["d"] == b"\0" * 16
+    p = tmp_path / "m.bs"
+    w.write(p)
+    h2, off2 = C.read_header(p)
+    assert h2["tensors"] == header["tensors"] and off2 == off
+    assert C.read_blob(p, h2, off2, 1) == b"x" * 37
+    info = C.info(p)
+    assert info["tensor_count"] == 4 and info["codec_stats"]["raw"] == 2
+
+
+def test_version_and_magic_errors(tmp_path):
+    hb = json.dumps({"tensors": [], "tensor_count": 0}).encode()
+    bad = b"BGSM" + struct.pack("<H", 9) + struct.pack("<I", len(hb)) + hb
+    with pytest.raises(BigSmallVersionError):
+        C.parse_header(bad)
+    with pytest.raises(ValueError):
+        C.parse_header(b"NOPE" + bad[4:])
+    C.write_container(tmp_path / "v1.bs", {"tensors": [], "tensor_count": 0}, b"")
+    assert C.read_header(tmp_path / "v1.bs")[0]["_format_version"] == 1
+
+
+def test_v1_files_read():
+    """A reference-written (v1, unaligned offsets) container parses identically."""
+    hdr = {"format": "bf16", "tensor_count": 1,
+           "tensors": [{"name": "w", "shape": [2], "dtype": "BF16", "codec": "raw", "special": None,
+                        "compressed_bytes": 4, "offset": 0, "md5": "", "extra": None}]}
+    hb = json.dumps(hdr, separators=(",", ":")).encode()
+    buf = b"BGSM" + struct.pack("<H", 1) + struct.pack("<I", len(hb)) + hb + b"\x01\x02\x03\x04"
+    h, off = C.parse_header(buf)
+    assert h["tensors"][0]["name"] == "w" and buf[off:] == b"\x01\x02\x03\x04"
+
+
+@pytest.mark.parametrize("world", [1, 2, 3, 4, 8])
+def test_bench_partition_covers_container_once(world):
+    import bench
+    tensors = bench.llama3_8b_tensors()
+    owned, load = bench.partition(tensors, world, 65536)
+    assert max(load) - min(load) <= 65536
+    seen = {}
+    for r in owned:
+        assert len({n for n, _, _ in r}) == len(r)
+        for name, c0, cc in r:
+            seen.setdefault(name, []).append((c0, cc))
+    for name, shape, _ in tensors:
+        nc = -(-math.prod(shape) // 65536)
+        pos = 0
+        for c0, cc in sorted(seen[name]):
+            assert c0 == pos
+            pos = c0 + (cc or nc)
+        assert pos == nc

@@ -1,0 +1,95 @@
+"""Reference-shaped API on the device: container -> HBM, _decode_blob, the
+ac_cuda backend slot and the codec registry (BigSmall bigsmall/decoder.py,
+bigsmall/kernels/__init__.py, bigsmall/codec_registry.py contracts)."""
+from __future__ import annotations
+
+import hashlib
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+from oracle import oracle as O  # noqa: E402
+from tests.conftest import golden_bytes  # noqa: E402
+
+
+def _model(seed=0):
+    g = torch.Generator().manual_seed(seed)
+    return {
+        "model.embed_tokens.weight": (torch.randn(1000, 64, generator=g) * 0.02).to(torch.bfloat16),
+        "model.layers.0.input_layernorm.weight": (1 + torch.randn(64, generator=g) * 0.01).to(torch.bfloat16),
+        "model.layers.0.self_attn.q_proj.weight": (torch.randn(64, 64, generator=g) / 8).to(torch.bfloat16),
+        "model.layers.1.mlp.up_proj.weight": (torch.randn(300, 64, generator=g) / 8).to(torch.bfloat16),
+        "model.layers.1.tiny.bias": (torch.randn(7, generator=g)).to(torch.bfloat16),
+        "model.positions": torch.arange(10, dtype=torch.int64),
+    }
+
+
+def test_compress_load_decompress_verify(tmp_path):
+    from bigsmall_b200 import decoder
+    sd = _model()
+    p = tmp_path / "m.bs"
+    decoder.compress_tensors(sd, p, chunk_elems=4096)
+    out = decoder.load(p, device="cuda")
+    for k, v in sd.items():
+        assert out[k].dtype == v.dtype and tuple(out[k].shape) == tuple(v.shape)
+        assert torch.equal(out[k].cpu().view(torch.uint8), v.view(torch.uint8)), k
+    host = decoder.decompress(p)
+    for k, v in sd.items():
+        assert host[k].tobytes() == v.view(torch.uint8).numpy().tobytes()
+    assert decoder.verify(p)
+
+
+def test_loader_pipelined_groups_and_tied(tmp_path):
+    from bigsmall_b200 import container as C, gpu
+    from bigsmall_b200.loader import ContainerImage, DeviceLoader
+    sd = _model(1)
+    w = C.ContainerWriter()
+    for k, v in sd.items():
+        if v.dtype == torch.bfloat16 and v.numel() >= 256:
+            blob = gpu.encode_xc(v.reshape(-1).cuda(), chunk_elems=256).cpu().numpy().tobytes()
+            w.add(k, v.shape, "BF16", "bf16_exp_chunked_v1", blob, "", gpu.xc_extras(256))
+        else:
+            raw = v.reshape(-1).view(torch.uint8).numpy().tobytes()
+            w.add(k, v.shape, {torch.bfloat16: "BF16", torch.int64: "I64"}[v.dtype], "raw", raw, "")
+    # a bf16_parallel_v1 tensor from the reference format and a tied alias
+    raw = golden_bytes("gauss_8k.raw")
+    w.add("ref.par", [8192], "BF16", "bf16_parallel_v1", O.par_encode(raw, 32), "", {"n_streams": 32})
+    w.add("lm_head.weight", [1000, 64], "BF16", "tied_ref", b"", "", {"tied_to": "model.embed_tokens.weight"})
+    img = ContainerImage.from_bytes(w.to_bytes())
+    ld = DeviceLoader(img, device=0, group_bytes=20_000)   # many small groups
+    assert len(ld.groups) > 3
+    for _ in range(2):
+        out = ld.run()
+    for k, v in sd.items():
+        assert torch.equal(out[k].cpu().view(torch.uint8), v.view(torch.uint8)), k
+    assert out["ref.par"].cpu().view(torch.uint8).numpy().tobytes() == raw
+    assert out["lm_head.weight"].data_ptr() == out["model.embed_tokens.weight"].data_ptr()
+    ld.close()
+
+
+def test_unknown_codec_raises_version_error():
+    from bigsmall_b200 import decoder
+    from bigsmall_b200.exceptions import BigSmallVersionError
+    with pytest.raises(BigSmallVersionError):
+        decoder._decode_blob({"codec": "bf16_se_rans", "shape": [4], "extra": None}, b"1234")
+    assert decoder._decode_blob({"codec": "raw", "shape": [2], "extra": None}, b"abcd") == b"abcd"
+    assert decoder._decode_blob({"codec": "tied_ref", "shape": [2], "extra": None}, b"") is None
+
+
+def test_ac_cuda_slot_and_registry(manifest):
+    from bigsmall_b200 import codec_registry, kernels
+    from bigsmall_b200.kernels import ac_cuda
+    assert kernels.use_gpu() and kernels.backend_name() == "cuda_c"
+    c = manifest["cases"]["edge"]
+    blob = golden_bytes(c["blobs"]["par128"]["file"])
+    out = ac_cuda.decode(blob, {"n_streams": 128}, c["n"])
+    assert hashlib.md5(out).hexdigest() == c["raw_md5"]
+    assert kernels.decode_bf16_parallel(blob, {}, c["n"]) == out
+    enc, dec = codec_registry.get_codec("bf16_exp_chunked_v1")
+    raw = golden_bytes("c1_head_16k.raw")
+    b, extras = enc(raw, chunk_elems=4096)
+    assert b == O.xc_encode(raw, 0, 12, 4096) and dec(b, extras, len(raw) // 2) == raw
+    assert "bf16_parallel_v1" in codec_registry.registered_names()

@@ -1,0 +1,88 @@
+"""Device KV-cache compression (reference tests/test_kv_cache.py:15-119 shapes
+and gates), plus the config-5 distribution: device encode == CPU oracle bytes,
+device decode bit-exact."""
+from __future__ import annotations
+
+import hashlib
+import struct
+
+import pytest
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+from oracle import oracle as O  # noqa: E402
+
+
+def _md5(t):
+    return hashlib.md5(t.contiguous().view(torch.uint8).cpu().numpy().tobytes()).hexdigest()
+
+
+def test_kv_roundtrip_lossless():
+    from bigsmall_b200.kv_cache import compress_kv_entry, decompress_kv_entry
+    torch.manual_seed(0)
+    k = torch.randn(1, 32, 64, 96).to(torch.bfloat16)
+    v = torch.randn(1, 32, 64, 96).to(torch.bfloat16)
+    k2, v2 = decompress_kv_entry(compress_kv_entry(k, v), device="cuda")
+    assert _md5(k) == _md5(k2) and _md5(v) == _md5(v2)
+    assert k2.shape == k.shape and k2.is_cuda
+
+
+def test_kv_ratio_below_75pct():
+    from bigsmall_b200.kv_cache import compress_kv_entry
+    torch.manual_seed(0)
+    k = (torch.randn(1, 32, 512, 96) * 0.5).to(torch.bfloat16)
+    v = (torch.randn(1, 32, 512, 96) * 0.5).to(torch.bfloat16)
+    raw = 2 * k.numel() * 2
+    assert len(compress_kv_entry(k, v)) / raw < 0.75
+
+
+def test_compressed_kv_cache_api():
+    from bigsmall_b200.kv_cache_manager import CompressedKVCache
+    torch.manual_seed(1)
+    c = CompressedKVCache(device="cuda")
+    assert len(c) == 0 and c.compression_ratio() is None
+    layers = {}
+    for i in range(3):
+        k = torch.randn(1, 8, 33 + i, 64, device="cuda").to(torch.bfloat16)
+        v = torch.randn(1, 8, 33 + i, 64, device="cuda").to(torch.bfloat16)
+        c.set(i, k, v)
+        layers[i] = (k, v)
+    k = torch.randn(1, 8, 40, 64, device="cuda").to(torch.bfloat16)
+    c.set(1, k, k)          # overwrite a layer
+    layers[1] = (k, k)
+    assert len(c) == 3 and c.has(2) and not c.has(5)
+    for i, (k, v) in layers.items():
+        k2, v2 = c.get(i)
+        assert torch.equal(k.view(torch.int16), k2.view(torch.int16))
+        assert torch.equal(v.view(torch.int16), v2.view(torch.int16))
+    assert 0 < c.compression_ratio() < 0.8
+    assert c.raw_size() == sum(2 * (a.numel() + b.numel()) for a, b in layers.values())
+    assert "CompressedKVCache(layers=3" in repr(c)
+    with pytest.raises(KeyError):
+        c.get(9)
+    with pytest.raises(ValueError):
+        c.set(0, k.float(), k)
+    c.clear()
+    assert len(c) == 0 and c.memory_usage() == 0
+
+
+def test_config5_distribution_device_encoder_matches_oracle():
+    from bigsmall_b200 import gpu
+    from bigsmall_b200.kv_cache import KVEncoder, decode_kv
+    g = torch.Generator().manual_seed(0)
+    scale = torch.exp(torch.randn(1, 8, 1, 128, generator=g))
+    k = (torch.randn(2, 8, 256, 128, generator=g) * scale).to(torch.bfloat16)
+    enc = KVEncoder(0)
+    kb = enc.encode(k.cuda())
+    raw = k.view(torch.uint8).numpy().tobytes()
+    assert kb.cpu().numpy().tobytes() == O.xc_encode(raw, 0, 12, gpu.DEFAULT_CHUNK_ELEMS)
+    k2, _ = decode_kv(kb, kb, k.shape, k.shape)
+    assert torch.equal(k2.cpu().view(torch.int16), k.view(torch.int16))
+
+
+def test_legacy_kv_versions_rejected_clearly():
+    from bigsmall_b200.kv_cache import decompress_kv_entry
+    blob = struct.pack("<BB", 2, 1) + struct.pack("<i", 4) + struct.pack("<I", 0)
+    with pytest.raises(ValueError, match="constriction"):
+        decompress_kv_entry(blob + blob[1:])

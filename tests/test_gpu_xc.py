@@ -68,8 +68,9 @@ def test_device_encoder_matches_oracle_bytes(manifest):
         x = torch.from_numpy(np.frombuffer(raw, dtype=np.int16).copy()).view(torch.bfloat16).cuda()
         for ce in (256, 65536):
             for prec in (11, 12):
-                d = gpu.encode_xc(x, prec=prec, chunk_elems=ce).cpu().numpy().tobytes()
-                assert d == O.xc_encode(raw, 0, prec, ce), (n, ce, prec)
+                for coder, cid in (("rans", 0), ("tans", 1)):
+                    d = gpu.encode_xc(x, coder=coder, prec=prec, chunk_elems=ce).cpu().numpy().tobytes()
+                    assert d == O.xc_encode(raw, cid, prec, ce), (n, ce, prec, coder)
 
 
 def test_full_size_config1_roundtrip_and_encoder_pin(manifest):
