@@ -226,7 +226,7 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=8.0)
-    ap.add_argument("--config", default="c2", choices=["c2", "small", "kv", "sweep"],
+    ap.add_argument("--config", default="c2", choices=["c2", "small", "kv", "sweep", "stream"],
                     help="c2: the benchmark workload; small: one 2^27-value tensor of the same "
                          "distribution (compressed ~170 MB, above L2) for ncu captures; kv: BASELINE "
                          "config 5 (KV cache encode+decode); sweep: config 3 (rANS vs tANS x chunk size)")
@@ -278,6 +278,8 @@ def main():
         return bench_kv(a, torch, dev, world, rank, dist, local)
     if a.config == "sweep":
         return bench_sweep(a, torch, dev, world, rank, dist, local)
+    if a.config == "stream":
+        return bench_stream(a, torch, dev, world, rank, dist, local)
     if a.config == "small":
         tensors = [("model.layers.0.mlp.small_proj.weight", (1 << 15, 4096), "linear")]
         config["workload"] = "one 2^27-value bf16 tensor, config-2 distribution (profiling case)"
@@ -573,6 +575,86 @@ def bench_sweep(a, torch, dev, world, rank, dist, local):
                 del blob, out
         del x
         torch.cuda.empty_cache()
+
+
+# ---------------------------------------------------------------------------
+# config 4: streaming layer-wise inference
+# ---------------------------------------------------------------------------
+def bench_stream(a, torch, dev, world, rank, dist, local):
+    """Qwen2.5-14B-shaped random-init bf16 model (48 layers, hidden 5120,
+    intermediate 13824, 40 Q / 8 KV heads x 128, vocab 152064), batch 1,
+    512 uniform-random prompt tokens then 128 greedy steps: resident model vs
+    BigSmallStreamingModel (compressed model resident in HBM, two decoded-layer
+    slots, decode of the next layer on a side stream)."""
+    from transformers import Qwen2Config
+    from bigsmall_b200 import gpu, synthetic
+    from bigsmall_b200.container import ContainerWriter
+    from bigsmall_b200.loader import ContainerImage
+    from bigsmall_b200.streaming import StreamingLoader
+    from bigsmall_b200.streaming_inference import BigSmallStreamingModel
+    torch.use_deterministic_algorithms(True, warn_only=True)
+    layers = int(os.environ.get("BS_STREAM_LAYERS", "48"))
+    steps = int(os.environ.get("BS_STREAM_STEPS", "128"))
+    cfg = Qwen2Config(vocab_size=152064, hidden_size=5120, intermediate_size=13824, num_hidden_layers=layers,
+                      num_attention_heads=40, num_key_value_heads=8, max_position_embeddings=32768,
+                      rope_theta=1000000.0, rms_norm_eps=1e-6, tie_word_embeddings=False)
+    t0 = time.time()
+    w = synthetic.random_weights(cfg, seed=0, device=dev)
+    ce = a.chunk_elems or gpu.DEFAULT_CHUNK_ELEMS
+    enc = gpu.XcEncoder(max(t.numel() for t in w.values()), ce, a.coder, gpu.DEFAULT_PREC, device=local)
+    wr = ContainerWriter()
+    for n, t in w.items():
+        wr.add(n, t.shape, "BF16", "bf16_exp_chunked_v1", enc.encode(t.reshape(-1)).cpu().numpy().tobytes(), "",
+               gpu.xc_extras(ce, a.coder, gpu.DEFAULT_PREC))
+    del enc
+    image = ContainerImage.from_bytes(wr.to_bytes())
+    del wr
+    raw_bytes = sum(2 * t.numel() for t in w.values())
+    comp_bytes = image.compressed_bytes()
+    setup_s = time.time() - t0
+    g = torch.Generator(device=dev).manual_seed(0)
+    prompt = torch.randint(0, cfg.vocab_size, (1, 512), generator=g, device=dev)
+
+    ref = synthetic.resident_model(cfg, w, device=dev)
+    for _ in range(2):                                         # warm-up: same shapes as the timed run
+        synthetic.greedy(ref, prompt, 4)
+    ids_r, lg_r, pre_r, dec_r = synthetic.greedy(ref, prompt, steps)
+    del ref
+
+    sm = BigSmallStreamingModel(StreamingLoader(image, device=dev), cfg)
+    for _ in range(2):
+        synthetic.greedy(sm.model, prompt, 4)
+    ids_s, lg_s, pre_s, dec_s = synthetic.greedy(sm.model, prompt, steps)
+    sm.check()
+    same_ids = bool(torch.equal(ids_r, ids_s))
+    same_logits = bool(torch.equal(lg_r.view(torch.int16), lg_s.view(torch.int16)))
+    # standalone decode time of one layer (for the hidden-fraction accounting)
+    side = torch.cuda.current_stream(dev)
+    layer_ms = _timed(torch, lambda: sm._bundles[(1, 1)].decode(side), 10, 3, side)
+    layer_raw = sum(2 * sm._slots[0][k].numel() for k in sm._slots[0])
+    dec_work = layers * layer_ms
+
+    def hidden(t_stream, t_res, n_passes):
+        work = dec_work * n_passes
+        return max(0.0, min(1.0, 1.0 - (t_stream - t_res) / work)) if work > 0 else None
+
+    res = {
+        "metric": "streaming inference ms/token (BASELINE config 4), batch 1", "unit": "ms/token",
+        "value": round(dec_s / steps, 3), "resident_ms_per_token": round(dec_r / steps, 3),
+        "prefill_ms": {"streaming": round(pre_s, 2), "resident": round(pre_r, 2)},
+        "layer_decode_ms": round(layer_ms, 4), "layer_decoded_GBs": round(layer_raw / layer_ms / 1e6, 1),
+        "hidden_fraction": {"prefill": hidden(pre_s, pre_r, 1), "decode": hidden(dec_s, dec_r, steps)},
+        "logits_bit_identical": same_logits, "tokens_identical": same_ids,
+        "hbm_resident_GB": {"streaming": round((comp_bytes + raw_bytes / layers * 0) / 1e9, 2),
+                            "compressed_model": round(comp_bytes / 1e9, 2), "full_model": round(raw_bytes / 1e9, 2)},
+        "ratio": round(comp_bytes / raw_bytes, 5), "higher_is_better": False, "n_gpus": 1,
+        "config": {"model": "Qwen2.5-14B-shaped random init (seed 0)", "layers": layers, "prompt": 512,
+                   "new_tokens": steps, "slots": 2, "chunk_elems": ce},
+        "setup_s": round(setup_s, 1)}
+    res["hbm_resident_GB"]["streaming"] = round((comp_bytes + sum(
+        2 * t.numel() for n, t in w.items() if ".layers." not in n) + 2 * layer_raw) / 1e9, 2)
+    print(json.dumps(res), flush=True)
+    sm.close()
 
 if __name__ == "__main__":
     main()

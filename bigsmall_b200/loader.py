@@ -291,3 +291,116 @@ def load_image(image: ContainerImage, device="cuda", names=None) -> dict[str, to
         return ld.run()
     finally:
         ld.close()
+
+
+class Bundle:
+    """A reusable decode of a fixed set of tensors (from a resident container)
+    into fixed output buffers: device plans plus device copies for raw tensors."""
+
+    def __init__(self, plans: list, copies: list):
+        self.plans = plans
+        self.copies = copies
+
+    def decode(self, stream: Optional[torch.cuda.Stream] = None) -> None:
+        for pl in self.plans:
+            pl.decode(stream)
+        if self.copies:
+            ctx = torch.cuda.stream(stream) if stream is not None else _nullctx()
+            with ctx:
+                for dst, src in self.copies:
+                    dst.copy_(src, non_blocking=True)
+
+    def check(self, stream: Optional[torch.cuda.Stream] = None) -> None:
+        for pl in self.plans:
+            pl.check(stream)
+
+    def close(self) -> None:
+        for pl in self.plans:
+            pl.close()
+        self.plans = []
+
+
+class _nullctx:
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *a):
+        return False
+
+
+class ResidentContainer:
+    """The compressed data section of a container uploaded to HBM once.
+
+    Any subset of its tensors can then be decoded, any number of times, into
+    caller-provided device buffers (:meth:`bundle`) or fresh tensors
+    (:meth:`decode`).  Only tensors stored with a device codec are accepted.
+    """
+
+    def __init__(self, image: ContainerImage, device=None):
+        self.image = image
+        self.device = torch.device("cuda", device if isinstance(device, int) else
+                                   (torch.device(device).index if device is not None else torch.cuda.current_device()))
+        if self.device.index is None:
+            self.device = torch.device("cuda", torch.cuda.current_device())
+        self.layout = {}
+        pos = 0
+        for t in image.header["tensors"]:
+            if t["codec"] == "tied_ref":
+                continue
+            if t["codec"] not in DEVICE_CODECS:
+                raise _unknown_codec(t["codec"])
+            self.layout[t["name"]] = (int(t["offset"]), pos, int(t["compressed_bytes"]))
+            pos += (int(t["compressed_bytes"]) + 15) // 16 * 16
+        self.data = torch.empty(max(16, pos), dtype=torch.uint8, device=self.device)
+        host = image.host
+        for hoff, doff, nb in self.layout.values():
+            if nb:
+                self.data[doff:doff + nb].copy_(host[hoff:hoff + nb], non_blocking=True)
+        torch.cuda.synchronize(self.device)
+
+    def resolve(self, name: str) -> str:
+        seen = set()
+        while self.image.tensors[name]["codec"] == "tied_ref":
+            if name in seen:
+                raise ValueError(f"Tied-ref cycle at {name!r}")
+            seen.add(name)
+            name = (self.image.tensors[name].get("extra") or {})["tied_to"]
+        return name
+
+    def blob(self, name: str) -> torch.Tensor:
+        _, d, nb = self.layout[self.resolve(name)]
+        return self.data[d:d + nb]
+
+    def empty_like(self, name: str) -> torch.Tensor:
+        m = self.image.tensors[self.resolve(name)]
+        return torch.empty(m["shape"] or [], dtype=TORCH_DTYPES.get(m["dtype"], torch.uint8), device=self.device)
+
+    def bundle(self, outputs: dict) -> Bundle:
+        """outputs: {name: device tensor of the tensor's shape/dtype}."""
+        xc, plans, copies = [], [], []
+        for name, out in outputs.items():
+            real = self.resolve(name)
+            m = self.image.tensors[real]
+            blob = self.blob(real)
+            flat = out.reshape(-1)
+            if m["codec"] == "bf16_exp_chunked_v1":
+                xc.append((blob, flat.view(torch.int16), int((m.get("extra") or {})["chunk_elems"])))
+            elif m["codec"] == "bf16_parallel_v1":
+                plans.append(gpu.ParPlan(bytes(self.image.blob_host(real)), blob, flat.view(torch.int16),
+                                         _ct.n_elements(m["shape"])))
+            else:   # raw
+                copies.append((flat.view(torch.uint8), blob))
+        if xc:
+            plans.insert(0, gpu.XcPlan(xc, device=self.device.index))
+        return Bundle(plans, copies)
+
+    def decode(self, names, stream=None) -> dict:
+        """Decode `names` into fresh tensors (synchronous, checked)."""
+        outs = {n: self.empty_like(n) for n in names}
+        b = self.bundle(outs)
+        try:
+            b.decode(stream)
+            b.check(stream)
+        finally:
+            b.close()
+        return outs
