@@ -128,15 +128,18 @@ class BigSmallStreamingModel:
         self._primed = False
         for i in range(self.n_layers):
             self._patch_layer(i)
-        # placeholders so the module tree has no meta parameters left
+        # bind layer i to slot i % slots once; with a layer count divisible by
+        # the slot count every later pass finds the same slot and skips rebinding
+        self._bound = [-1] * self.n_layers
         for i in range(self.n_layers):
-            self._bind(i, 0)
+            self._bind(i, i % self.n_slots)
 
     # ------------------------------------------------------------------
     def _bind(self, layer: int, slot: int) -> None:
         mod = _get_module(self.model, self.layer_template.format(layer))
         for k, t in self._slots[slot].items():
             _set_param(mod, k, t)
+        self._bound[layer] = slot
 
     def _prime(self, first_layer: int = 0) -> None:
         """Enqueue the decodes of the next `slots` layer executions."""
@@ -159,7 +162,8 @@ class BigSmallStreamingModel:
             if not outer.prefetch:
                 slot = 0
                 outer._bundles[(layer_idx, slot)].decode(main)
-                outer._bind(layer_idx, slot)
+                if outer._bound[layer_idx] != slot:
+                    outer._bind(layer_idx, slot)
                 return original(*args, **kwargs)
             if not outer._primed or outer._expect != layer_idx:
                 # first call, or out of the expected order: drain the side
@@ -168,7 +172,8 @@ class BigSmallStreamingModel:
                 outer._prime(first_layer=layer_idx)
             slot = outer._k % outer.n_slots
             main.wait_event(outer._decoded[slot])
-            outer._bind(layer_idx, slot)
+            if outer._bound[layer_idx] != slot:
+                outer._bind(layer_idx, slot)
             out = original(*args, **kwargs)
             outer._released[slot].record(main)
             nxt = (layer_idx + outer.n_slots) % outer.n_layers
