@@ -1,0 +1,78 @@
+"""Install this engine behind an imported reference ``bigsmall`` package.
+
+The three insertion points (BigSmall paths):
+  * ``bigsmall/kernels/__init__.py:56-64`` imports ``bigsmall.kernels.ac_cuda``
+    first and calls ``ac_cuda.decode(blob, extras, n) -> bytes`` for
+    bf16_parallel_v1 -> this package's ``kernels.ac_cuda`` module is placed at
+    that module name and the backend probe cache is reset;
+  * ``bigsmall/decoder.py:49-97`` ``_decode_blob`` is an if-chain that raises
+    for codec names it does not know -> it is wrapped so bf16_exp_chunked_v1
+    (and bf16_parallel_v1) decode on the device, everything else is passed to
+    the original function;
+  * ``bigsmall/codec_registry.py:45-47`` ``register_codec`` -> the codec names
+    are registered so ``verify_fast`` and encode-side selection know them.
+``StreamingLoader`` (``bigsmall/streaming.py:163-181``) and ``decompress``
+import ``_decode_blob`` by name, so their module attributes are patched too.
+"""
+from __future__ import annotations
+
+import sys
+import types
+
+from . import codec_registry as _reg
+from . import decoder as _dec
+from .kernels import ac_cuda as _ac_cuda
+
+DEVICE_CODECS = ("bf16_exp_chunked_v1", "bf16_parallel_v1")
+
+
+def install(bigsmall_pkg) -> dict:
+    """Wire the device engine into an imported reference package.  Returns the
+    original callables so :func:`uninstall` can restore them."""
+    name = bigsmall_pkg.__name__
+    saved = {}
+    # 1. backend slot
+    kern = sys.modules.get(f"{name}.kernels") or getattr(bigsmall_pkg, "kernels", None)
+    sys.modules[f"{name}.kernels.ac_cuda"] = _ac_cuda
+    if kern is not None:
+        saved["ac_cuda"] = getattr(kern, "ac_cuda", None)
+        kern.ac_cuda = _ac_cuda
+        for attr, val in (("_GPU_BACKEND", None), ("_GPU_DECODE_FN", None)):
+            if hasattr(kern, attr):
+                setattr(kern, attr, val)
+    # 2. dispatch
+    dec = sys.modules.get(f"{name}.decoder") or getattr(bigsmall_pkg, "decoder")
+    orig = dec._decode_blob
+    saved["_decode_blob"] = orig
+
+    def _decode_blob(t, blob):
+        if t.get("codec") in DEVICE_CODECS:
+            return _dec._decode_blob(t, blob)
+        return orig(t, blob)
+
+    _decode_blob.__wrapped__ = orig
+    dec._decode_blob = _decode_blob
+    for mod_name in (f"{name}.streaming",):
+        m = sys.modules.get(mod_name)
+        if isinstance(m, types.ModuleType) and getattr(m, "_decode_blob", None) is orig:
+            saved[mod_name] = orig
+            m._decode_blob = _decode_blob
+    # 3. registry
+    reg = sys.modules.get(f"{name}.codec_registry") or getattr(bigsmall_pkg, "codec_registry", None)
+    if reg is not None:
+        _reg.install_into(reg)
+    return saved
+
+
+def uninstall(bigsmall_pkg, saved: dict) -> None:
+    name = bigsmall_pkg.__name__
+    dec = sys.modules.get(f"{name}.decoder") or getattr(bigsmall_pkg, "decoder")
+    dec._decode_blob = saved["_decode_blob"]
+    kern = sys.modules.get(f"{name}.kernels") or getattr(bigsmall_pkg, "kernels", None)
+    if kern is not None:
+        if saved.get("ac_cuda") is None and hasattr(kern, "ac_cuda"):
+            delattr(kern, "ac_cuda")
+        sys.modules.pop(f"{name}.kernels.ac_cuda", None)
+    for mod_name, fn in saved.items():
+        if mod_name.endswith(".streaming") and mod_name in sys.modules:
+            sys.modules[mod_name]._decode_blob = fn
