@@ -555,7 +555,7 @@ def bench_sweep(a, torch, dev, world, rank, dist, local):
         hist = torch.bincount(((x.view(torch.int16).to(torch.int32) >> 7) & 0xFF), minlength=256).double()
         pr = hist[hist > 0] / n
         h_exp = float(-(pr * pr.log2()).sum())
-        for coder in ("rans", "tans"):
+        for coder in ("rans", "tans", "pair"):
             for cbytes in (64 << 10, 256 << 10, 1 << 20, 4 << 20):
                 ce = cbytes // 2
                 blob = gpu.encode_xc(x, coder=coder, chunk_elems=ce)

@@ -32,6 +32,7 @@ DEV_BITS = {0x01: "header", 0x02: "freq", 0x04: "chunk_table", 0x08: "stream",
 
 CODER_RANS = 0
 CODER_TANS = 1
+CODER_RANS_PAIR = 2
 
 
 class XcTensor(ctypes.Structure):

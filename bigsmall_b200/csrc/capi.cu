@@ -202,6 +202,7 @@ int bs_xc_plan_create(const bs_xc_tensor *tensors, int n_tensors, int device, bs
         d.chunk_elems = t.chunk_elems;
         d.n_chunks = static_cast<uint32_t>(nc);
         d.chunk_begin = t.chunk_begin;
+        d.aux = 0;
         d.coder = 0xFFFFFFFFu;
         u2i[i] = static_cast<int>(ht.size());
         ht.push_back(d);
@@ -234,7 +235,7 @@ int bs_xc_plan_create(const bs_xc_tensor *tensors, int n_tensors, int device, bs
     const uint64_t o_t = cv.take(sizeof(XcTensorDev) * ht.size());
     const uint64_t o_i = cv.take(sizeof(XcItem) * items.size());
     const uint64_t o_e = cv.take(4 * ht.size());
-    const uint64_t o_tab = cv.take(4ull * kXcMaxTable * ht.size());
+    const uint64_t o_tab = cv.take(4ull * kXcTableWords * ht.size());
     int rc = alloc_plan_mem(p, cv.off);
     if (rc) { free_plan(p); return rc; }
     auto *base = static_cast<uint8_t *>(p->d_mem);
@@ -626,7 +627,7 @@ int bs_xc_encode_bound(uint64_t n, uint32_t ce, uint64_t *bytes) {
 }
 
 int bs_xc_encode_workspace(uint64_t n, uint32_t ce, int coder, uint64_t *bytes) {
-    if (!bytes || ce < 256 || (ce & 255) || (coder != BS_CODER_RANS && coder != BS_CODER_TANS))
+    if (!bytes || ce < 256 || (ce & 255) || coder < BS_CODER_RANS || coder > BS_CODER_RANS_PAIR)
         return fail(BS_E_INVALID_ARG, "bad encode_workspace arguments");
     *bytes = n ? xc_encode_workspace(n, ce, coder) : 0;
     return BS_OK;
@@ -637,7 +638,8 @@ int bs_xc_encode(const void *d_in, uint64_t n, int coder, int prec, uint32_t ce,
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     if (ce < 256 || (ce & 255)) return fail(BS_E_INVALID_ARG, "chunk_elems must be a positive multiple of 256");
     if (prec < 8 || prec > 12) return fail(BS_E_INVALID_ARG, "precision must be in [8, 12]");
-    if (coder != BS_CODER_RANS && coder != BS_CODER_TANS) return fail(BS_E_INVALID_ARG, "coder must be 0 (rANS) or 1 (tANS)");
+    if (coder < BS_CODER_RANS || coder > BS_CODER_RANS_PAIR)
+        return fail(BS_E_INVALID_ARG, "coder must be 0 (rANS), 1 (tANS) or 2 (rANS over exponent pairs)");
     if (!d_out_len) return fail(BS_E_INVALID_ARG, "d_out_len is NULL");
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) return fail(BS_E_CUDA, "no current device");

@@ -13,18 +13,27 @@ constexpr uint32_t kFull = 0xFFFFFFFFu;
 
 // ---- bf16_exp_chunked_v1 layout (little-endian; sections in this order, each
 // 16-byte aligned):
-//   0 "BSXC" | 4 u16 version=1 | 6 u8 coder (0 rANS, 1 tANS) | 7 u8 P
-//   8 u64 n | 16 u32 chunk_elems | 20 u32 n_chunks | 24 u32 lanes=32 | 28 u32 0
+//   0 "BSXC" | 4 u16 version=1 | 6 u8 coder (0 rANS, 1 tANS, 2 rANS over
+//   exponent pairs) | 7 u8 P
+//   8 u64 n | 16 u32 chunk_elems | 20 u32 n_chunks | 24 u32 lanes=32
+//   28 u32 aux (coder 2: window base e_lo; else 0)
 //   32 u64 chunks_off | 40 u64 plane_off | 48 u64 blob_bytes | 56 u64 0
 //   64 u16 freq[256] | 576 u32 chunk_start[n_chunks+1] (16 B units)
 //   plane_off = rup16(576 + 4*(n_chunks+1)): n bytes of (sign << 7) | mantissa
 //   chunks_off = plane_off + rup16(n): per chunk [u32 init[32]][u16 words...]
 //   zero-padded to 16 B; blob_bytes = end of the last chunk record.
+//   Coder 2 codes the pair (2k, 2k+1) as one symbol a*16 + b, a = e - e_lo
+//   for e in [e_lo, e_lo + 14] else 15 (escape; the exponent byte is stored in
+//   the record's escape list); its records are [u32 init[32]][u32 n_words]
+//   [u32 n_esc][u32 0][u32 0][u16 words][u8 escapes] zero-padded to 16 B.
 constexpr uint32_t kXcMagic = 0x43585342u;  // "BSXC" little-endian
 constexpr uint32_t kXcFreqOff = 64;
 constexpr uint32_t kXcTabOff = 576;
 constexpr uint32_t kXcLanes = 32;
 constexpr uint32_t kXcMaxTable = 4096;      // 2^12 entries, the largest precision
+constexpr uint32_t kXcTableWords = 2 * kXcMaxTable;   // u32 words per tensor's table slot
+                                                      // (the pair coder's entries are 8 bytes)
+constexpr uint32_t kXcPairRecHdr = 144;     // pair-coder record: 128 B states + 16 B counts
 
 // Device-side tensor descriptor of a decode plan.  The host fills the first
 // block; the table-build kernel fills the parsed header fields.
@@ -36,7 +45,7 @@ struct XcTensorDev {
     uint32_t chunk_elems;
     uint32_t n_chunks;
     uint32_t chunk_begin;     // d_out holds element chunk_begin * chunk_elems first
-    uint32_t pad0;
+    uint32_t aux;             // pair coder: first exponent of the 15-wide window (from the header)
     // parsed from the blob header by xc_prepare_kernel
     uint64_t chunks_off;
     uint64_t plane_off;

@@ -84,7 +84,7 @@ __global__ void __launch_bounds__(256) xc_prepare_kernel(XcTensorDev *tens, uint
     const int t = blockIdx.x;
     const int tid = threadIdx.x;
     XcTensorDev &T = tens[t];
-    __shared__ uint32_t s_err, s_prec, s_coder;
+    __shared__ uint32_t s_err, s_prec, s_coder, s_aux;
     __shared__ uint64_t s_chunks_off, s_plane_off, s_total;
     __shared__ uint32_t s_freq[256], s_cum[257];
     __shared__ uint32_t s_next[256];
@@ -101,16 +101,18 @@ __global__ void __launch_bounds__(256) xc_prepare_kernel(XcTensorDev *tens, uint
             uint32_t ver = ver_coder_prec & 0xFFFF, coder = (ver_coder_prec >> 16) & 0xFF;
             uint32_t prec = ver_coder_prec >> 24;
             uint64_t n = h64[1];
-            uint32_t ce = h32[4], nc = h32[5], lanes = h32[6];
+            uint32_t ce = h32[4], nc = h32[5], lanes = h32[6], aux = h32[7];
             uint64_t co = h64[4], po = h64[5], total = h64[6];
             const uint64_t po_want = (kXcTabOff + 4ull * (nc + 1ull) + 15) & ~15ull;
-            if (h32[0] != kXcMagic || ver != 1 || coder > 1 || prec < 8 || prec > 12 || n != T.n ||
+            if (h32[0] != kXcMagic || ver != 1 || coder > 2 || prec < 8 || prec > 12 || n != T.n ||
                 ce != T.chunk_elems || nc != T.n_chunks || lanes != kXcLanes || po != po_want ||
-                co != po + ((n + 15) & ~15ull) || total < co || (total & 15) || total > T.blob_bytes)
+                co != po + ((n + 15) & ~15ull) || total < co || (total & 15) || total > T.blob_bytes ||
+                (coder == 2 ? aux > 241 : aux != 0))
                 err = BS_DEV_HEADER;
             s_total = total;
             s_prec = prec;
             s_coder = coder;
+            s_aux = aux;
             s_chunks_off = co;
             s_plane_off = po;
         }
@@ -150,7 +152,7 @@ __global__ void __launch_bounds__(256) xc_prepare_kernel(XcTensorDev *tens, uint
         if (tid == 31) s_cum[256] = incl;
     }
     __syncthreads();
-    if (s_cum[256] != M || (coder == 0 && f >= M)) {
+    if (s_cum[256] != M || (coder != 1 && f >= M)) {
         if (tid == 0 || f >= M) atomicOr(&s_err, BS_DEV_FREQ);
     }
     __syncthreads();
@@ -161,8 +163,30 @@ __global__ void __launch_bounds__(256) xc_prepare_kernel(XcTensorDev *tens, uint
         }
         return;
     }
-    uint32_t *tab = tables + static_cast<uint64_t>(t) * kXcMaxTable;
-    if (coder == 0) {
+    uint32_t *tab = tables + static_cast<uint64_t>(t) * kXcTableWords;
+    if (coder == 2) {
+        // pair entry (8 bytes): x = (slot - cum) | freq << 16; y = the two
+        // exponents pre-shifted to their bf16 positions (e_a << 7 | e_b << 23),
+        // with bit 15 / bit 31 flagging an escape (exponent in the record)
+        const uint32_t per = (M + 255) / 256;
+        const uint32_t s0 = tid * per, e_lo = s_aux;
+        if (s0 < M) {
+            int lo = 0, hi = 255;
+            while (lo < hi) {
+                int mid = (lo + hi + 1) >> 1;
+                if (s_cum[mid] <= s0) lo = mid; else hi = mid - 1;
+            }
+            uint32_t s = lo;
+            uint2 *tab2 = reinterpret_cast<uint2 *>(tab);
+            for (uint32_t k = 0; k < per && s0 + k < M; k++) {
+                const uint32_t slot = s0 + k;
+                while (s_cum[s + 1] <= slot) s++;
+                const uint32_t a = s >> 4, b = s & 15;
+                const uint32_t y = (a == 15 ? 0x8000u : (e_lo + a) << 7) | (b == 15 ? 0x80000000u : (e_lo + b) << 23);
+                tab2[slot] = make_uint2((slot - s_cum[s]) | (s_freq[s] << 16), y);
+            }
+        }
+    } else if (coder == 0) {
         // rANS entry: (slot - cum) | sym << 12 | freq << 20; 16 slots per thread
         const uint32_t per = (M + 255) / 256;
         uint32_t s0 = tid * per;
@@ -223,6 +247,7 @@ __global__ void __launch_bounds__(256) xc_prepare_kernel(XcTensorDev *tens, uint
         T.prec = P;
         T.chunks_off = s_chunks_off;
         T.plane_off = s_plane_off;
+        T.aux = s_aux;
     }
 }
 
@@ -408,6 +433,214 @@ __device__ __forceinline__ void decode_chunk(const uint32_t *__restrict__ s_tab,
     if (code && lane == 0) atomicOr(err, code);
 }
 
+// --------------------------------------------------------------------------
+// coder 2: rANS over exponent pairs.  One step decodes the two consecutive
+// values a lane writes into one 32-bit output word, so a lane's 8 values take
+// 4 steps.  The 8-byte table entry gives the state update (x) and both
+// exponents already in their bf16 bit positions (y); a rare escape (bit 15 /
+// bit 31 of y) takes its exponent from the record's escape list in a
+// warp-uniform fix-up path.
+// --------------------------------------------------------------------------
+constexpr uint32_t kPairMirror = kFill;                 // 8 pair-steps consume <= 512 B
+constexpr uint32_t kPairWarpRing = kRingBytes + kPairMirror;
+constexpr uint32_t kPairTableBytes = 8 * kXcMaxTable;
+
+__device__ __forceinline__ uint2 lds_u64(uint32_t a) {
+    uint2 v;
+    asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(a));
+    return v;
+}
+
+__device__ __forceinline__ void pair_ring_issue(Ring &r, uint32_t lane) {
+    const uint32_t off = r.fetched + 16 * lane;
+    if (off < r.bytes) {
+        const uint32_t pos = off & (kRingBytes - 1);
+        cp_async16(r.buf + pos, r.src + off);
+        if (pos < kPairMirror) cp_async16(r.buf + kRingBytes + pos, r.src + off);
+    }
+    cp_async_commit();
+    r.fetched += kFill;
+}
+
+__device__ __forceinline__ void pair_ring_ensure(Ring &r, uint32_t consumed_bytes) {
+    uint32_t need = consumed_bytes + kPairMirror;
+    if (need > r.bytes) need = r.bytes;
+    if (need > r.landed) {
+        cp_async_wait_all();
+        __syncwarp();
+        r.landed = r.fetched;
+    }
+}
+
+__device__ __forceinline__ void pair_ring_refill(Ring &r, uint32_t consumed_bytes, uint32_t lane) {
+    if (r.fetched < r.bytes && r.fetched + kFill - consumed_bytes <= kRingBytes) {
+        __syncwarp();
+        pair_ring_issue(r, lane);
+    }
+}
+
+// patch escaped exponents of one output word; `pos` is the warp's next escape
+__device__ __forceinline__ uint32_t pair_patch(uint32_t word, uint32_t y, bool valid_b, const uint8_t *esc,
+                                               uint32_t n_esc, uint32_t &pos, uint32_t lt, uint32_t &bad) {
+    const bool ea = (y & 0x8000u) != 0;
+    const bool eb = valid_b && (y & 0x80000000u) != 0;
+    const uint32_t ba = __ballot_sync(kFull, ea), bb = __ballot_sync(kFull, eb);
+    const uint32_t pa = pos + __popc(ba & lt) + __popc(bb & lt);
+    const uint32_t pb = pa + (ea ? 1u : 0u);
+    if (ea) {
+        if (pa < n_esc) word = (word & ~0x7F80u) | (static_cast<uint32_t>(esc[pa]) << 7);
+        else bad = 1;
+    }
+    if (eb) {
+        if (pb < n_esc) word = (word & ~0x7F800000u) | (static_cast<uint32_t>(esc[pb]) << 23);
+        else bad = 1;
+    }
+    pos += __popc(ba) + __popc(bb);
+    return word;
+}
+
+__device__ __forceinline__ uint32_t merge_pair2(uint32_t y, uint32_t cc) {
+    return (cc & 0x807F807Fu) | (y & 0x7F807F80u);
+}
+
+__device__ __forceinline__ void decode_chunk_pair(uint32_t tab_s, uint8_t *ring_buf,
+                                                  const uint8_t *__restrict__ rec, uint32_t rec_bytes,
+                                                  const uint8_t *__restrict__ plane,
+                                                  uint16_t *__restrict__ out, uint32_t cn, uint32_t P,
+                                                  uint32_t *err) {
+    const uint32_t lane = threadIdx.x & 31;
+    const uint32_t lt = lanemask_lt();
+    const uint32_t smask = (1u << P) - 1;
+    const uint32_t ring_s = static_cast<uint32_t>(__cvta_generic_to_shared(ring_buf));
+    const uint32_t *rec32 = reinterpret_cast<const uint32_t *>(rec);
+    uint32_t x = rec32[lane];
+    const uint32_t n_words = rec32[32], n_esc = rec32[33];
+    uint32_t bad = (rec32[34] | rec32[35]) != 0 ? 1u : 0u;
+    const uint64_t body = static_cast<uint64_t>(kXcPairRecHdr) + 2ull * n_words + n_esc;
+    if (body > rec_bytes || rec_bytes - body >= 16) bad = 1;
+    if (__any_sync(kFull, bad)) {
+        if (lane == 0) atomicOr(err, BS_DEV_STREAM);
+        return;
+    }
+    const uint8_t *esc = rec + kXcPairRecHdr + 2ull * n_words;
+    uint32_t stage = (2 * n_words + 15) & ~15u;
+    if (stage > rec_bytes - kXcPairRecHdr) stage = rec_bytes - kXcPairRecHdr;
+    Ring r{ring_buf, rec + kXcPairRecHdr, stage, 0, 0};
+#pragma unroll
+    for (int k = 0; k < (int)(kRingBytes / kFill); k++) pair_ring_issue(r, lane);
+
+    uint32_t raddr = ring_s, consumed = 0, epos = 0;
+    const uint32_t G = cn >> 8, rem = cn & 255;
+
+    auto step = [&](bool active) -> uint32_t {
+        const uint2 t = lds_u64(tab_s + ((x & smask) << 3));
+        const uint32_t nx = (t.x >> 16) * (x >> P) + (t.x & 0xFFFFu);
+        if (active) x = nx;
+        const bool need = active && (x < kRansL);
+        const uint32_t m = __ballot_sync(kFull, need);
+        const uint32_t w = lds_u16(raddr + 2 * __popc(m & lt));
+        if (need) x = x * 65536u + w;
+        raddr += 2 * __popc(m);
+        return t.y;
+    };
+    auto group = [&](uint32_t g, uint2 sm) {
+        const uint32_t y0 = step(true), y1 = step(true), y2 = step(true), y3 = step(true);
+        uint4 v;
+        v.x = merge_pair2(y0, __byte_perm(sm.x, 0, 0x1100));
+        v.y = merge_pair2(y1, __byte_perm(sm.x, 0, 0x3322));
+        v.z = merge_pair2(y2, __byte_perm(sm.y, 0, 0x1100));
+        v.w = merge_pair2(y3, __byte_perm(sm.y, 0, 0x3322));
+        if (__any_sync(kFull, ((y0 | y1 | y2 | y3) & 0x80008000u) != 0)) {
+            v.x = pair_patch(v.x, y0, true, esc, n_esc, epos, lt, bad);
+            v.y = pair_patch(v.y, y1, true, esc, n_esc, epos, lt, bad);
+            v.z = pair_patch(v.z, y2, true, esc, n_esc, epos, lt, bad);
+            v.w = pair_patch(v.w, y3, true, esc, n_esc, epos, lt, bad);
+        }
+        st_out16(out + g * 256 + lane * 8, v);
+    };
+    const uint32_t ring_end = ring_s + kRingBytes;
+    const uint8_t *pl = plane + lane * 8;
+    uint2 sm_a = make_uint2(0, 0), sm_b = make_uint2(0, 0);
+    if (G > 0) sm_a = ld_plane8(pl);
+    if (G > 1) sm_b = ld_plane8(pl + 256);
+    uint32_t g = 0;
+    for (; g + 1 < G; g += 2) {
+        pair_ring_ensure(r, consumed);
+        if (raddr >= ring_end) raddr -= kRingBytes;
+        const uint32_t rstart = raddr;
+        const uint2 s0 = sm_a, s1 = sm_b;
+        sm_a = ld_plane8(pl + min(g + 2, G - 1) * 256);
+        sm_b = ld_plane8(pl + min(g + 3, G - 1) * 256);
+        group(g, s0);
+        group(g + 1, s1);
+        consumed += raddr - rstart;
+        pair_ring_refill(r, consumed, lane);
+    }
+    if (g < G) {
+        pair_ring_ensure(r, consumed);
+        if (raddr >= ring_end) raddr -= kRingBytes;
+        const uint32_t rstart = raddr;
+        group(g, sm_a);
+        consumed += raddr - rstart;
+    }
+    if (rem) {
+        pair_ring_ensure(r, consumed);
+        if (raddr >= ring_end) raddr -= kRingBytes;
+        const uint32_t rstart = raddr;
+        const uint32_t e_base = G * 256 + lane * 8;
+#pragma unroll 1
+        for (uint32_t jj = 0; jj < 4; jj++) {
+            const uint32_t e = lane * 8 + 2 * jj;
+            const bool active = e < rem;
+            const bool second = e + 1 < rem;
+            const uint32_t y = step(active);
+            uint32_t c0 = active ? plane[e_base + 2 * jj] : 0u, c1 = second ? plane[e_base + 2 * jj + 1] : 0u;
+            uint32_t word = merge_pair2(y, c0 | (c0 << 8) | (c1 << 16) | (c1 << 24));
+            if (__any_sync(kFull, active && (y & (second ? 0x80008000u : 0x8000u)) != 0))
+                word = pair_patch(word, active ? y : 0u, second, esc, n_esc, epos, lt, bad);
+            if (active) out[e_base + 2 * jj] = static_cast<uint16_t>(word);
+            if (second) out[e_base + 2 * jj + 1] = static_cast<uint16_t>(word >> 16);
+        }
+        consumed += raddr - rstart;
+    }
+    cp_async_wait_all();
+    __syncwarp();
+    const bool bad_state = x != kRansL;
+    const bool bad_stream = consumed != 2 * n_words || epos != n_esc || bad;
+    uint32_t code = (bad_state ? BS_DEV_FINAL_STATE : 0u) | (bad_stream ? BS_DEV_STREAM : 0u);
+    code = __reduce_or_sync(kFull, code);
+    if (code && lane == 0) atomicOr(err, code);
+}
+
+__global__ void __launch_bounds__(kThreads) xc_decode_pair_kernel(const XcTensorDev *__restrict__ tens,
+                                                                  const XcItem *__restrict__ items,
+                                                                  const uint32_t *__restrict__ tables,
+                                                                  uint32_t *errs) {
+    extern __shared__ __align__(16) uint8_t smem[];
+    uint8_t *s_ring = smem + kPairTableBytes;
+    const XcItem it = items[blockIdx.x];
+    const XcTensorDev &T = tens[it.tensor];
+    if (T.coder != 2) return;   // other coders: xc_decode_kernel; flagged tensors: skipped
+    const uint32_t P = T.prec;
+    const uint32_t M = 1u << P;
+    const uint4 *src = reinterpret_cast<const uint4 *>(tables + static_cast<uint64_t>(it.tensor) * kXcTableWords);
+    for (uint32_t i = threadIdx.x; i < M / 2; i += kThreads) reinterpret_cast<uint4 *>(smem)[i] = src[i];
+    __syncthreads();
+    const uint32_t warp = threadIdx.x >> 5;
+    if (warp >= it.n_chunks) return;
+    const uint32_t c = it.first_chunk + warp;
+    const uint8_t *blob = T.blob;
+    const uint32_t *cs = reinterpret_cast<const uint32_t *>(blob + kXcTabOff);
+    const uint32_t a = cs[c], z = cs[c + 1];
+    const uint64_t e0 = static_cast<uint64_t>(c) * T.chunk_elems;
+    const uint64_t left = T.n - e0;
+    const uint32_t cn = left < T.chunk_elems ? static_cast<uint32_t>(left) : T.chunk_elems;
+    decode_chunk_pair(static_cast<uint32_t>(__cvta_generic_to_shared(smem)), s_ring + warp * kPairWarpRing,
+                      blob + T.chunks_off + 16ull * a, 16u * (z - a), blob + T.plane_off + e0,
+                      T.out + (e0 - static_cast<uint64_t>(T.chunk_begin) * T.chunk_elems), cn, P,
+                      &errs[it.tensor]);
+}
+
 __global__ void __launch_bounds__(kThreads) xc_decode_kernel(const XcTensorDev *__restrict__ tens,
                                                              const XcItem *__restrict__ items,
                                                              const uint32_t *__restrict__ tables,
@@ -422,7 +655,7 @@ __global__ void __launch_bounds__(kThreads) xc_decode_kernel(const XcTensorDev *
     if (coder > 1) return;   // the table build flagged this tensor
     const uint32_t P = T.prec;
     const uint32_t M = 1u << P;
-    const uint4 *src = reinterpret_cast<const uint4 *>(tables + static_cast<uint64_t>(it.tensor) * kXcMaxTable);
+    const uint4 *src = reinterpret_cast<const uint4 *>(tables + static_cast<uint64_t>(it.tensor) * kXcTableWords);
     for (uint32_t i = threadIdx.x; i < M / 4; i += kThreads) reinterpret_cast<uint4 *>(s_tab)[i] = src[i];
     __syncthreads();
 
@@ -465,6 +698,18 @@ cudaError_t launch_xc_decode(const XcTensorDev *d_tens, const XcItem *d_items, i
         attr_set = true;
     }
     xc_decode_kernel<<<n_items, kThreads, smem, s>>>(d_tens, d_items, d_tables, d_errs);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    // the pair coder's kernel; each CTA returns at once unless its tensor uses coder 2
+    const size_t psmem = kPairTableBytes + kWarps * kPairWarpRing;
+    static bool pair_attr_set = false;
+    if (!pair_attr_set) {
+        e = cudaFuncSetAttribute(xc_decode_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 static_cast<int>(psmem));
+        if (e != cudaSuccess) return e;
+        pair_attr_set = true;
+    }
+    xc_decode_pair_kernel<<<n_items, kThreads, psmem, s>>>(d_tens, d_items, d_tables, d_errs);
     return cudaGetLastError();
 }
 
@@ -481,7 +726,7 @@ cudaError_t launch_xc_decode(const XcTensorDev *d_tens, const XcItem *d_items, i
 // --------------------------------------------------------------------------
 constexpr int kNoallocMaxTensors = BS_NOALLOC_MAX_TENSORS;
 constexpr uint64_t kNoallocTablesOff = 0;
-constexpr uint64_t kNoallocTensOff = kNoallocTablesOff + 4ull * kXcMaxTable * kNoallocMaxTensors;
+constexpr uint64_t kNoallocTensOff = kNoallocTablesOff + 4ull * kXcTableWords * kNoallocMaxTensors;
 constexpr uint64_t kNoallocErrsOff = kNoallocTensOff + 256ull * ((sizeof(XcTensorDev) * kNoallocMaxTensors + 255) / 256);
 constexpr uint64_t kNoallocScratchBytes = kNoallocErrsOff + 256;
 
@@ -514,7 +759,7 @@ __global__ void __launch_bounds__(kThreads) xc_decode_noalloc_kernel(const Noall
     if (coder > 1) return;   // xc_prepare_kernel flagged this tensor
     const uint32_t P = T.prec;
     const uint32_t M = 1u << P;
-    const uint4 *src = reinterpret_cast<const uint4 *>(tables + static_cast<uint64_t>(ti) * kXcMaxTable);
+    const uint4 *src = reinterpret_cast<const uint4 *>(tables + static_cast<uint64_t>(ti) * kXcTableWords);
     for (uint32_t i = threadIdx.x; i < M / 4; i += kThreads) reinterpret_cast<uint4 *>(s_tab)[i] = src[i];
     __syncthreads();
     const uint32_t warp = threadIdx.x >> 5;
@@ -536,6 +781,36 @@ __global__ void __launch_bounds__(kThreads) xc_decode_noalloc_kernel(const Noall
         decode_chunk<0>(s_tab, ring, rec, rec_bytes, plane, out, cn, P, &errs[ti]);
     else
         decode_chunk<1>(s_tab, ring, rec, rec_bytes, plane, out, cn, P, &errs[ti]);
+}
+
+__global__ void __launch_bounds__(kThreads) xc_decode_noalloc_pair_kernel(const NoallocArgs a,
+                                                                          const XcTensorDev *__restrict__ tens,
+                                                                          const uint32_t *__restrict__ tables,
+                                                                          uint32_t *errs) {
+    extern __shared__ __align__(16) uint8_t smem[];
+    uint8_t *s_ring = smem + kPairTableBytes;
+    int ti = 0;
+    while (ti + 1 < a.n && blockIdx.x >= a.cta_prefix[ti + 1]) ti++;
+    const XcTensorDev &T = tens[ti];
+    if (T.coder != 2) return;
+    const uint32_t P = T.prec;
+    const uint32_t M = 1u << P;
+    const uint4 *src = reinterpret_cast<const uint4 *>(tables + static_cast<uint64_t>(ti) * kXcTableWords);
+    for (uint32_t i = threadIdx.x; i < M / 2; i += kThreads) reinterpret_cast<uint4 *>(smem)[i] = src[i];
+    __syncthreads();
+    const uint32_t warp = threadIdx.x >> 5;
+    const uint32_t c0 = a.tens[ti].chunk_begin;
+    const uint32_t c = c0 + (blockIdx.x - a.cta_prefix[ti]) * kWarps + warp;
+    if (c >= c0 + a.range_count[ti]) return;
+    const uint8_t *blob = T.blob;
+    const uint32_t *cs = reinterpret_cast<const uint32_t *>(blob + kXcTabOff);
+    const uint32_t ca = cs[c], cz = cs[c + 1];
+    const uint64_t e0 = static_cast<uint64_t>(c) * T.chunk_elems;
+    const uint64_t left = T.n - e0;
+    const uint32_t cn = left < T.chunk_elems ? static_cast<uint32_t>(left) : T.chunk_elems;
+    decode_chunk_pair(static_cast<uint32_t>(__cvta_generic_to_shared(smem)), s_ring + warp * kPairWarpRing,
+                      blob + T.chunks_off + 16ull * ca, 16u * (cz - ca), blob + T.plane_off + e0,
+                      T.out + (e0 - static_cast<uint64_t>(T.chunk_begin) * T.chunk_elems), cn, P, &errs[ti]);
 }
 
 namespace {
@@ -586,6 +861,15 @@ cudaError_t launch_xc_noalloc(const XcTensorDev *h_tens, const uint32_t *range_c
         const size_t smem = kXcMaxTable * 4 + kWarps * kWarpRing;
         xc_decode_noalloc_kernel<<<a.cta_prefix[n], kThreads, smem, s>>>(a, d_tens, d_tables, d_errs);
         e = cudaGetLastError();
+        if (e == cudaSuccess) {
+            const size_t psmem = kPairTableBytes + kWarps * kPairWarpRing;
+            e = cudaFuncSetAttribute(xc_decode_noalloc_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     static_cast<int>(psmem));
+            if (e == cudaSuccess) {
+                xc_decode_noalloc_pair_kernel<<<a.cta_prefix[n], kThreads, psmem, s>>>(a, d_tens, d_tables, d_errs);
+                e = cudaGetLastError();
+            }
+        }
     }
     if (e == cudaSuccess) e = cudaMemcpyAsync(h_status, d_errs, 4ull * n, cudaMemcpyDeviceToHost, s);
     if (e == cudaSuccess) e = cudaStreamSynchronize(s);

@@ -28,14 +28,16 @@ namespace bsg {
 
 namespace {
 constexpr int kEncWarps = 8;
-constexpr uint64_t kWsCounts = 0;       // u64[256]
+constexpr uint64_t kWsCounts = 0;       // u64[256] exponent histogram
 constexpr uint64_t kWsTab = 2048;       // u32[256]: freq | cum << 16
 constexpr uint64_t kWsFlags = 3072;     // u32 flags
-constexpr uint64_t kWsRec = 4096;       // u32[n_chunks]: words per record
+constexpr uint64_t kWsAux = 3076;       // u32 pair coder: window base e_lo
+constexpr uint64_t kWsPairCounts = 4096;   // u64[256] pair-symbol histogram
+constexpr uint64_t kWsRec = 6144;       // u32[n_chunks] words per record, then u32[n_chunks] escapes
 
 inline uint64_t rup(uint64_t x, uint64_t a) { return (x + a - 1) / a * a; }
-inline uint64_t slot_bytes(uint32_t ce) { return rup(128 + 2ull * ce, 16); }
-inline uint64_t slotlist_off(uint64_t nc) { return rup(kWsRec + 4 * nc, 256); }   // u16[4096] (tANS)
+inline uint64_t slot_bytes(uint32_t ce) { return rup(kXcPairRecHdr + 2ull * ce, 16); }
+inline uint64_t slotlist_off(uint64_t nc) { return rup(kWsRec + 8 * nc, 256); }   // u16[4096] (tANS)
 inline uint64_t slots_off(uint64_t nc) { return slotlist_off(nc) + 2 * kXcMaxTable; }
 // tANS: one u32 (bits | nbits << 16) per lane and step, rup(chunk, 256) per chunk
 inline uint64_t tans_scratch_off(uint64_t nc, uint32_t ce) { return slots_off(nc) + nc * slot_bytes(ce); }
@@ -105,7 +107,8 @@ __global__ void __launch_bounds__(256) xc_enc_hist_kernel(const uint16_t *__rest
 // never below 1; a single present symbol gets M-1 plus a phantom neighbour.
 __global__ void __launch_bounds__(256) xc_enc_setup_kernel(const unsigned long long *counts, uint64_t n,
                                                            int coder, int prec, uint32_t ce, uint32_t nc,
-                                                           uint8_t *out, uint32_t *enc_tab, uint16_t *slot_list) {
+                                                           uint8_t *out, uint32_t *enc_tab, uint16_t *slot_list,
+                                                           const uint32_t *aux) {
     __shared__ int64_t f[256];
     __shared__ uint32_t s_cum[256];
     __shared__ uint8_t s_spread[kXcMaxTable];
@@ -162,7 +165,7 @@ __global__ void __launch_bounds__(256) xc_enc_setup_kernel(const unsigned long l
         h32[4] = ce;
         h32[5] = nc;
         h32[6] = kXcLanes;
-        h32[7] = 0;
+        h32[7] = coder == BS_CODER_RANS_PAIR ? *aux : 0u;
         h64[4] = chunks_off;
         h64[5] = plane_off;
         h64[7] = 0;
@@ -200,6 +203,138 @@ __global__ void __launch_bounds__(256) xc_enc_setup_kernel(const unsigned long l
             if ((grp & lt) == 0) s_occ[sym] += __popc(grp);
             __syncwarp();
         }
+    }
+}
+
+// 2b. pair coder: exponent window and pair-symbol histogram ------------------
+__device__ __forceinline__ uint32_t pair_a(uint32_t v, uint32_t e_lo) {
+    const uint32_t d = ((v >> 7) & 0xFF) - e_lo;   // wraps to a large value below e_lo
+    return d <= 14 ? d : 15u;
+}
+
+// the 15-wide exponent window holding the most values (lowest base on ties)
+__global__ void xc_enc_window_kernel(const unsigned long long *counts, uint32_t *aux) {
+    if (threadIdx.x != 0) return;
+    unsigned long long best = 0, m = 0;
+    uint32_t bw = 0;
+    for (int k = 0; k < 15; k++) m += counts[k];
+    best = m;
+    for (uint32_t w = 1; w + 14 < 256; w++) {
+        m += counts[w + 14] - counts[w - 1];
+        if (m > best) { best = m; bw = w; }
+    }
+    *aux = bw;
+}
+
+// pairs (2k, 2k+1) of the tensor; an odd tail value pairs with b = 0
+__global__ void __launch_bounds__(256) xc_enc_pair_hist_kernel(const uint16_t *__restrict__ in, uint64_t n,
+                                                               const uint32_t *aux,
+                                                               unsigned long long *pcounts) {
+    __shared__ uint32_t h[8][256];
+    const uint32_t w = threadIdx.x >> 5;
+    for (int i = threadIdx.x; i < 8 * 256; i += 256) (&h[0][0])[i] = 0;
+    __syncthreads();
+    const uint32_t e_lo = *aux;
+    const uint64_t n8 = n / 8;
+    const uint64_t stride = static_cast<uint64_t>(gridDim.x) * blockDim.x;
+    for (uint64_t q = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; q < n8; q += stride) {
+        const uint4 v = reinterpret_cast<const uint4 *>(in)[q];
+        const uint32_t wv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int k = 0; k < 4; k++)
+            atomicAdd(&h[w][pair_a(wv[k] & 0xFFFF, e_lo) * 16 + pair_a(wv[k] >> 16, e_lo)], 1u);
+    }
+    if (blockIdx.x == 0) {
+        for (uint64_t i = n8 * 8 + 2 * threadIdx.x; i < n; i += 2 * blockDim.x) {
+            const uint32_t b = i + 1 < n ? pair_a(in[i + 1], e_lo) : 0u;
+            atomicAdd(&h[w][pair_a(in[i], e_lo) * 16 + b], 1u);
+        }
+    }
+    __syncthreads();
+    uint32_t t = 0;
+#pragma unroll
+    for (int k = 0; k < 8; k++) t += h[k][threadIdx.x];
+    if (t) atomicAdd(&pcounts[threadIdx.x], static_cast<unsigned long long>(t));
+}
+
+// 3c. per-chunk reverse rANS over exponent pairs, then the escape list ------
+__global__ void __launch_bounds__(kEncWarps * 32) xc_enc_chunks_pair_kernel(
+    const uint16_t *__restrict__ in, uint64_t n, uint32_t ce, uint32_t nc, int prec,
+    const uint32_t *__restrict__ enc_tab, const uint32_t *aux, uint8_t *__restrict__ slots, uint64_t slot_b,
+    uint32_t *__restrict__ rec_words, uint32_t *__restrict__ rec_esc) {
+    __shared__ uint32_t s_tab[256];
+    s_tab[threadIdx.x] = enc_tab[threadIdx.x];
+    __syncthreads();
+    const uint32_t e_lo = *aux;
+    const uint32_t lane = threadIdx.x & 31;
+    const uint32_t c = blockIdx.x * kEncWarps + (threadIdx.x >> 5);
+    if (c >= nc) return;
+    const uint32_t P = static_cast<uint32_t>(prec);
+    const uint64_t e0 = static_cast<uint64_t>(c) * ce;
+    const uint32_t cn = (n - e0) < ce ? static_cast<uint32_t>(n - e0) : ce;
+    const uint16_t *src = in + e0;
+    uint8_t *slot = slots + static_cast<uint64_t>(c) * slot_b;
+    uint16_t *wend = reinterpret_cast<uint16_t *>(slot + slot_b);
+    const uint32_t gt = lanemask_gt_e();
+    uint32_t lt;
+    asm("mov.u32 %0, %%lanemask_lt;" : "=r"(lt));
+    uint32_t x = kRansL, cur = 0;
+    const uint32_t G = cn >> 8, rem = cn & 255;
+
+    auto enc = [&](uint32_t sym, bool active) {
+        const uint32_t t = s_tab[sym];
+        const uint32_t f = t & 0xFFFF, cf = t >> 16;
+        const bool emit = active && (static_cast<uint64_t>(x) >= (static_cast<uint64_t>(f) << (32 - P)));
+        const uint32_t m = __ballot_sync(kFull, emit);
+        if (emit) {
+            wend[-1 - static_cast<int64_t>(cur + __popc(m & gt))] = static_cast<uint16_t>(x & 0xFFFF);
+            x >>= 16;
+        }
+        cur += __popc(m);
+        if (active) {
+            const uint32_t q = x / f;
+            x = (q << P) + (x - q * f) + cf;
+        }
+    };
+    if (rem) {
+        const uint32_t eb = G * 256 + lane * 8;
+        for (int jj = 3; jj >= 0; jj--) {
+            const uint32_t e = lane * 8 + 2 * jj;
+            const bool act = e < rem;
+            const uint32_t a = act ? pair_a(src[eb + 2 * jj], e_lo) : 0u;
+            const uint32_t b = e + 1 < rem ? pair_a(src[eb + 2 * jj + 1], e_lo) : 0u;
+            enc(a * 16 + b, act);
+        }
+    }
+    for (int g = static_cast<int>(G) - 1; g >= 0; g--) {
+        const uint4 v = reinterpret_cast<const uint4 *>(src + g * 256 + lane * 8)[0];
+        enc(pair_a(v.w & 0xFFFF, e_lo) * 16 + pair_a(v.w >> 16, e_lo), true);
+        enc(pair_a(v.z & 0xFFFF, e_lo) * 16 + pair_a(v.z >> 16, e_lo), true);
+        enc(pair_a(v.y & 0xFFFF, e_lo) * 16 + pair_a(v.y >> 16, e_lo), true);
+        enc(pair_a(v.x & 0xFFFF, e_lo) * 16 + pair_a(v.x >> 16, e_lo), true);
+    }
+    reinterpret_cast<uint32_t *>(slot)[lane] = x;
+    // escape list, forward: per pair-step, lanes in order, first value then second
+    uint8_t *esc = slot + kXcPairRecHdr;
+    uint32_t epos = 0;
+    const uint32_t S2 = (G + (rem ? 1u : 0u)) * 4;
+    for (uint32_t s2 = 0; s2 < S2; s2++) {
+        const uint32_t e = (s2 >> 2) * 256 + lane * 8 + 2 * (s2 & 3);
+        const bool act = e < cn, has_b = e + 1 < cn;
+        const uint32_t v0 = act ? src[e] : 0u, v1 = has_b ? src[e + 1] : 0u;
+        const bool ea = act && pair_a(v0, e_lo) == 15;
+        const bool eb = has_b && pair_a(v1, e_lo) == 15;
+        const uint32_t ba = __ballot_sync(kFull, ea), bb = __ballot_sync(kFull, eb);
+        if (ba | bb) {
+            const uint32_t pa = epos + __popc(ba & lt) + __popc(bb & lt);
+            if (ea) esc[pa] = static_cast<uint8_t>((v0 >> 7) & 0xFF);
+            if (eb) esc[pa + (ea ? 1u : 0u)] = static_cast<uint8_t>((v1 >> 7) & 0xFF);
+            epos += __popc(ba) + __popc(bb);
+        }
+    }
+    if (lane == 0) {
+        rec_words[c] = cur;
+        rec_esc[c] = epos;
     }
 }
 
@@ -364,7 +499,13 @@ __global__ void __launch_bounds__(kEncWarps * 32) xc_enc_chunks_tans_kernel(
 }
 
 // 4. record offsets -----------------------------------------------------------
-__global__ void __launch_bounds__(1024) xc_enc_scan_kernel(const uint32_t *__restrict__ rec_words, uint32_t nc,
+__device__ __forceinline__ uint64_t rec16(const uint32_t *rec_words, const uint32_t *rec_esc, uint32_t c, int coder) {
+    return coder == BS_CODER_RANS_PAIR ? (kXcPairRecHdr + 2ull * rec_words[c] + rec_esc[c] + 15u) >> 4
+                                       : (128ull + 2ull * rec_words[c] + 15u) >> 4;
+}
+
+__global__ void __launch_bounds__(1024) xc_enc_scan_kernel(const uint32_t *__restrict__ rec_words,
+                                                           const uint32_t *__restrict__ rec_esc, int coder, uint32_t nc,
                                                            uint8_t *out, uint64_t chunks_off, uint64_t out_cap,
                                                            unsigned long long *out_len, uint32_t *flags) {
     __shared__ uint64_t s_part[1024];
@@ -372,7 +513,7 @@ __global__ void __launch_bounds__(1024) xc_enc_scan_kernel(const uint32_t *__res
     const uint32_t per = (nc + 1023) / 1024;
     const uint32_t lo = tid * per, hi = min(nc, lo + per);
     uint64_t sum = 0;
-    for (uint32_t c = lo; c < hi; c++) sum += (128u + 2u * rec_words[c] + 15u) >> 4;
+    for (uint32_t c = lo; c < hi; c++) sum += rec16(rec_words, rec_esc, c, coder);
     s_part[tid] = sum;
     __syncthreads();
     for (uint32_t d = 1; d < 1024; d <<= 1) {
@@ -385,7 +526,7 @@ __global__ void __launch_bounds__(1024) xc_enc_scan_kernel(const uint32_t *__res
     uint32_t *tab = reinterpret_cast<uint32_t *>(out + kXcTabOff);
     for (uint32_t c = lo; c < hi; c++) {
         tab[c] = static_cast<uint32_t>(run);
-        run += (128u + 2u * rec_words[c] + 15u) >> 4;
+        run += rec16(rec_words, rec_esc, c, coder);
     }
     if (tid == 1023) {
         const uint64_t total16 = s_part[1023];
@@ -405,6 +546,7 @@ __global__ void __launch_bounds__(1024) xc_enc_scan_kernel(const uint32_t *__res
 // 5. compaction -----------------------------------------------------------------
 __global__ void __launch_bounds__(256) xc_enc_compact_kernel(const uint8_t *__restrict__ slots, uint64_t slot_b,
                                                              const uint32_t *__restrict__ rec_words,
+                                                             const uint32_t *__restrict__ rec_esc,
                                                              uint8_t *out, uint64_t chunks_off,
                                                              const uint32_t *flags, int coder) {
     if (*flags) return;
@@ -415,6 +557,20 @@ __global__ void __launch_bounds__(256) xc_enc_compact_kernel(const uint8_t *__re
     const uint8_t *slot = slots + static_cast<uint64_t>(c) * slot_b;
     if (threadIdx.x < 32)
         reinterpret_cast<uint32_t *>(dst)[threadIdx.x] = reinterpret_cast<const uint32_t *>(slot)[threadIdx.x];
+    if (coder == BS_CODER_RANS_PAIR) {
+        // [states][n_words][n_esc][0][0][words][escapes] zero-padded to 16 B
+        const uint32_t E = rec_esc[c];
+        uint32_t *d32 = reinterpret_cast<uint32_t *>(dst);
+        if (threadIdx.x == 0) { d32[32] = W; d32[33] = E; d32[34] = 0; d32[35] = 0; }
+        const uint16_t *ws = reinterpret_cast<const uint16_t *>(slot + slot_b) - W;
+        uint16_t *wd = reinterpret_cast<uint16_t *>(dst + kXcPairRecHdr);
+        for (uint32_t i = threadIdx.x; i < W; i += blockDim.x) wd[i] = ws[i];
+        const uint8_t *es = slot + kXcPairRecHdr;
+        uint8_t *ed = dst + kXcPairRecHdr + 2ull * W;
+        const uint32_t tail = ((kXcPairRecHdr + 2u * W + E + 15u) & ~15u) - kXcPairRecHdr - 2u * W;
+        for (uint32_t i = threadIdx.x; i < tail; i += blockDim.x) ed[i] = i < E ? es[i] : 0;
+        return;
+    }
     // rANS records hold their words at the end of the slot (written backwards),
     // tANS records right after the lane states (written forwards)
     const uint16_t *ws = coder == BS_CODER_TANS ? reinterpret_cast<const uint16_t *>(slot + 128)
@@ -431,7 +587,10 @@ cudaError_t launch_xc_encode(const uint16_t *d_in, uint64_t n, int coder, int pr
     auto *counts = reinterpret_cast<unsigned long long *>(d_ws + kWsCounts);
     auto *tab = reinterpret_cast<uint32_t *>(d_ws + kWsTab);
     auto *flags = reinterpret_cast<uint32_t *>(d_ws + kWsFlags);
+    auto *aux = reinterpret_cast<uint32_t *>(d_ws + kWsAux);
+    auto *pcounts = reinterpret_cast<unsigned long long *>(d_ws + kWsPairCounts);
     auto *recw = reinterpret_cast<uint32_t *>(d_ws + kWsRec);
+    auto *rece = recw + nc;
     uint8_t *slots = d_ws + slots_off(nc);
     const uint64_t sb = slot_bytes(ce);
     const uint64_t plane_off = rup(kXcTabOff + 4 * (nc + 1), 16);
@@ -445,10 +604,21 @@ cudaError_t launch_xc_encode(const uint16_t *d_in, uint64_t n, int coder, int pr
     int grid = static_cast<int>(want < static_cast<uint64_t>(sms) * 8 ? (want ? want : 1) : static_cast<uint64_t>(sms) * 8);
     xc_enc_hist_kernel<<<grid, 256, 0, s>>>(d_in, n, counts, d_out + plane_off);
     uint16_t *slot_list = reinterpret_cast<uint16_t *>(d_ws + slotlist_off(nc));
-    xc_enc_setup_kernel<<<1, 256, 0, s>>>(counts, n, coder, prec, ce, static_cast<uint32_t>(nc), d_out, tab,
-                                          slot_list);
+    const unsigned long long *qcounts = counts;
+    if (coder == BS_CODER_RANS_PAIR) {
+        e = cudaMemsetAsync(pcounts, 0, 2048, s);
+        if (e != cudaSuccess) return e;
+        xc_enc_window_kernel<<<1, 32, 0, s>>>(counts, aux);
+        xc_enc_pair_hist_kernel<<<grid, 256, 0, s>>>(d_in, n, aux, pcounts);
+        qcounts = pcounts;
+    }
+    xc_enc_setup_kernel<<<1, 256, 0, s>>>(qcounts, n, coder, prec, ce, static_cast<uint32_t>(nc), d_out, tab,
+                                          slot_list, aux);
     const unsigned enc_blocks = static_cast<unsigned>((nc + kEncWarps - 1) / kEncWarps);
-    if (coder == BS_CODER_TANS) {
+    if (coder == BS_CODER_RANS_PAIR) {
+        xc_enc_chunks_pair_kernel<<<enc_blocks, kEncWarps * 32, 0, s>>>(d_in, n, ce, static_cast<uint32_t>(nc), prec,
+                                                                       tab, aux, slots, sb, recw, rece);
+    } else if (coder == BS_CODER_TANS) {
         auto *scr = reinterpret_cast<uint32_t *>(d_ws + tans_scratch_off(nc, ce));
         xc_enc_chunks_tans_kernel<<<enc_blocks, kEncWarps * 32, 0, s>>>(d_in, n, ce, static_cast<uint32_t>(nc), prec,
                                                                        tab, slot_list, slots, sb, scr, recw);
@@ -456,10 +626,10 @@ cudaError_t launch_xc_encode(const uint16_t *d_in, uint64_t n, int coder, int pr
         xc_enc_chunks_kernel<<<enc_blocks, kEncWarps * 32, 0, s>>>(d_in, n, ce, static_cast<uint32_t>(nc), prec,
                                                                   tab, slots, sb, recw);
     }
-    xc_enc_scan_kernel<<<1, 1024, 0, s>>>(recw, static_cast<uint32_t>(nc), d_out, chunks_off, out_cap,
+    xc_enc_scan_kernel<<<1, 1024, 0, s>>>(recw, rece, coder, static_cast<uint32_t>(nc), d_out, chunks_off, out_cap,
                                           reinterpret_cast<unsigned long long *>(d_out_len), flags);
-    xc_enc_compact_kernel<<<static_cast<unsigned>(nc), 256, 0, s>>>(slots, sb, recw, d_out, chunks_off, flags,
-                                                                    coder);
+    xc_enc_compact_kernel<<<static_cast<unsigned>(nc), 256, 0, s>>>(slots, sb, recw, rece, d_out, chunks_off,
+                                                                    flags, coder);
     (void)ws_bytes;
     return cudaGetLastError();
 }

@@ -23,7 +23,7 @@ from . import _lib
 DEFAULT_CHUNK_ELEMS = 65536   # 128 KiB of bf16 per chunk (one warp-state group)
 DEFAULT_PREC = 12             # M = 4096
 
-CODERS = {"rans": _lib.CODER_RANS, "tans": _lib.CODER_TANS}
+CODERS = {"rans": _lib.CODER_RANS, "tans": _lib.CODER_TANS, "pair": _lib.CODER_RANS_PAIR}
 
 
 def _as_cuda(t: torch.Tensor, name: str) -> torch.Tensor:

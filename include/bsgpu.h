@@ -50,6 +50,7 @@ extern "C" {
 /* bf16_exp_chunked_v1 coders */
 #define BS_CODER_RANS        0
 #define BS_CODER_TANS        1
+#define BS_CODER_RANS_PAIR   2   /* rANS over exponent pairs (one step per two values) */
 
 typedef struct bs_plan bs_plan;
 
@@ -105,7 +106,7 @@ int bs_plan_destroy(bs_plan *plan);
  * HBM for its own arena or KV cache (a fresh cudaMalloc can fail there), or a
  * latency-critical path where cudaMalloc/cudaFree would synchronise the whole
  * device.  Its scratch (descriptors, decode tables, status words; about
- * 130 KiB) is a static device array that every GPU loading the library holds
+ * 260 KiB) is a static device array that every GPU loading the library holds
  * until the process exits.  The first call on a device resolves that array's
  * address (with the device current); make that first call before any stream
  * capture.  All calls share the array, so calls whose GPU work overlaps race:

@@ -865,6 +865,12 @@ int bso_tans_decode(const uint8_t *blob, int64_t len, int64_t n_weights, uint16_
 /*   chunks_off = plane_off + rup16(n): per chunk [u32 init[32]][u16 words]  */
 /*                zero-padded to 16 bytes; blob_bytes = end of last record.  */
 /* Element e of a chunk belongs to lane (e%256)/8 at step (e/256)*8 + e%8.  */
+/* Coder 2 (rANS over exponent pairs): header u32 at 28 = e_lo; exponent e  */
+/* maps to a = e - e_lo when 0 <= e - e_lo <= 14, else a = 15 (escape); the */
+/* symbol of elements (2k, 2k+1) is a*16 + b (b = 0 for a missing second    */
+/* element); lane l codes pair-steps s2 (element (s2/4)*256 + l*8 +         */
+/* 2*(s2%4)); a chunk record is [u32 init[32]][u32 n_words][u32 n_esc][u32  */
+/* 0][u32 0][u16 words][u8 escape exponents, in step/lane/a-then-b order].  */
 /* ======================================================================== */
 #define XC_HDR 64
 #define XC_FREQ_OFF 64
@@ -1050,10 +1056,122 @@ static int64_t xc_encode_chunk(const uint8_t *ex, int64_t cn, int coder, int P, 
     return bytes;
 }
 
+/* ---- coder 2: rANS over exponent pairs ---------------------------------- */
+static int xc2_window(const int64_t *hist) {
+    int best = 0;
+    int64_t bm = -1;
+    for (int w = 0; w + 14 < 256; w++) {
+        int64_t m = 0;
+        for (int k = 0; k < 15; k++) m += hist[w + k];
+        if (m > bm) { bm = m; best = w; }
+    }
+    return best;
+}
+
+static inline uint32_t xc2_a(uint32_t e, int e_lo) {
+    int d = (int)e - e_lo;
+    return (d >= 0 && d <= 14) ? (uint32_t)d : 15u;
+}
+
+/* pair symbol of pair-step s2 for lane l, or -1 if inactive */
+static inline int xc2_sym(const uint8_t *ex, int64_t cn, int e_lo, int64_t s2, int l, int64_t *e_out) {
+    int64_t e = (s2 >> 2) * 256 + l * 8 + 2 * (s2 & 3);
+    if (e >= cn) return -1;
+    uint32_t a = xc2_a(ex[e], e_lo);
+    uint32_t b = (e + 1 < cn) ? xc2_a(ex[e + 1], e_lo) : 0u;
+    *e_out = e;
+    return (int)(a * 16 + b);
+}
+
+static int64_t xc2_encode_chunk(const uint8_t *ex, int64_t cn, int e_lo, int P, const uint16_t *freq,
+                                const uint32_t *cum, uint8_t *rec, int64_t cap) {
+    const int64_t S2 = ((cn + 255) / 256) * 4;
+    uint64_t x[XC_LANES];
+    vec16 words = {0, 0, 0};
+    for (int l = 0; l < XC_LANES; l++) x[l] = RANS_L;
+    for (int64_t s2 = S2 - 1; s2 >= 0; s2--) {
+        for (int l = XC_LANES - 1; l >= 0; l--) {
+            int64_t e;
+            int sym = xc2_sym(ex, cn, e_lo, s2, l, &e);
+            if (sym < 0) continue;
+            uint64_t f = freq[sym], cf = cum[sym];
+            if (x[l] >= (f << (32 - P))) { v16_push(&words, (uint16_t)(x[l] & 0xFFFF)); x[l] >>= 16; }
+            x[l] = ((x[l] / f) << P) + (x[l] % f) + cf;
+        }
+    }
+    for (int64_t a = 0, b = words.n - 1; a < b; a++, b--) { uint16_t t = words.v[a]; words.v[a] = words.v[b]; words.v[b] = t; }
+    /* escapes, forward */
+    int64_t n_esc = 0;
+    uint8_t *esc = (uint8_t *)malloc((size_t)(cn + 1));
+    for (int64_t s2 = 0; s2 < S2; s2++)
+        for (int l = 0; l < XC_LANES; l++) {
+            int64_t e;
+            int sym = xc2_sym(ex, cn, e_lo, s2, l, &e);
+            if (sym < 0) continue;
+            if ((sym >> 4) == 15) esc[n_esc++] = ex[e];
+            if (e + 1 < cn && (sym & 15) == 15) esc[n_esc++] = ex[e + 1];
+        }
+    int64_t bytes = rup16(144 + 2 * words.n + n_esc);
+    if (bytes > cap) { free(words.v); free(esc); return BSO_E_CAP; }
+    memset(rec, 0, (size_t)bytes);
+    for (int l = 0; l < XC_LANES; l++) wr32(rec + 4 * l, (uint32_t)x[l]);
+    wr32(rec + 128, (uint32_t)words.n);
+    wr32(rec + 132, (uint32_t)n_esc);
+    for (int64_t k = 0; k < words.n; k++) wr16(rec + 144 + 2 * k, words.v[k]);
+    memcpy(rec + 144 + 2 * words.n, esc, (size_t)n_esc);
+    free(words.v);
+    free(esc);
+    return bytes;
+}
+
+static int xc2_decode_chunk(const uint8_t *rec, int64_t rec_bytes, int64_t cn, int e_lo, int P,
+                            const uint32_t *tab /* sym | f<<16 */, const uint32_t *cumf,
+                            const uint8_t *plane, uint16_t *out) {
+    if (rec_bytes < 144) return BSO_E_CORRUPT;
+    const int64_t n_words = rd32(rec + 128), n_esc = rd32(rec + 132);
+    if (rd32(rec + 136) || rd32(rec + 140)) return BSO_E_CORRUPT;
+    if (144 + 2 * n_words + n_esc > rec_bytes || rec_bytes - (144 + 2 * n_words + n_esc) >= 16) return BSO_E_CORRUPT;
+    const uint8_t *wd = rec + 144, *esc = rec + 144 + 2 * n_words;
+    const uint32_t M = 1u << P;
+    uint32_t x[XC_LANES];
+    for (int l = 0; l < XC_LANES; l++) x[l] = rd32(rec + 4 * l);
+    int64_t wp = 0, ep = 0;
+    const int64_t S2 = ((cn + 255) / 256) * 4;
+    for (int64_t s2 = 0; s2 < S2; s2++) {
+        for (int l = 0; l < XC_LANES; l++) {
+            int64_t e = (s2 >> 2) * 256 + l * 8 + 2 * (s2 & 3);
+            if (e >= cn) continue;
+            uint32_t slot = x[l] & (M - 1);
+            uint32_t t = tab[slot];
+            uint32_t sym = t & 0xFFFF, f = t >> 16;
+            x[l] = f * (x[l] >> P) + slot - cumf[sym];
+            uint32_t a = sym >> 4, b = sym & 15;
+            uint32_t ea, eb = 0;
+            if (a == 15) { if (ep >= n_esc) return BSO_E_CORRUPT; ea = esc[ep++]; } else ea = (uint32_t)e_lo + a;
+            if (e + 1 < cn) {
+                if (b == 15) { if (ep >= n_esc) return BSO_E_CORRUPT; eb = esc[ep++]; } else eb = (uint32_t)e_lo + b;
+            }
+            uint8_t sm = plane[e];
+            out[e] = (uint16_t)(((uint32_t)(sm & 0x80) << 8) | (ea << 7) | (sm & 0x7F));
+            if (e + 1 < cn) {
+                sm = plane[e + 1];
+                out[e + 1] = (uint16_t)(((uint32_t)(sm & 0x80) << 8) | (eb << 7) | (sm & 0x7F));
+            }
+            if (x[l] < RANS_L) {
+                if (wp >= n_words) return BSO_E_CORRUPT;
+                x[l] = (x[l] << 16) | rd16(wd + 2 * wp++);
+            }
+        }
+    }
+    for (int l = 0; l < XC_LANES; l++) if (x[l] != RANS_L) return BSO_E_CORRUPT;
+    if (wp != n_words || ep != n_esc) return BSO_E_CORRUPT;
+    return BSO_OK;
+}
+
 int64_t bso_xc_encode(const uint16_t *w, int64_t n, int coder, int prec, uint32_t chunk_elems,
                       uint8_t *out, int64_t cap) {
     if (n == 0) return 0;
-    if ((coder != 0 && coder != 1) || prec < 8 || prec > 12 || chunk_elems == 0 || (chunk_elems & 255))
+    if (coder < 0 || coder > 2 || prec < 8 || prec > 12 || chunk_elems == 0 || (chunk_elems & 255))
         return BSO_E_ARG;
     int64_t nc64 = (n + chunk_elems - 1) / chunk_elems;
     if (nc64 > 0x7FFFFFFFll) return BSO_E_ARG;
@@ -1063,7 +1181,23 @@ int64_t bso_xc_encode(const uint16_t *w, int64_t n, int coder, int prec, uint32_
     if (!ex) return BSO_E_NOMEM;
     for (int64_t i = 0; i < n; i++) { ex[i] = (uint8_t)((w[i] >> 7) & 0xFF); counts[ex[i]]++; }
     uint16_t freq[256];
-    bso_xc_quantise(counts, prec, freq);
+    int e_lo = 0;
+    if (coder == 2) {
+        /* pair-symbol histogram over every chunk (a missing second element is b = 0) */
+        e_lo = xc2_window(counts);
+        int64_t pc[256] = {0};
+        for (uint32_t k = 0; k < nc; k++) {
+            int64_t e0 = (int64_t)k * chunk_elems;
+            int64_t cn = n - e0 < chunk_elems ? n - e0 : chunk_elems;
+            for (int64_t e = 0; e < cn; e += 2) {
+                uint32_t a = xc2_a(ex[e0 + e], e_lo), b = e + 1 < cn ? xc2_a(ex[e0 + e + 1], e_lo) : 0u;
+                pc[a * 16 + b]++;
+            }
+        }
+        bso_xc_quantise(pc, prec, freq);
+    } else {
+        bso_xc_quantise(counts, prec, freq);
+    }
     uint32_t cum[256];
     uint32_t c = 0;
     for (int s = 0; s < 256; s++) { cum[s] = c; c += freq[s]; }
@@ -1086,7 +1220,8 @@ int64_t bso_xc_encode(const uint16_t *w, int64_t n, int coder, int prec, uint32_
         wr32(out + XC_TAB_OFF + 4 * k, (uint32_t)((pos - chunks_off) / 16));
         int64_t e0 = (int64_t)k * chunk_elems;
         int64_t cn = n - e0 < chunk_elems ? n - e0 : chunk_elems;
-        int64_t b = xc_encode_chunk(ex + e0, cn, coder, prec, freq, cum, slot_list, out + pos, cap - pos);
+        int64_t b = coder == 2 ? xc2_encode_chunk(ex + e0, cn, e_lo, prec, freq, cum, out + pos, cap - pos)
+                               : xc_encode_chunk(ex + e0, cn, coder, prec, freq, cum, slot_list, out + pos, cap - pos);
         if (b < 0) { rc = (int)b; break; }
         pos += b;
     }
@@ -1102,7 +1237,7 @@ int64_t bso_xc_encode(const uint16_t *w, int64_t n, int coder, int prec, uint32_
     wr32(out + 16, chunk_elems);
     wr32(out + 20, nc);
     wr32(out + 24, XC_LANES);
-    wr32(out + 28, 0);
+    wr32(out + 28, (uint32_t)e_lo);
     wr64(out + 32, (uint64_t)chunks_off);
     wr64(out + 40, (uint64_t)plane_off);
     wr64(out + 48, (uint64_t)total);
@@ -1122,8 +1257,10 @@ int bso_xc_decode(const uint8_t *blob, int64_t len, int64_t n_weights, uint16_t 
     int64_t chunks_off = (int64_t)rd64(blob + 32), plane_off = (int64_t)rd64(blob + 40);
     int64_t total = (int64_t)rd64(blob + 48);
     if (n != n_weights) return BSO_E_COUNT;
-    if ((coder != 0 && coder != 1) || P < 8 || P > 12 || lanes != XC_LANES || ce == 0 || (ce & 255))
+    const uint32_t aux = rd32(blob + 28);
+    if (coder < 0 || coder > 2 || P < 8 || P > 12 || lanes != XC_LANES || ce == 0 || (ce & 255))
         return BSO_E_CORRUPT;
+    if (coder == 2 ? aux > 241 : aux != 0) return BSO_E_CORRUPT;
     if ((int64_t)nc != (n + ce - 1) / ce) return BSO_E_CORRUPT;
     if (plane_off != rup16(XC_TAB_OFF + 4 * ((int64_t)nc + 1)) || chunks_off != plane_off + rup16(n) ||
         (total & 15) || total < chunks_off)
@@ -1142,6 +1279,11 @@ int bso_xc_decode(const uint8_t *blob, int64_t len, int64_t n_weights, uint16_t 
             if (freq[s] >= M) { free(tab); return BSO_E_CORRUPT; }
             for (uint32_t j = 0; j < freq[s]; j++) tab[cum[s] + j] = (uint32_t)s | ((uint32_t)freq[s] << 8) | (j << 20);
         }
+    } else if (coder == 2) {
+        for (int s = 0; s < 256; s++) {
+            if (freq[s] >= M) { free(tab); return BSO_E_CORRUPT; }
+            for (uint32_t j = 0; j < freq[s]; j++) tab[cum[s] + j] = (uint32_t)s | ((uint32_t)freq[s] << 16);
+        }
     } else {
         slot_list = (uint16_t *)malloc(sizeof(uint16_t) * M);
         uint32_t cum2[256];
@@ -1154,6 +1296,12 @@ int bso_xc_decode(const uint8_t *blob, int64_t len, int64_t n_weights, uint16_t 
         int64_t b = chunks_off + 16 * (int64_t)rd32(blob + XC_TAB_OFF + 4 * (k + 1));
         if (b < a + 128 || b > total) { rc = BSO_E_CORRUPT; break; }
         const uint8_t *rec = blob + a;
+        if (coder == 2) {
+            int64_t e0c = (int64_t)k * ce;
+            int64_t cnc = n - e0c < ce ? n - e0c : ce;
+            rc = xc2_decode_chunk(rec, b - a, cnc, (int)aux, P, tab, cum, plane + e0c, out + e0c);
+            continue;
+        }
         const int64_t navail = (b - a - 128) / 2;
         const uint8_t *wd = rec + 128;
         int64_t e0 = (int64_t)k * ce;

@@ -1,0 +1,137 @@
+"""GPU parity of coder 2 of bf16_exp_chunked_v1: rANS over exponent pairs
+with a 15-exponent window and per-chunk escape bytes (sm_100a).
+
+The checker is the CPU oracle (oracle/bs_oracle.c, ``xc2_*``); decode must
+reproduce the raw bf16 bytes exactly and the device encoder must write the
+oracle's bytes.  Integer/byte work: every comparison is bit-exact.
+"""
+from __future__ import annotations
+
+import hashlib
+import struct
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+from oracle import oracle as O  # noqa: E402
+from tests.conftest import golden_bytes  # noqa: E402
+
+
+def _dev(b: bytes):
+    return torch.from_numpy(np.frombuffer(b, dtype=np.uint8).copy()).cuda()
+
+
+def _decode(blob: bytes, n: int, ce: int) -> bytes:
+    from bigsmall_b200 import gpu
+    out = torch.empty(n, dtype=torch.bfloat16, device="cuda")
+    gpu.decode_xc_into(_dev(blob), out, ce)
+    return out.cpu().view(torch.uint8).numpy().tobytes()
+
+
+def _normal(n, seed, scale=0.02) -> bytes:
+    g = torch.Generator().manual_seed(seed)
+    return (torch.randn(n, generator=g) * scale).to(torch.bfloat16).view(torch.uint8).numpy().tobytes()
+
+
+def _uniform(n, seed) -> bytes:
+    return np.random.default_rng(seed).integers(0, 1 << 16, n, dtype=np.uint16).tobytes()
+
+
+def _wide(n, seed) -> bytes:
+    """Heavy-tailed values: a few percent of exponents fall outside any 15-wide window."""
+    rng = np.random.default_rng(seed)
+    w = (rng.standard_normal(n) * np.exp(rng.standard_normal(n) * 3)).astype(np.float32)
+    return (w.view(np.uint32) >> 16).astype(np.uint16).tobytes()
+
+
+def test_decode_golden_inputs(manifest):
+    for name, c in manifest["cases"].items():
+        raw = golden_bytes(f"{name}.raw")
+        for ce in (256, 65536):
+            for prec in (11, 12):
+                blob = O.xc_encode(raw, 2, prec, ce)
+                assert hashlib.md5(_decode(blob, c["n"], ce)).hexdigest() == c["raw_md5"], (name, ce, prec)
+
+
+@pytest.mark.parametrize("n", [1, 2, 3, 31, 255, 256, 257, 4095, 4097, 65535, 65536, 65537, 300_001])
+def test_decode_ragged_sizes(n):
+    for make in (_normal, _wide, _uniform):
+        raw = make(n, n)
+        for ce in (256, 65536):
+            blob = O.xc_encode(raw, 2, 12, ce)
+            assert _decode(blob, n, ce) == raw, (make.__name__, n, ce)
+
+
+def test_device_encoder_matches_oracle_bytes(manifest):
+    from bigsmall_b200 import gpu
+    cases = [golden_bytes(f"{name}.raw") for name in manifest["cases"]]
+    cases += [_normal(n, n) for n in (1, 3, 257, 65536, 200_003)]
+    cases += [_wide(n, n) for n in (513, 100_001)]
+    cases += [_uniform(70_001, 4)]
+    for raw in cases:
+        x = torch.from_numpy(np.frombuffer(raw, dtype=np.int16).copy()).view(torch.bfloat16).cuda()
+        for ce in (256, 65536):
+            for prec in (11, 12):
+                d = gpu.encode_xc(x, coder="pair", prec=prec, chunk_elems=ce).cpu().numpy().tobytes()
+                assert d == O.xc_encode(raw, 2, prec, ce), (len(raw) // 2, ce, prec)
+
+
+def test_device_roundtrip_full_size_config1(manifest):
+    from bigsmall_b200 import gpu
+    from tests.golden.make_golden import c1_tensor
+    full = manifest["full_size"]["c1"]
+    x = c1_tensor().cuda()
+    blob = gpu.encode_xc(x, coder="pair")
+    out = torch.empty_like(x)
+    gpu.decode_xc_into(blob, out, gpu.DEFAULT_CHUNK_ELEMS)
+    assert hashlib.md5(out.cpu().view(torch.uint8).numpy().tobytes()).hexdigest() == full["raw_md5"]
+    rans = gpu.encode_xc(x, coder="rans")
+    # the pair coder spends at most a fraction of a percent more than per-exponent rANS
+    assert blob.numel() <= rans.numel() * 1.005
+
+
+def test_mixed_coders_in_one_plan():
+    from bigsmall_b200 import gpu
+    specs = [(300_001, 0, 65536), (40_000, 2, 256), (1, 2, 256), (123_457, 1, 4096), (65536 * 2, 2, 65536)]
+    entries, outs, raws = [], [], []
+    for i, (n, coder, ce) in enumerate(specs):
+        raw = _wide(n, i) if i % 2 else _normal(n, i)
+        blob = _dev(O.xc_encode(raw, coder, 12, ce))
+        out = torch.empty(n, dtype=torch.bfloat16, device="cuda")
+        entries.append((blob, out, ce))
+        outs.append(out)
+        raws.append(raw)
+    with gpu.XcPlan(entries) as plan:
+        for _ in range(2):
+            for o in outs:
+                o.fill_(0)
+            plan.run()
+            for raw, o in zip(raws, outs):
+                assert o.cpu().view(torch.uint8).numpy().tobytes() == raw
+
+
+def test_corrupt_pair_records_raise_without_fault():
+    from bigsmall_b200 import gpu
+    from bigsmall_b200.exceptions import BsCorruptError
+    n = 100_000
+    raw = _wide(n, 11)
+    good = O.xc_encode(raw, 2, 12, 4096)
+    co = struct.unpack_from("<Q", good, 32)[0]
+    ne = struct.unpack_from("<I", good, co + 132)[0]
+    assert ne > 0
+    variants = {}
+    b = bytearray(good); struct.pack_into("<I", b, 28, 250); variants["window"] = (bytes(b), 0x01)
+    b = bytearray(good); struct.pack_into("<I", b, co + 132, ne - 1); variants["n_esc"] = (bytes(b), 0x08)
+    b = bytearray(good); struct.pack_into("<I", b, co + 136, 1); variants["reserved"] = (bytes(b), 0x08)
+    b = bytearray(good); b[co + 3] ^= 0x40; variants["lane_state"] = (bytes(b), 0x18)
+    b = bytearray(good); struct.pack_into("<I", b, co + 128, 1 << 20); variants["n_words"] = (bytes(b), 0x08)
+    for name, (blob, bits) in variants.items():
+        out = torch.empty(n, dtype=torch.bfloat16, device="cuda")
+        with pytest.raises(BsCorruptError) as ei:
+            gpu.decode_xc_into(_dev(blob), out, 4096)
+        st = ei.value.device_status[0]
+        assert st and (st & bits), (name, hex(st))
+    assert _decode(good, n, 4096) == raw

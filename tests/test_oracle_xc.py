@@ -21,7 +21,7 @@ def md5(b):
     return hashlib.md5(b).hexdigest()
 
 
-@pytest.mark.parametrize("coder", [0, 1])
+@pytest.mark.parametrize("coder", [0, 1, 2])
 @pytest.mark.parametrize("prec", [10, 11, 12])
 @pytest.mark.parametrize("chunk", [256, 4096, 65536])
 def test_xc_roundtrip_golden_inputs(manifest, coder, prec, chunk):
@@ -61,7 +61,7 @@ def test_xc_quantise_rules():
     assert f.sum() == 256 and (f[1:] >= 1).all() and f[0] == 0
 
 
-@pytest.mark.parametrize("coder", [0, 1])
+@pytest.mark.parametrize("coder", [0, 1, 2])
 def test_xc_corruption_detected(coder):
     rng = np.random.default_rng(1)
     raw = (rng.standard_normal(20000).astype(np.float32).view(np.uint32) >> 16).astype(np.uint16).tobytes()
@@ -81,3 +81,58 @@ def test_xc_corruption_detected(coder):
     bad[co + 5] ^= 0x5A
     with pytest.raises(O.OracleError):
         O.xc_decode(bytes(bad), n)
+
+
+def _u16(n, seed):
+    return np.random.default_rng(seed).integers(0, 1 << 16, n, dtype=np.uint16).tobytes()
+
+
+@pytest.mark.parametrize("n", [1, 2, 3, 255, 256, 257, 4095, 4097, 65537])
+def test_xc_pair_coder_escapes_and_ragged_tails(n):
+    """Coder 2 codes exponent pairs inside a 15-wide window, escaping the rest
+    byte by byte; uniformly random words put most exponents outside it."""
+    for raw in (_u16(n, n), (np.random.default_rng(n).standard_normal(n).astype(np.float32).view(np.uint32)
+                             >> 16).astype(np.uint16).tobytes()):
+        for ce in (256, 4096):
+            blob = O.xc_encode(raw, 2, 12, ce)
+            assert blob[6] == 2
+            assert O.xc_decode(blob, n) == raw, (n, ce)
+
+
+def test_xc_pair_coder_window_and_record_layout():
+    rng = np.random.default_rng(5)
+    w = (rng.standard_normal(50000) * 0.02).astype(np.float32)
+    raw = (w.view(np.uint32) >> 16).astype(np.uint16)
+    blob = O.xc_encode(raw.tobytes(), 2, 12, 4096)
+    e_lo = struct.unpack_from("<I", blob, 28)[0]
+    ex = (raw >> 7) & 0xFF
+    hist = np.bincount(ex, minlength=256)
+    win = [int(hist[w:w + 15].sum()) for w in range(242)]
+    assert e_lo == int(np.argmax(win))                     # first maximal window
+    co = struct.unpack_from("<Q", blob, 32)[0]
+    ends = np.frombuffer(blob, dtype="<u4", count=14, offset=576)
+    n_esc_total = 0
+    for k in range(13):
+        rec = co + 16 * int(ends[k])
+        size = 16 * int(ends[k + 1] - ends[k])
+        nw, ne, z0, z1 = struct.unpack_from("<IIII", blob, rec + 128)
+        assert (z0, z1) == (0, 0)
+        assert 144 + 2 * nw + ne <= size < 144 + 2 * nw + ne + 16
+        n_esc_total += ne
+    outside = int(((ex < e_lo) | (ex > e_lo + 14)).sum())
+    assert n_esc_total == outside
+
+
+def test_xc_pair_coder_bad_escape_count_detected():
+    raw = _u16(20000, 9)
+    blob = bytearray(O.xc_encode(raw, 2, 12, 4096))
+    co = struct.unpack_from("<Q", blob, 32)[0]
+    ne = struct.unpack_from("<I", blob, co + 132)[0]
+    assert ne > 0
+    struct.pack_into("<I", blob, co + 132, ne - 1)
+    with pytest.raises(O.OracleError):
+        O.xc_decode(bytes(blob), 20000)
+    bad = bytearray(O.xc_encode(raw, 2, 12, 4096))
+    struct.pack_into("<I", bad, 28, 300)                  # window base out of range
+    with pytest.raises(O.OracleError):
+        O.xc_decode(bytes(bad), 20000)

@@ -39,7 +39,7 @@ def _blob(x, coder, ce):
 def _cases(seed0):
     """(blob, n_total, chunk_elems, chunk_begin, chunk_count) per tensor."""
     specs = [(300_001, 0, 65536, 0, 0), (4096, 1, 256, 0, 0), (1_000_003, 0, 4096, 10, 50),
-             (77, 1, 256, 0, 0), (200_000, 0, 65536, 1, 0)]
+             (77, 1, 256, 0, 0), (200_000, 0, 65536, 1, 0), (150_001, 2, 4096, 3, 20), (9_999, 2, 256, 0, 0)]
     out = []
     for i, (n, coder, ce, c0, cc) in enumerate(specs):
         x = _tensor(n, seed0 + i, scale=0.01 * (i + 1))
