@@ -222,7 +222,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--chunk-elems", type=int, default=None)
-    ap.add_argument("--coder", default="rans")
+    ap.add_argument("--coder", default="pair", choices=["rans", "tans", "pair"])
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=8.0)
@@ -381,7 +381,7 @@ def main():
         _, d, nb = loader.layout[name]
         entries.append((loader.dev_data[d:d + nb], loader.out[name].reshape(-1).view(torch.int16), ce,
                         math.prod(m["shape"]), c0, cc))
-    plan = gpu.XcPlan(entries, device=local)
+    plan = gpu.XcPlan(entries, device=local, coders=a.coder)
     for _ in range(a.warmup):
         plan.decode(stream)
     plan.check(stream)
@@ -426,7 +426,8 @@ def main():
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_source": f"hbm_gbs of {peak_kind}",
                          "traffic": traffic,
-                         "kernel": "xc_prepare_kernel + xc_decode_kernel (one plan launch pair per step)",
+                         "kernel": f"{'xc_decode_pair_kernel' if a.coder == 'pair' else 'xc_decode_kernel'} "
+                                   "(+ xc_prepare_kernel: one plan launch pair per step, timed together)",
                          "algorithmic_bytes_per_step": algo_bytes},
             "e2e": None if e2e_ms is None else {
                 "value": round(2 * total_elems / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
@@ -501,7 +502,7 @@ def bench_kv(a, torch, dev, world, rank, dist, local):
     ln = lens[:, 0].tolist()
     blobs = [o[:int(l)] for o, l in zip(outs, ln)]
     dec = [torch.empty_like(x) for x in kv]
-    plan = gpu.XcPlan([(bl, d.view(torch.int16), ce) for bl, d in zip(blobs, dec)], device=local)
+    plan = gpu.XcPlan([(bl, d.view(torch.int16), ce) for bl, d in zip(blobs, dec)], device=local, coders=a.coder)
     dec_ms = _timed(torch, lambda: plan.decode(stream), a.steps, a.warmup, stream)
     plan.check(stream)
     ok = all(torch.equal(x.view(torch.int16), d.view(torch.int16)) for x, d in zip(kv, dec))
@@ -560,7 +561,7 @@ def bench_sweep(a, torch, dev, world, rank, dist, local):
                 ce = cbytes // 2
                 blob = gpu.encode_xc(x, coder=coder, chunk_elems=ce)
                 out = torch.empty_like(x)
-                plan = gpu.XcPlan([(blob, out.view(torch.int16), ce)], device=local)
+                plan = gpu.XcPlan([(blob, out.view(torch.int16), ce)], device=local, coders=coder)
                 ms = _timed(torch, lambda: plan.decode(stream), a.steps, a.warmup, stream)
                 plan.check(stream)
                 ok = torch.equal(out.view(torch.int16), x.view(torch.int16))

@@ -45,7 +45,7 @@ class XcTensor(ctypes.Structure):
         ("chunk_elems", ctypes.c_uint32),
         ("chunk_begin", ctypes.c_uint32),
         ("chunk_count", ctypes.c_uint32),
-        ("reserved", ctypes.c_uint32),
+        ("coder_mask", ctypes.c_uint32),
     ]
 
 

@@ -1,4 +1,4 @@
-"""``bf16_exp_chunked_v1``: chunked exponent rANS/tANS + raw sign|mantissa plane.
+"""``bf16_exp_chunked_v1``: chunked exponent rANS/tANS/pair-rANS + raw sign|mantissa plane.
 
 Host-bytes front-end of the device codec (the format is described in
 ``bigsmall_b200/csrc/common.cuh``).  ``decode`` uploads the blob, decodes on the
@@ -23,7 +23,7 @@ def _device(device=None) -> torch.device:
     return torch.device(device)
 
 
-def encode(raw: bytes, coder: str = "rans", prec: int = gpu.DEFAULT_PREC,
+def encode(raw: bytes, coder: str = gpu.DEFAULT_CODER, prec: int = gpu.DEFAULT_PREC,
            chunk_elems: int = gpu.DEFAULT_CHUNK_ELEMS, device=None, **_) -> tuple[bytes, dict]:
     if len(raw) % 2 != 0:
         raise ValueError(f"BF16 byte length must be even, got {len(raw)}")
@@ -48,7 +48,7 @@ def decode_to_device(blob, extras: dict, n_weights: int, device=None) -> torch.T
     if d.data_ptr() % 16:
         d = d.clone()
     ce = int((extras or {}).get("chunk_elems", gpu.DEFAULT_CHUNK_ELEMS))
-    gpu.decode_xc_into(d, out, ce)
+    gpu.decode_xc_into(d, out, ce, coder=(extras or {}).get("coder"))
     return out
 
 

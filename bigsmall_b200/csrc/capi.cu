@@ -79,6 +79,7 @@ struct bs_plan {
     XcTensorDev *d_tens = nullptr;
     XcItem *d_items = nullptr;
     int n_items = 0;
+    uint32_t coders = 0;        // decode kernels to launch (bit per coder)
     uint32_t *d_tables = nullptr;
     // bf16_parallel_v1
     const uint8_t *d_blob = nullptr;
@@ -179,7 +180,7 @@ int bs_xc_plan_create(const bs_xc_tensor *tensors, int n_tensors, int device, bs
         const bs_xc_tensor &t = tensors[i];
         if (t.n_elems == 0) continue;
         const std::string who = "tensor " + std::to_string(i) + ": ";
-        if (t.reserved != 0) return fail(BS_E_INVALID_ARG, who + "reserved field must be 0");
+        if (t.coder_mask & ~kXcAllCoders) return fail(BS_E_INVALID_ARG, who + "coder_mask has unknown coder bits");
         if (!t.d_blob || !t.d_out) return fail(BS_E_INVALID_ARG, who + "NULL pointer");
         if ((reinterpret_cast<uintptr_t>(t.d_blob) | reinterpret_cast<uintptr_t>(t.d_out)) & 15)
             return fail(BS_E_INVALID_ARG, who + "blob and output must be 16-byte aligned");
@@ -204,6 +205,7 @@ int bs_xc_plan_create(const bs_xc_tensor *tensors, int n_tensors, int device, bs
         d.chunk_begin = t.chunk_begin;
         d.aux = 0;
         d.coder = 0xFFFFFFFFu;
+        d.coder_mask = t.coder_mask;
         u2i[i] = static_cast<int>(ht.size());
         ht.push_back(d);
         ranges.push_back({t.chunk_begin, static_cast<uint32_t>(cnt)});
@@ -231,6 +233,7 @@ int bs_xc_plan_create(const bs_xc_tensor *tensors, int n_tensors, int device, bs
     p->n_internal = static_cast<int>(ht.size());
     p->user_to_internal = u2i;
     p->n_items = static_cast<int>(items.size());
+    p->coders = xc_launch_mask(ht.data(), static_cast<int>(ht.size()));
     Carve cv;
     const uint64_t o_t = cv.take(sizeof(XcTensorDev) * ht.size());
     const uint64_t o_i = cv.take(sizeof(XcItem) * items.size());
@@ -266,7 +269,8 @@ int bs_plan_decode(bs_plan *p, void *stream) {
     if (p->kind == kPlanXc) {
         if (p->n_internal == 0) return BS_OK;
         e = launch_xc_prepare(p->d_tens, p->n_internal, p->d_tables, p->d_errs, s);
-        if (e == cudaSuccess) e = launch_xc_decode(p->d_tens, p->d_items, p->n_items, p->d_tables, p->d_errs, s);
+        if (e == cudaSuccess)
+            e = launch_xc_decode(p->d_tens, p->d_items, p->n_items, p->d_tables, p->d_errs, p->coders, s);
     } else if (p->kind == kPlanPar) {
         if (p->n_internal == 0) return BS_OK;
         e = cudaMemsetAsync(p->d_errs, 0, 4, s);
@@ -335,7 +339,7 @@ int bs_xc_decode_noalloc(const bs_xc_tensor *tensors, int n_tensors, void *strea
         u2i[i] = -1;
         if (t.n_elems == 0) continue;
         const std::string who = "tensor " + std::to_string(i) + ": ";
-        if (t.reserved != 0) return fail(BS_E_INVALID_ARG, who + "reserved field must be 0");
+        if (t.coder_mask & ~kXcAllCoders) return fail(BS_E_INVALID_ARG, who + "coder_mask has unknown coder bits");
         if (!t.d_blob || !t.d_out) return fail(BS_E_INVALID_ARG, who + "NULL pointer");
         if ((reinterpret_cast<uintptr_t>(t.d_blob) | reinterpret_cast<uintptr_t>(t.d_out)) & 15)
             return fail(BS_E_INVALID_ARG, who + "blob and output must be 16-byte aligned");
@@ -359,6 +363,7 @@ int bs_xc_decode_noalloc(const bs_xc_tensor *tensors, int n_tensors, void *strea
         d.n_chunks = static_cast<uint32_t>(nc);
         d.chunk_begin = t.chunk_begin;
         d.coder = 0xFFFFFFFFu;
+        d.coder_mask = t.coder_mask;
         ht[n] = d;
         rc_count[n] = static_cast<uint32_t>(cnt);
         u2i[i] = n++;

@@ -28,6 +28,7 @@
 //                      is read with 8-byte loads two groups ahead; output
 //                      leaves as 16-byte streaming stores.
 #include <cstdint>
+#include <atomic>
 #include <mutex>
 
 #include "common.cuh"
@@ -107,7 +108,8 @@ __global__ void __launch_bounds__(256) xc_prepare_kernel(XcTensorDev *tens, uint
             if (h32[0] != kXcMagic || ver != 1 || coder > 2 || prec < 8 || prec > 12 || n != T.n ||
                 ce != T.chunk_elems || nc != T.n_chunks || lanes != kXcLanes || po != po_want ||
                 co != po + ((n + 15) & ~15ull) || total < co || (total & 15) || total > T.blob_bytes ||
-                (coder == 2 ? aux > 241 : aux != 0))
+                (coder == 2 ? aux > 241 : aux != 0) ||
+                (T.coder_mask != 0 && coder <= 2 && !((T.coder_mask >> coder) & 1u)))
                 err = BS_DEV_HEADER;
             s_total = total;
             s_prec = prec;
@@ -686,31 +688,50 @@ cudaError_t launch_xc_prepare(XcTensorDev *d_tens, int n_tensors, uint32_t *d_ta
     return cudaGetLastError();
 }
 
-cudaError_t launch_xc_decode(const XcTensorDev *d_tens, const XcItem *d_items, int n_items,
-                             const uint32_t *d_tables, uint32_t *d_errs, cudaStream_t s) {
-    if (n_items <= 0) return cudaSuccess;
-    const size_t smem = kXcMaxTable * 4 + kWarps * kWarpRing;
-    static bool attr_set = false;   // idempotent; a benign race
-    if (!attr_set) {
-        cudaError_t e = cudaFuncSetAttribute(xc_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             static_cast<int>(smem));
-        if (e != cudaSuccess) return e;
-        attr_set = true;
-    }
-    xc_decode_kernel<<<n_items, kThreads, smem, s>>>(d_tens, d_items, d_tables, d_errs);
-    cudaError_t e = cudaGetLastError();
+// Dynamic shared-memory opt-in, once per (kernel, device): the attribute
+// belongs to the module loaded in each device's context.
+template <typename K>
+static cudaError_t smem_opt_in(K kernel, size_t bytes, std::atomic<uint8_t> *done) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
-    // the pair coder's kernel; each CTA returns at once unless its tensor uses coder 2
-    const size_t psmem = kPairTableBytes + kWarps * kPairWarpRing;
-    static bool pair_attr_set = false;
-    if (!pair_attr_set) {
-        e = cudaFuncSetAttribute(xc_decode_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 static_cast<int>(psmem));
+    if (dev < 0 || dev >= 128) return cudaErrorInvalidDevice;
+    if (done[dev].load(std::memory_order_acquire)) return cudaSuccess;
+    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes));
+    if (e == cudaSuccess) done[dev].store(1, std::memory_order_release);
+    return e;
+}
+static std::atomic<uint8_t> g_attr_rans[128], g_attr_pair[128], g_attr_na_pair[128];
+
+uint32_t xc_launch_mask(const XcTensorDev *h_tens, int n) {
+    uint32_t m = 0;
+    for (int i = 0; i < n; i++) m |= h_tens[i].coder_mask ? h_tens[i].coder_mask : kXcAllCoders;
+    return m;
+}
+
+// One launch per coder family present: coders 0/1 share xc_decode_kernel,
+// coder 2 has its own.  A CTA whose tensor uses the other family (possible
+// only with coder_mask 0) or was flagged by the prepare kernel returns at once.
+cudaError_t launch_xc_decode(const XcTensorDev *d_tens, const XcItem *d_items, int n_items,
+                             const uint32_t *d_tables, uint32_t *d_errs, uint32_t coders, cudaStream_t s) {
+    if (n_items <= 0) return cudaSuccess;
+    cudaError_t e = cudaSuccess;
+    if (coders & ((1u << BS_CODER_RANS) | (1u << BS_CODER_TANS))) {
+        const size_t smem = kXcMaxTable * 4 + kWarps * kWarpRing;
+        e = smem_opt_in(xc_decode_kernel, smem, g_attr_rans);
         if (e != cudaSuccess) return e;
-        pair_attr_set = true;
+        xc_decode_kernel<<<n_items, kThreads, smem, s>>>(d_tens, d_items, d_tables, d_errs);
+        e = cudaGetLastError();
+        if (e != cudaSuccess) return e;
     }
-    xc_decode_pair_kernel<<<n_items, kThreads, psmem, s>>>(d_tens, d_items, d_tables, d_errs);
-    return cudaGetLastError();
+    if (coders & (1u << BS_CODER_RANS_PAIR)) {
+        const size_t psmem = kPairTableBytes + kWarps * kPairWarpRing;
+        e = smem_opt_in(xc_decode_pair_kernel, psmem, g_attr_pair);
+        if (e != cudaSuccess) return e;
+        xc_decode_pair_kernel<<<n_items, kThreads, psmem, s>>>(d_tens, d_items, d_tables, d_errs);
+        e = cudaGetLastError();
+    }
+    return e;
 }
 
 // --------------------------------------------------------------------------
@@ -857,18 +878,18 @@ cudaError_t launch_xc_noalloc(const XcTensorDev *h_tens, const uint32_t *range_c
     xc_noalloc_stage_kernel<<<1, kNoallocMaxTensors, 0, s>>>(a, d_tens);
     e = cudaGetLastError();
     if (e == cudaSuccess) e = launch_xc_prepare(d_tens, n, d_tables, d_errs, s);
-    if (e == cudaSuccess && a.cta_prefix[n] > 0) {
-        const size_t smem = kXcMaxTable * 4 + kWarps * kWarpRing;
+    const uint32_t coders = xc_launch_mask(h_tens, n);
+    if (e == cudaSuccess && a.cta_prefix[n] > 0 && (coders & ((1u << BS_CODER_RANS) | (1u << BS_CODER_TANS)))) {
+        const size_t smem = kXcMaxTable * 4 + kWarps * kWarpRing;   // below the 48 KiB default
         xc_decode_noalloc_kernel<<<a.cta_prefix[n], kThreads, smem, s>>>(a, d_tens, d_tables, d_errs);
         e = cudaGetLastError();
+    }
+    if (e == cudaSuccess && a.cta_prefix[n] > 0 && (coders & (1u << BS_CODER_RANS_PAIR))) {
+        const size_t psmem = kPairTableBytes + kWarps * kPairWarpRing;
+        e = smem_opt_in(xc_decode_noalloc_pair_kernel, psmem, g_attr_na_pair);
         if (e == cudaSuccess) {
-            const size_t psmem = kPairTableBytes + kWarps * kPairWarpRing;
-            e = cudaFuncSetAttribute(xc_decode_noalloc_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     static_cast<int>(psmem));
-            if (e == cudaSuccess) {
-                xc_decode_noalloc_pair_kernel<<<a.cta_prefix[n], kThreads, psmem, s>>>(a, d_tens, d_tables, d_errs);
-                e = cudaGetLastError();
-            }
+            xc_decode_noalloc_pair_kernel<<<a.cta_prefix[n], kThreads, psmem, s>>>(a, d_tens, d_tables, d_errs);
+            e = cudaGetLastError();
         }
     }
     if (e == cudaSuccess) e = cudaMemcpyAsync(h_status, d_errs, 4ull * n, cudaMemcpyDeviceToHost, s);

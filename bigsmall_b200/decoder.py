@@ -116,7 +116,7 @@ def verify(src) -> bool:
     return ok
 
 
-def compress_tensors(tensors: dict, dst=None, coder: str = "rans", prec: int = 12,
+def compress_tensors(tensors: dict, dst=None, coder: Optional[str] = None, prec: int = 12,
                      chunk_elems: int = exp_chunked.gpu.DEFAULT_CHUNK_ELEMS, raw_tiny: int = 512,
                      with_md5: bool = True):
     """Encode a {name: torch.Tensor} dict into a container on the device.
@@ -128,6 +128,7 @@ def compress_tensors(tensors: dict, dst=None, coder: str = "rans", prec: int = 1
     """
     import torch
     from . import gpu
+    coder = coder or gpu.DEFAULT_CODER
     w = _ct.ContainerWriter(fmt="bf16")
     enc = None
     for name, t in tensors.items():

@@ -24,6 +24,8 @@ DEFAULT_CHUNK_ELEMS = 65536   # 128 KiB of bf16 per chunk (one warp-state group)
 DEFAULT_PREC = 12             # M = 4096
 
 CODERS = {"rans": _lib.CODER_RANS, "tans": _lib.CODER_TANS, "pair": _lib.CODER_RANS_PAIR}
+# rANS over exponent pairs: half the coder steps per value for ~0.1 pp of ratio
+DEFAULT_CODER = "pair"
 
 
 def _as_cuda(t: torch.Tensor, name: str) -> torch.Tensor:
@@ -92,6 +94,16 @@ class _Plan:
         self.close()
 
 
+def coder_mask(coder) -> int:
+    """BS_CODER_* bit of a coder name or value; 0 (any coder) for None."""
+    if coder is None:
+        return 0
+    c = CODERS[coder] if isinstance(coder, str) else int(coder)
+    if c not in CODERS.values():
+        raise ValueError(f"unknown coder {coder!r}")
+    return 1 << c
+
+
 class XcPlan(_Plan):
     """Decode plan for a batch of bf16_exp_chunked_v1 tensors.
 
@@ -101,12 +113,23 @@ class XcPlan(_Plan):
     ``(blob, out, chunk_elems, n_total, chunk_begin, chunk_count)`` to decode
     only chunks [chunk_begin, chunk_begin + chunk_count) of a tensor of
     ``n_total`` values into ``out`` (element chunk_begin * chunk_elems first).
-    One plan decodes all entries with two kernel launches; it can be re-run
-    any number of times.
+    One plan decodes all entries with one prepare launch plus one decode
+    launch per coder family present; it can be re-run any number of times.
+
+    ``coders``: the coder each blob was written with ("rans", "tans", "pair"
+    or a BS_CODER_* value), one for all entries or a sequence with one per
+    entry; None (or a None element) means unknown, which launches every
+    decode kernel.  A blob whose header names another coder fails with
+    BS_DEV_HEADER rather than being skipped.
     """
 
-    def __init__(self, entries: Iterable[tuple], device: Optional[int] = None):
+    def __init__(self, entries: Iterable[tuple], device: Optional[int] = None, coders=None):
         entries = list(entries)
+        if coders is None or isinstance(coders, (str, int)):
+            coders = [coders] * len(entries)
+        coders = list(coders)
+        if len(coders) != len(entries):
+            raise ValueError("coders must have one element per entry")
         keep = []
         arr = (_lib.XcTensor * max(1, len(entries)))()
         dev = device
@@ -131,7 +154,7 @@ class XcPlan(_Plan):
             arr[i].chunk_elems = int(ce)
             arr[i].chunk_begin = int(c0)
             arr[i].chunk_count = int(cc)
-            arr[i].reserved = 0
+            arr[i].coder_mask = coder_mask(coders[i])
             keep += [blob, out]
         if dev is None:
             dev = torch.cuda.current_device()
@@ -165,9 +188,9 @@ class ParPlan(_Plan):
 
 
 def decode_xc_into(blob: torch.Tensor, out: torch.Tensor, chunk_elems: int,
-                   stream=None, check: bool = True) -> torch.Tensor:
+                   stream=None, check: bool = True, coder=None) -> torch.Tensor:
     """Decode one bf16_exp_chunked_v1 blob (device) into ``out`` (device)."""
-    with XcPlan([(blob, out, chunk_elems)]) as p:
+    with XcPlan([(blob, out, chunk_elems)], coders=coder) as p:
         p.decode(stream)
         if check:
             p.check(stream)
@@ -190,7 +213,7 @@ def encode_bound(n: int, chunk_elems: int = DEFAULT_CHUNK_ELEMS) -> int:
     return int(v.value)
 
 
-def encode_workspace(n: int, chunk_elems: int = DEFAULT_CHUNK_ELEMS, coder: str = "rans") -> int:
+def encode_workspace(n: int, chunk_elems: int = DEFAULT_CHUNK_ELEMS, coder: str = DEFAULT_CODER) -> int:
     v = ctypes.c_uint64()
     c = CODERS[coder] if isinstance(coder, str) else int(coder)
     _lib.check(_lib.load().bs_xc_encode_workspace(n, chunk_elems, c, ctypes.byref(v)), "bs_xc_encode_workspace")
@@ -201,7 +224,7 @@ class XcEncoder:
     """Reusable device encoder: owns an output buffer and a workspace sized for
     tensors of up to ``max_elems`` values (no allocation per call)."""
 
-    def __init__(self, max_elems: int, chunk_elems: int = DEFAULT_CHUNK_ELEMS, coder: str = "rans",
+    def __init__(self, max_elems: int, chunk_elems: int = DEFAULT_CHUNK_ELEMS, coder: str = DEFAULT_CODER,
                  prec: int = DEFAULT_PREC, device=None):
         self.chunk_elems = int(chunk_elems)
         self.coder = CODERS[coder] if isinstance(coder, str) else int(coder)
@@ -250,14 +273,14 @@ class XcEncoder:
         return self.out[:n].clone()
 
 
-def encode_xc(x: torch.Tensor, coder: str = "rans", prec: int = DEFAULT_PREC,
+def encode_xc(x: torch.Tensor, coder: str = DEFAULT_CODER, prec: int = DEFAULT_PREC,
               chunk_elems: int = DEFAULT_CHUNK_ELEMS, stream=None) -> torch.Tensor:
     """Encode a bf16 CUDA tensor into a bf16_exp_chunked_v1 blob on the device."""
     enc = XcEncoder(max(1, x.numel()), chunk_elems, coder, prec, device=_dev_index(x))
     return enc.encode(x.reshape(-1), stream)
 
 
-def xc_extras(chunk_elems: int = DEFAULT_CHUNK_ELEMS, coder: str = "rans", prec: int = DEFAULT_PREC) -> dict:
+def xc_extras(chunk_elems: int = DEFAULT_CHUNK_ELEMS, coder: str = DEFAULT_CODER, prec: int = DEFAULT_PREC) -> dict:
     """The per-tensor ``extra`` dict the container header stores for the codec."""
     return {"chunk_elems": int(chunk_elems), "coder": coder, "prec": int(prec)}
 
@@ -276,6 +299,6 @@ def sync(device=None) -> None:
 
 
 __all__: Sequence[str] = [
-    "DEFAULT_CHUNK_ELEMS", "DEFAULT_PREC", "XcPlan", "ParPlan", "XcEncoder", "decode_xc_into",
+    "DEFAULT_CHUNK_ELEMS", "DEFAULT_PREC", "DEFAULT_CODER", "XcPlan", "ParPlan", "XcEncoder", "decode_xc_into",
     "decode_par_into", "encode_xc", "encode_bound", "encode_workspace", "xc_extras", "aligned_view",
 ]

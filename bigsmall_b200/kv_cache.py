@@ -35,17 +35,18 @@ def _check_bf16(t: torch.Tensor, what: str) -> None:
 class KVEncoder:
     """Reusable device encoder for K/V tensors (grows its buffers on demand)."""
 
-    def __init__(self, device=None, chunk_elems: int = KV_CHUNK_ELEMS):
+    def __init__(self, device=None, chunk_elems: int = KV_CHUNK_ELEMS, coder: str = gpu.DEFAULT_CODER):
         self.device = torch.device("cuda", device if isinstance(device, int) else
                                    (torch.device(device).index if device is not None else torch.cuda.current_device()))
         if self.device.index is None:
             self.device = torch.device("cuda", torch.cuda.current_device())
         self.chunk_elems = chunk_elems
+        self.coder = coder
         self._enc: Optional[gpu.XcEncoder] = None
 
     def encoder(self, n: int) -> gpu.XcEncoder:
         if self._enc is None or self._enc.max_elems < n:
-            self._enc = gpu.XcEncoder(max(n, 1), self.chunk_elems, device=self.device.index)
+            self._enc = gpu.XcEncoder(max(n, 1), self.chunk_elems, self.coder, device=self.device.index)
         return self._enc
 
     def encode(self, t: torch.Tensor) -> torch.Tensor:
@@ -65,7 +66,7 @@ def encode_kv(keys: torch.Tensor, values: torch.Tensor, enc: Optional[KVEncoder]
 
 
 def decode_kv(k_blob: torch.Tensor, v_blob: torch.Tensor, k_shape, v_shape, device=None,
-              chunk_elems: int = KV_CHUNK_ELEMS, out: Optional[tuple] = None):
+              chunk_elems: int = KV_CHUNK_ELEMS, out: Optional[tuple] = None, coder=None):
     """Decode both blobs (device) with one plan; returns (keys, values) bf16."""
     dev = k_blob.device if device is None else torch.device(device)
     if out is None:
@@ -75,7 +76,7 @@ def decode_kv(k_blob: torch.Tensor, v_blob: torch.Tensor, k_shape, v_shape, devi
         k, v = out
     entries = [(b, o.view(torch.int16).reshape(-1), chunk_elems) for b, o in ((k_blob, k), (v_blob, v)) if o.numel()]
     if entries:
-        with gpu.XcPlan(entries, device=dev.index) as p:
+        with gpu.XcPlan(entries, device=dev.index, coders=coder) as p:
             p.run()
     return k, v
 

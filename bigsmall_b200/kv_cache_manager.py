@@ -39,7 +39,7 @@ class CompressedKVCache:
         if layer_idx not in self._store:
             raise KeyError(f"layer {layer_idx} not in CompressedKVCache")
         kb, vb, ks, vs = self._store[layer_idx]
-        return decode_kv(kb, vb, ks, vs, device=self.device, out=out)
+        return decode_kv(kb, vb, ks, vs, device=self.device, out=out, coder=self._enc.coder)
 
     def has(self, layer_idx: int) -> bool:
         return layer_idx in self._store

@@ -196,7 +196,7 @@ class DeviceLoader:
         for g in groups:
             g.host_spans = [(layout[p.name][0], layout[p.name][1], layout[p.name][2])
                             for p in g.parts if p.meta["codec"] != "tied_ref"]
-            xc_entries = []
+            xc_entries, xc_coders = [], []
             for p in g.parts:
                 m = p.meta
                 _, d, nb = layout[p.name]
@@ -205,6 +205,7 @@ class DeviceLoader:
                     ce = int((m.get("extra") or {})["chunk_elems"])
                     out = self.out[p.name].reshape(-1).view(torch.int16)
                     xc_entries.append((blob, out, ce, _ct.n_elements(m["shape"]), p.chunk_begin, p.chunk_count))
+                    xc_coders.append((m.get("extra") or {}).get("coder"))
                 elif m["codec"] == "bf16_parallel_v1":
                     n = _ct.n_elements(m["shape"])
                     out = self.out[p.name].reshape(-1).view(torch.int16)
@@ -215,7 +216,7 @@ class DeviceLoader:
                         raise ValueError(f"raw tensor {p.name}: {nb} bytes for {dst.numel()}")
                     g.copies.append((dst, blob))
             if xc_entries:
-                g.plans.insert(0, gpu.XcPlan(xc_entries, device=self.device.index))
+                g.plans.insert(0, gpu.XcPlan(xc_entries, device=self.device.index, coders=xc_coders))
             g.event = torch.cuda.Event()
 
     # -- run -------------------------------------------------------------------
@@ -377,7 +378,7 @@ class ResidentContainer:
 
     def bundle(self, outputs: dict) -> Bundle:
         """outputs: {name: device tensor of the tensor's shape/dtype}."""
-        xc, plans, copies = [], [], []
+        xc, coders, plans, copies = [], [], [], []
         for name, out in outputs.items():
             real = self.resolve(name)
             m = self.image.tensors[real]
@@ -385,13 +386,14 @@ class ResidentContainer:
             flat = out.reshape(-1)
             if m["codec"] == "bf16_exp_chunked_v1":
                 xc.append((blob, flat.view(torch.int16), int((m.get("extra") or {})["chunk_elems"])))
+                coders.append((m.get("extra") or {}).get("coder"))
             elif m["codec"] == "bf16_parallel_v1":
                 plans.append(gpu.ParPlan(bytes(self.image.blob_host(real)), blob, flat.view(torch.int16),
                                          _ct.n_elements(m["shape"])))
             else:   # raw
                 copies.append((flat.view(torch.uint8), blob))
         if xc:
-            plans.insert(0, gpu.XcPlan(xc, device=self.device.index))
+            plans.insert(0, gpu.XcPlan(xc, device=self.device.index, coders=coders))
         return Bundle(plans, copies)
 
     def decode(self, names, stream=None) -> dict:

@@ -69,7 +69,11 @@ typedef struct bs_xc_tensor {
     uint32_t    chunk_elems;
     uint32_t    chunk_begin;
     uint32_t    chunk_count;
-    uint32_t    reserved;      /* must be 0 */
+    uint32_t    coder_mask;    /* bit c set: the blob may use coder c (BS_CODER_*);
+                                  0: any coder.  A plan launches the decode kernel
+                                  of each coder its tensors may use; a blob whose
+                                  coder is not in a nonzero mask fails with
+                                  BS_DEV_HEADER instead of being decoded. */
 } bs_xc_tensor;
 
 /* ---- library ------------------------------------------------------------ */

@@ -135,3 +135,27 @@ def test_corrupt_pair_records_raise_without_fault():
         st = ei.value.device_status[0]
         assert st and (st & bits), (name, hex(st))
     assert _decode(good, n, 4096) == raw
+
+
+def test_coder_hint_selects_kernels_and_rejects_mismatch():
+    """A plan given the blobs' coders launches only their decode kernels; a
+    blob written with another coder fails with BS_DEV_HEADER, never skipped."""
+    from bigsmall_b200 import gpu
+    from bigsmall_b200.exceptions import BsCorruptError
+    n = 70_001
+    raw = _normal(n, 21)
+    pair = O.xc_encode(raw, 2, 12, 4096)
+    rans = O.xc_encode(raw, 0, 12, 4096)
+    assert _decode(pair, n, 4096) == raw
+    for blob, hint in ((pair, "pair"), (rans, "rans"), (pair, None), (rans, [None])):
+        out = torch.empty(n, dtype=torch.bfloat16, device="cuda")
+        with gpu.XcPlan([(_dev(blob), out, 4096)], coders=hint) as p:
+            p.run()
+        assert out.cpu().view(torch.uint8).numpy().tobytes() == raw, hint
+    for blob, hint in ((pair, "rans"), (rans, "pair"), (pair, "tans")):
+        out = torch.empty(n, dtype=torch.bfloat16, device="cuda")
+        with pytest.raises(BsCorruptError) as ei:
+            gpu.decode_xc_into(_dev(blob), out, 4096, coder=hint)
+        assert ei.value.device_status[0] & 0x01, hint
+    with pytest.raises(ValueError):
+        gpu.XcPlan([(_dev(pair), torch.empty(n, dtype=torch.bfloat16, device="cuda"), 4096)], coders=["pair", "rans"])

@@ -82,7 +82,7 @@ def test_full_size_config1_roundtrip_and_encoder_pin(manifest):
     x = c1_tensor()
     raw = x.view(torch.uint8).numpy().tobytes()
     assert md5(raw) == full["raw_md5"]
-    blob = gpu.encode_xc(x.cuda())
+    blob = gpu.encode_xc(x.cuda(), coder="rans")
     hb = blob.cpu().numpy().tobytes()
     assert md5(hb) == md5(O.xc_encode(raw, 0, 12, gpu.DEFAULT_CHUNK_ELEMS))
     out = torch.empty_like(x, device="cuda")

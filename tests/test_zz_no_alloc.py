@@ -69,7 +69,7 @@ def _noalloc(cases, outs):
         arr[i].chunk_elems = ce
         arr[i].chunk_begin = c0
         arr[i].chunk_count = cc
-        arr[i].reserved = 0
+        arr[i].coder_mask = 0
     st = (ctypes.c_uint32 * max(1, len(cases)))()
     stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
     rc = L.bs_xc_decode_noalloc(arr, len(cases), stream, st)
