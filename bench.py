@@ -169,9 +169,10 @@ def measured_peak():
         return FALLBACK_HBM_GBS, "fallback"
 
 
-def profile_traffic():
-    """dram bytes per decode launch from the committed ncu summary, if any."""
-    p = os.path.join(ROOT, "profiles", "xc_decode_c2.json")
+def profile_traffic(coder: str):
+    """dram bytes per config-2 decode launch from the committed ncu summary
+    of this coder's kernel, if any."""
+    p = os.path.join(ROOT, "profiles", f"xc_decode_c2_{coder}.json")
     try:
         with open(p) as f:
             return json.load(f)
@@ -226,10 +227,11 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=8.0)
-    ap.add_argument("--config", default="c2", choices=["c2", "small", "kv", "sweep", "stream"],
+    ap.add_argument("--config", default="c2", choices=["c2", "small", "kv", "sweep", "stream", "mix"],
                     help="c2: the benchmark workload; small: one 2^27-value tensor of the same "
                          "distribution (compressed ~170 MB, above L2) for ncu captures; kv: BASELINE "
-                         "config 5 (KV cache encode+decode); sweep: config 3 (rANS vs tANS x chunk size)")
+                         "config 5 (KV cache encode+decode); sweep: config 3 (coders x chunk size); "
+                         "stream: config 4; mix: HBM calibration of the decode's read:write mix")
     a = ap.parse_args()
     a.warmup = max(3, a.warmup)
 
@@ -280,6 +282,8 @@ def main():
         return bench_sweep(a, torch, dev, world, rank, dist, local)
     if a.config == "stream":
         return bench_stream(a, torch, dev, world, rank, dist, local)
+    if a.config == "mix":
+        return bench_mix(a, torch, dev, world, rank, dist, local)
     if a.config == "small":
         tensors = [("model.layers.0.mlp.small_proj.weight", (1 << 15, 4096), "linear")]
         config["workload"] = "one 2^27-value bf16 tensor, config-2 distribution (profiling case)"
@@ -414,7 +418,7 @@ def main():
         peak, peak_kind = measured_peak()
         value = 2 * total_elems / (ms * 1e-3) / 1e9
         achieved = algo_bytes / (local_ms * 1e-3) / 1e9
-        prof = profile_traffic()
+        prof = profile_traffic(a.coder) if a.config == "c2" else None
         traffic = None
         if prof and prof.get("chunk_elems") == ce and world == 1:
             traffic = prof.get("traffic_bytes_per_launch")
@@ -576,6 +580,40 @@ def bench_sweep(a, torch, dev, world, rank, dist, local):
                 del blob, out
         del x
         torch.cuda.empty_cache()
+
+
+# ---------------------------------------------------------------------------
+# HBM calibration: plain streaming kernels at the decode's DRAM read:write mix
+# ---------------------------------------------------------------------------
+def bench_mix(a, torch, dev, world, rank, dist, local):
+    """Rate of bs_stream_probe for 1:1 (copy), 2:3 (the decode's mix: ~10.6 GB
+    read per 16 GB written on config 2) and 0:1 (write only), 5 GiB per
+    stream, best launch shape of 4/8/16 CTAs per SM.  One JSON line."""
+    import ctypes
+    from bigsmall_b200 import _lib
+    L = _lib.load()
+    units = (5 << 30) // 16
+    src = torch.empty(2 * units * 16, dtype=torch.uint8, device=dev).fill_(1)
+    dst = torch.empty(3 * units * 16, dtype=torch.uint8, device=dev)
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    stream = torch.cuda.current_stream(dev)
+    peak, peak_kind = measured_peak()
+    res = {}
+    for name, rd, wr in (("copy_1to1", 1, 1), ("mix_2to3", 2, 3), ("write_only", 0, 1)):
+        best = None
+        for per_sm in (4, 8, 16):
+            def launch():
+                _lib.check(L.bs_stream_probe(src.data_ptr(), dst.data_ptr(), units, rd, wr, sms * per_sm,
+                                             ctypes.c_void_p(stream.cuda_stream)), "bs_stream_probe")
+            ms = _timed(torch, launch, a.steps, a.warmup, stream)
+            gbs = 16 * units * (rd + wr) / ms / 1e6
+            if best is None or gbs > best["GBs"]:
+                best = {"GBs": round(gbs, 1), "ms": round(ms, 4), "ctas_per_sm": per_sm,
+                        "read_GB": round(16 * units * rd / 1e9, 2), "write_GB": round(16 * units * wr / 1e9, 2)}
+        res[name] = best
+    if rank == 0:
+        print(json.dumps({"config": "HBM calibration (bs_stream_probe)", "peak": f"{peak} ({peak_kind})",
+                          **res, "mix_2to3_frac_of_peak": round(res["mix_2to3"]["GBs"] / peak, 4)}), flush=True)
 
 
 # ---------------------------------------------------------------------------

@@ -65,6 +65,7 @@ SIGNATURES = {
     "bs_xc_encode_bound": (_I, [_U64, _U32, ctypes.POINTER(_U64)]),
     "bs_xc_encode_workspace": (_I, [_U64, _U32, _I, ctypes.POINTER(_U64)]),
     "bs_xc_encode": (_I, [_P, _U64, _I, _I, _U32, _P, _U64, _P, _P, _U64, _P]),
+    "bs_stream_probe": (_I, [_P, _P, _U64, _I, _I, _I, _P]),
 }
 
 _lib = None

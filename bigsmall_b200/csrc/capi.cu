@@ -669,4 +669,22 @@ int bs_xc_encode(const void *d_in, uint64_t n, int coder, int prec, uint32_t ce,
     return BS_OK;
 }
 
+int bs_stream_probe(const void *d_in, void *d_out, uint64_t units, int rd, int wr, int grid, void *stream) {
+    if (!((rd == 1 && wr == 1) || (rd == 2 && wr == 3) || (rd == 0 && wr == 1)))
+        return fail(BS_E_INVALID_ARG, "bs_stream_probe: (rd, wr) must be (1,1), (2,3) or (0,1)");
+    if (grid <= 0 || units == 0 || (rd && !d_in) || !d_out) return fail(BS_E_INVALID_ARG, "bs_stream_probe: bad arguments");
+    if ((reinterpret_cast<uintptr_t>(d_in) | reinterpret_cast<uintptr_t>(d_out)) & 15)
+        return fail(BS_E_INVALID_ARG, "bs_stream_probe: buffers must be 16-byte aligned");
+    int device = 0;
+    if (cudaGetDevice(&device) != cudaSuccess) {
+        cudaGetLastError();
+        return fail(BS_E_CUDA, "no current CUDA device");
+    }
+    if ((rd && !on_device(d_in, device)) || !on_device(d_out, device))
+        return fail(BS_E_INVALID_ARG, "bs_stream_probe: buffers must be device memory of the current device");
+    cudaError_t e = launch_stream_mix(d_in, d_out, units, rd, wr, grid, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "bs_stream_probe");
+    return BS_OK;
+}
+
 }  // extern "C"

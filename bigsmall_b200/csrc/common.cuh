@@ -90,6 +90,8 @@ struct ParStream {
 namespace bsg {
 cudaError_t launch_xc_prepare(XcTensorDev *d_tens, int n_tensors, uint32_t *d_tables,
                               uint32_t *d_errs, cudaStream_t s);
+cudaError_t launch_stream_mix(const void *d_in, void *d_out, uint64_t units, int rd, int wr, int grid,
+                              cudaStream_t s);
 constexpr uint32_t kXcAllCoders = 7u;   // BS_CODER_RANS | TANS | RANS_PAIR bits
 // Union of the tensors' coder masks (a zero mask counts as every coder).
 uint32_t xc_launch_mask(const XcTensorDev *h_tens, int n);

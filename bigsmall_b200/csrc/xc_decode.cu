@@ -443,9 +443,11 @@ __device__ __forceinline__ void decode_chunk(const uint32_t *__restrict__ s_tab,
 // bit 31 of y) takes its exponent from the record's escape list in a
 // warp-uniform fix-up path.
 // --------------------------------------------------------------------------
+constexpr uint32_t kPairRingBytes = 2048;                // per-warp staging ring (power of 2)
 constexpr uint32_t kPairMirror = kFill;                 // 8 pair-steps consume <= 512 B
-constexpr uint32_t kPairWarpRing = kRingBytes + kPairMirror;
+constexpr uint32_t kPairWarpRing = kPairRingBytes + kPairMirror;
 constexpr uint32_t kPairTableBytes = 8 * kXcMaxTable;
+constexpr int kPairMinBlocks = 4;                        // CTAs per SM the registers must allow
 
 __device__ __forceinline__ uint2 lds_u64(uint32_t a) {
     uint2 v;
@@ -456,9 +458,9 @@ __device__ __forceinline__ uint2 lds_u64(uint32_t a) {
 __device__ __forceinline__ void pair_ring_issue(Ring &r, uint32_t lane) {
     const uint32_t off = r.fetched + 16 * lane;
     if (off < r.bytes) {
-        const uint32_t pos = off & (kRingBytes - 1);
+        const uint32_t pos = off & (kPairRingBytes - 1);
         cp_async16(r.buf + pos, r.src + off);
-        if (pos < kPairMirror) cp_async16(r.buf + kRingBytes + pos, r.src + off);
+        if (pos < kPairMirror) cp_async16(r.buf + kPairRingBytes + pos, r.src + off);
     }
     cp_async_commit();
     r.fetched += kFill;
@@ -475,7 +477,7 @@ __device__ __forceinline__ void pair_ring_ensure(Ring &r, uint32_t consumed_byte
 }
 
 __device__ __forceinline__ void pair_ring_refill(Ring &r, uint32_t consumed_bytes, uint32_t lane) {
-    if (r.fetched < r.bytes && r.fetched + kFill - consumed_bytes <= kRingBytes) {
+    if (r.fetched < r.bytes && r.fetched + kFill - consumed_bytes <= kPairRingBytes) {
         __syncwarp();
         pair_ring_issue(r, lane);
     }
@@ -529,7 +531,7 @@ __device__ __forceinline__ void decode_chunk_pair(uint32_t tab_s, uint8_t *ring_
     if (stage > rec_bytes - kXcPairRecHdr) stage = rec_bytes - kXcPairRecHdr;
     Ring r{ring_buf, rec + kXcPairRecHdr, stage, 0, 0};
 #pragma unroll
-    for (int k = 0; k < (int)(kRingBytes / kFill); k++) pair_ring_issue(r, lane);
+    for (int k = 0; k < (int)(kPairRingBytes / kFill); k++) pair_ring_issue(r, lane);
 
     uint32_t raddr = ring_s, consumed = 0, epos = 0;
     const uint32_t G = cn >> 8, rem = cn & 255;
@@ -560,7 +562,7 @@ __device__ __forceinline__ void decode_chunk_pair(uint32_t tab_s, uint8_t *ring_
         }
         st_out16(out + g * 256 + lane * 8, v);
     };
-    const uint32_t ring_end = ring_s + kRingBytes;
+    const uint32_t ring_end = ring_s + kPairRingBytes;
     const uint8_t *pl = plane + lane * 8;
     uint2 sm_a = make_uint2(0, 0), sm_b = make_uint2(0, 0);
     if (G > 0) sm_a = ld_plane8(pl);
@@ -568,7 +570,7 @@ __device__ __forceinline__ void decode_chunk_pair(uint32_t tab_s, uint8_t *ring_
     uint32_t g = 0;
     for (; g + 1 < G; g += 2) {
         pair_ring_ensure(r, consumed);
-        if (raddr >= ring_end) raddr -= kRingBytes;
+        if (raddr >= ring_end) raddr -= kPairRingBytes;
         const uint32_t rstart = raddr;
         const uint2 s0 = sm_a, s1 = sm_b;
         sm_a = ld_plane8(pl + min(g + 2, G - 1) * 256);
@@ -580,14 +582,14 @@ __device__ __forceinline__ void decode_chunk_pair(uint32_t tab_s, uint8_t *ring_
     }
     if (g < G) {
         pair_ring_ensure(r, consumed);
-        if (raddr >= ring_end) raddr -= kRingBytes;
+        if (raddr >= ring_end) raddr -= kPairRingBytes;
         const uint32_t rstart = raddr;
         group(g, sm_a);
         consumed += raddr - rstart;
     }
     if (rem) {
         pair_ring_ensure(r, consumed);
-        if (raddr >= ring_end) raddr -= kRingBytes;
+        if (raddr >= ring_end) raddr -= kPairRingBytes;
         const uint32_t rstart = raddr;
         const uint32_t e_base = G * 256 + lane * 8;
 #pragma unroll 1
@@ -614,7 +616,7 @@ __device__ __forceinline__ void decode_chunk_pair(uint32_t tab_s, uint8_t *ring_
     if (code && lane == 0) atomicOr(err, code);
 }
 
-__global__ void __launch_bounds__(kThreads) xc_decode_pair_kernel(const XcTensorDev *__restrict__ tens,
+__global__ void __launch_bounds__(kThreads, kPairMinBlocks) xc_decode_pair_kernel(const XcTensorDev *__restrict__ tens,
                                                                   const XcItem *__restrict__ items,
                                                                   const uint32_t *__restrict__ tables,
                                                                   uint32_t *errs) {
@@ -804,7 +806,7 @@ __global__ void __launch_bounds__(kThreads) xc_decode_noalloc_kernel(const Noall
         decode_chunk<1>(s_tab, ring, rec, rec_bytes, plane, out, cn, P, &errs[ti]);
 }
 
-__global__ void __launch_bounds__(kThreads) xc_decode_noalloc_pair_kernel(const NoallocArgs a,
+__global__ void __launch_bounds__(kThreads, kPairMinBlocks) xc_decode_noalloc_pair_kernel(const NoallocArgs a,
                                                                           const XcTensorDev *__restrict__ tens,
                                                                           const uint32_t *__restrict__ tables,
                                                                           uint32_t *errs) {

@@ -317,11 +317,8 @@ __global__ void __launch_bounds__(kEncWarps * 32) xc_enc_chunks_pair_kernel(
     // escape list, forward: per pair-step, lanes in order, first value then second
     uint8_t *esc = slot + kXcPairRecHdr;
     uint32_t epos = 0;
-    const uint32_t S2 = (G + (rem ? 1u : 0u)) * 4;
-    for (uint32_t s2 = 0; s2 < S2; s2++) {
-        const uint32_t e = (s2 >> 2) * 256 + lane * 8 + 2 * (s2 & 3);
-        const bool act = e < cn, has_b = e + 1 < cn;
-        const uint32_t v0 = act ? src[e] : 0u, v1 = has_b ? src[e + 1] : 0u;
+    auto esc_step = [&](uint32_t w, bool act, bool has_b) {
+        const uint32_t v0 = w & 0xFFFF, v1 = w >> 16;
         const bool ea = act && pair_a(v0, e_lo) == 15;
         const bool eb = has_b && pair_a(v1, e_lo) == 15;
         const uint32_t ba = __ballot_sync(kFull, ea), bb = __ballot_sync(kFull, eb);
@@ -330,6 +327,23 @@ __global__ void __launch_bounds__(kEncWarps * 32) xc_enc_chunks_pair_kernel(
             if (ea) esc[pa] = static_cast<uint8_t>((v0 >> 7) & 0xFF);
             if (eb) esc[pa + (ea ? 1u : 0u)] = static_cast<uint8_t>((v1 >> 7) & 0xFF);
             epos += __popc(ba) + __popc(bb);
+        }
+    };
+    for (uint32_t g = 0; g < G; g++) {
+        const uint4 v = reinterpret_cast<const uint4 *>(src + g * 256 + lane * 8)[0];
+        esc_step(v.x, true, true);
+        esc_step(v.y, true, true);
+        esc_step(v.z, true, true);
+        esc_step(v.w, true, true);
+    }
+    if (rem) {
+        const uint32_t eb0 = G * 256 + lane * 8;
+        for (uint32_t jj = 0; jj < 4; jj++) {
+            const uint32_t e = lane * 8 + 2 * jj;
+            const bool act = e < rem, has_b = e + 1 < rem;
+            const uint32_t w = (act ? static_cast<uint32_t>(src[eb0 + 2 * jj]) : 0u) |
+                               (has_b ? static_cast<uint32_t>(src[eb0 + 2 * jj + 1]) << 16 : 0u);
+            esc_step(w, act, has_b);
         }
     }
     if (lane == 0) {

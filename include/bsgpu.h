@@ -148,6 +148,14 @@ int bs_xc_encode(const void *d_in, uint64_t n_elems, int coder, int prec,
                  uint64_t *d_out_len, void *d_workspace, uint64_t ws_bytes,
                  void *stream);
 
+/* ---- measurement helper (no reference counterpart) ------------------------
+ * HBM calibration probe: `units` x 16-byte words per stream; reads rd streams
+ * of d_in and writes wr streams of d_out (d_in holds rd*units*16 bytes, d_out
+ * wr*units*16), grid-stride over `grid` CTAs of 256 threads, with the
+ * decoder's load/store instructions.  (rd, wr) in {(1,1), (2,3), (0,1)}: 2:3 is
+ * the decode's DRAM read:write mix, so its rate is that mix's practical ceiling. */
+int bs_stream_probe(const void *d_in, void *d_out, uint64_t units, int rd, int wr, int grid, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -91,5 +91,8 @@ def test_ac_cuda_slot_and_registry(manifest):
     enc, dec = codec_registry.get_codec("bf16_exp_chunked_v1")
     raw = golden_bytes("c1_head_16k.raw")
     b, extras = enc(raw, chunk_elems=4096)
-    assert b == O.xc_encode(raw, 0, 12, 4096) and dec(b, extras, len(raw) // 2) == raw
+    assert extras["coder"] == "pair"
+    assert b == O.xc_encode(raw, 2, 12, 4096) and dec(b, extras, len(raw) // 2) == raw
+    b0, extras0 = enc(raw, chunk_elems=4096, coder="rans")
+    assert b0 == O.xc_encode(raw, 0, 12, 4096) and dec(b0, extras0, len(raw) // 2) == raw
     assert "bf16_parallel_v1" in codec_registry.registered_names()

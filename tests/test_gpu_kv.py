@@ -73,12 +73,13 @@ def test_config5_distribution_device_encoder_matches_oracle():
     g = torch.Generator().manual_seed(0)
     scale = torch.exp(torch.randn(1, 8, 1, 128, generator=g))
     k = (torch.randn(2, 8, 256, 128, generator=g) * scale).to(torch.bfloat16)
-    enc = KVEncoder(0)
-    kb = enc.encode(k.cuda())
     raw = k.view(torch.uint8).numpy().tobytes()
-    assert kb.cpu().numpy().tobytes() == O.xc_encode(raw, 0, 12, gpu.DEFAULT_CHUNK_ELEMS)
-    k2, _ = decode_kv(kb, kb, k.shape, k.shape)
-    assert torch.equal(k2.cpu().view(torch.int16), k.view(torch.int16))
+    for coder, cid in (("pair", 2), ("rans", 0)):
+        enc = KVEncoder(0, coder=coder)
+        kb = enc.encode(k.cuda())
+        assert kb.cpu().numpy().tobytes() == O.xc_encode(raw, cid, 12, gpu.DEFAULT_CHUNK_ELEMS), coder
+        k2, _ = decode_kv(kb, kb, k.shape, k.shape, coder=coder)
+        assert torch.equal(k2.cpu().view(torch.int16), k.view(torch.int16)), coder
 
 
 def test_legacy_kv_versions_rejected_clearly():

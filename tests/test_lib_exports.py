@@ -39,6 +39,11 @@ def test_host_side_validation_without_gpu():
     v = ctypes.c_uint64()
     assert lib.bs_xc_encode_bound(1000, 100, ctypes.byref(v)) == _lib.BS_E_INVALID_ARG
     assert lib.bs_xc_encode_bound(1000, 256, ctypes.byref(v)) == 0 and v.value > 2000
+    for coder, ok in ((0, True), (1, True), (2, True), (3, False), (-1, False)):
+        rc = lib.bs_xc_encode_workspace(100_000, 4096, coder, ctypes.byref(v))
+        assert (rc == 0) == ok, coder
+    assert lib.bs_stream_probe(None, None, 16, 3, 3, 1, None) == _lib.BS_E_INVALID_ARG
+    assert lib.bs_stream_probe(None, None, 16, 2, 3, 1, None) == _lib.BS_E_INVALID_ARG
     h = ctypes.c_void_p()
     # no CUDA device in a CPU-only container: creation must fail cleanly
     rc = lib.bs_xc_plan_create(None, 0, 0, ctypes.byref(h))
