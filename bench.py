@@ -227,11 +227,13 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=8.0)
-    ap.add_argument("--config", default="c2", choices=["c2", "small", "kv", "sweep", "stream", "mix"],
+    ap.add_argument("--config", default="c2", choices=["c2", "small", "kv", "sweep", "stream", "mix", "legacy"],
                     help="c2: the benchmark workload; small: one 2^27-value tensor of the same "
                          "distribution (compressed ~170 MB, above L2) for ncu captures; kv: BASELINE "
                          "config 5 (KV cache encode+decode); sweep: config 3 (coders x chunk size); "
-                         "stream: config 4; mix: HBM calibration of the decode's read:write mix")
+                         "stream: config 4; mix: HBM calibration of the decode's read:write mix; "
+                         "legacy: the reference's serial formats (bf16_se_single_kernel, bf16_se_tans) "
+                         "on the config-1 tensor and on a batch of config-2 k/v tensors")
     a = ap.parse_args()
     a.warmup = max(3, a.warmup)
 
@@ -284,6 +286,8 @@ def main():
         return bench_stream(a, torch, dev, world, rank, dist, local)
     if a.config == "mix":
         return bench_mix(a, torch, dev, world, rank, dist, local)
+    if a.config == "legacy":
+        return bench_legacy(a, torch, dev, world, rank, dist, local)
     if a.config == "small":
         tensors = [("model.layers.0.mlp.small_proj.weight", (1 << 15, 4096), "linear")]
         config["workload"] = "one 2^27-value bf16 tensor, config-2 distribution (profiling case)"
@@ -614,6 +618,73 @@ def bench_mix(a, torch, dev, world, rank, dist, local):
     if rank == 0:
         print(json.dumps({"config": "HBM calibration (bs_stream_probe)", "peak": f"{peak} ({peak_kind})",
                           **res, "mix_2to3_frac_of_peak": round(res["mix_2to3"]["GBs"] / peak, 4)}), flush=True)
+
+
+# ---------------------------------------------------------------------------
+# legacy serial formats on the device (SURVEY rank-4 row), with their CPU leg
+# ---------------------------------------------------------------------------
+def legacy_cpu_leg(kind: str, raws: list, threads: int):
+    """cpu_baseline leg of --config legacy: the reference's encoder for the
+    format (its C restatement) writes the blobs, and the reference's CPU
+    decoder (same restatement) is timed on them with `threads` host threads.
+    Returns (blobs, seconds per decode of all blobs)."""
+    from oracle import oracle as O
+    from concurrent.futures import ThreadPoolExecutor
+    enc = getattr(O, f"{kind}_encode")
+    with ThreadPoolExecutor(threads) as ex:
+        blobs = list(ex.map(enc, raws))
+    nw = [len(r) // 2 for r in raws]
+    O.decode_many(kind, blobs[:1], nw[:1], 1)
+    t0 = time.perf_counter()
+    outs = O.decode_many(kind, blobs, nw, threads)
+    dt = time.perf_counter() - t0
+    assert all(o.tobytes() == r for o, r in zip(outs, raws)), "CPU decode mismatch"
+    return blobs, dt
+
+
+def bench_legacy(a, torch, dev, world, rank, dist, local):
+    """bf16_se_single_kernel / bf16_se_tans decoded on the device.  Case 1:
+    the BASELINE config-1 tensor (16.8M values; one serial (sign,exp) stream).
+    Case 2: 16 tensors of the config-2 k/v shape (1024x4096) in one plan, all
+    streams concurrent.  One JSON line per (codec, case)."""
+    import numpy as np
+    from bigsmall_b200 import gpu
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    g = torch.Generator().manual_seed(0)
+    n1 = 4096 * 4096
+    x = torch.randn(n1, generator=g) * 0.02
+    idx = torch.randperm(n1, generator=g)[: n1 // 1000]
+    x[idx] *= 30
+    c1 = x.to(torch.bfloat16).view(torch.int16).numpy().tobytes()
+    gd = torch.Generator(device=dev).manual_seed(1)
+    kv = [gen_tensor(torch, gd, (1024, 4096), "linear", dev).view(torch.int16).cpu().numpy().tobytes()
+          for _ in range(16)]
+    stream = torch.cuda.current_stream(dev)
+    for kind, codec in (("sk", "bf16_se_single_kernel"), ("tans", "bf16_se_tans")):
+        for case, raws in (("config-1 tensor 4096x4096", [c1]), ("16 x config-2 k/v 1024x4096, one plan", kv)):
+            blobs, cpu_s = legacy_cpu_leg(kind, raws, 1 if len(raws) == 1 else threads)
+            entries, outs = [], []
+            for blob, raw in zip(blobs, raws):
+                d = torch.from_numpy(np.frombuffer(blob, dtype=np.uint8).copy()).to(dev)
+                o = torch.empty(len(raw) // 2, dtype=torch.int16, device=dev)
+                entries.append((codec, blob, d, o, len(raw) // 2))
+                outs.append(o)
+            plan = gpu.SePlan(entries, device=local)
+            ms = _timed(torch, lambda: plan.decode(stream), a.steps, a.warmup, stream)
+            plan.check(stream)
+            ok = all(o.cpu().numpy().tobytes() == r for o, r in zip(outs, raws))
+            nbytes = sum(len(r) for r in raws)
+            print(json.dumps({"config": "legacy serial format decode", "codec": codec, "case": case,
+                              "values": nbytes // 2, "decode_ms": round(ms, 3),
+                              "decoded_GBs": round(nbytes / ms / 1e6, 3),
+                              "cpu_baseline": {"value": round(nbytes / cpu_s / 1e9, 3), "unit": "GB/s",
+                                               "cores": 1 if len(raws) == 1 else threads, "kind": "port",
+                                               "sample": "the same blobs, reference decoder restated in C"},
+                              "ratio": round(sum(len(b) for b in blobs) / nbytes, 5),
+                              "gpu_launches_per_decode": 2, "verified": ok}), flush=True)
+            plan.close()
 
 
 # ---------------------------------------------------------------------------

@@ -33,6 +33,8 @@ DEV_BITS = {0x01: "header", 0x02: "freq", 0x04: "chunk_table", 0x08: "stream",
 CODER_RANS = 0
 CODER_TANS = 1
 CODER_RANS_PAIR = 2
+SE_SINGLE_KERNEL = 1
+SE_TANS = 2
 
 
 class XcTensor(ctypes.Structure):
@@ -46,6 +48,18 @@ class XcTensor(ctypes.Structure):
         ("chunk_begin", ctypes.c_uint32),
         ("chunk_count", ctypes.c_uint32),
         ("coder_mask", ctypes.c_uint32),
+    ]
+
+
+class SeBlob(ctypes.Structure):
+    """Mirror of ``bs_se_blob`` in include/bsgpu.h."""
+    _fields_ = [
+        ("codec", ctypes.c_int),
+        ("h_blob", ctypes.c_void_p),
+        ("blob_bytes", ctypes.c_uint64),
+        ("n_weights", ctypes.c_uint64),
+        ("d_blob", ctypes.c_void_p),
+        ("d_out", ctypes.c_void_p),
     ]
 
 
@@ -66,6 +80,9 @@ SIGNATURES = {
     "bs_xc_encode_workspace": (_I, [_U64, _U32, _I, ctypes.POINTER(_U64)]),
     "bs_xc_encode": (_I, [_P, _U64, _I, _I, _U32, _P, _U64, _P, _P, _U64, _P]),
     "bs_stream_probe": (_I, [_P, _P, _U64, _I, _I, _I, _P]),
+    "bs_se_plan_create": (_I, [_I, _P, _U64, _U64, _P, _P, _I, ctypes.POINTER(_P)]),
+    "bs_se_parse": (_I, [_I, _P, _U64, _U64, ctypes.POINTER(_U32)]),
+    "bs_se_plan_create_many": (_I, [ctypes.POINTER(SeBlob), _I, _I, ctypes.POINTER(_P)]),
 }
 
 _lib = None

@@ -10,7 +10,7 @@ from __future__ import annotations
 
 from typing import Callable, Optional
 
-from .codecs import bf16_parallel, exp_chunked
+from .codecs import bf16_parallel, exp_chunked, se_legacy
 
 _REGISTRY: dict[str, tuple[Callable, Callable]] = {}
 
@@ -41,11 +41,13 @@ def _dec_par(blob, extras, n_weights):
 
 register_codec(exp_chunked.CODEC, _enc_xc, _dec_xc)
 register_codec(bf16_parallel.CODEC, bf16_parallel.encode, _dec_par)
+for _name in se_legacy.CODECS:
+    register_codec(_name, se_legacy.encode, se_legacy.decoder_for(_name))
 
 
 def install_into(reference_registry) -> None:
     """Register this package's codecs in a reference codec_registry module."""
     for name, (enc, dec) in _REGISTRY.items():
-        if name == bf16_parallel.CODEC and reference_registry.get_codec(name) is not None:
+        if (name == bf16_parallel.CODEC or name in se_legacy.CODECS) and reference_registry.get_codec(name) is not None:
             enc = reference_registry.get_codec(name)[0]   # keep the reference encoder
         reference_registry.register_codec(name, enc, dec)

@@ -81,19 +81,15 @@ struct bs_plan {
     int n_items = 0;
     uint32_t coders = 0;        // decode kernels to launch (bit per coder)
     uint32_t *d_tables = nullptr;
-    // bf16_parallel_v1
-    const uint8_t *d_blob = nullptr;
-    uint16_t *d_out = nullptr;
+    // serial-stream formats (bf16_parallel_v1, bf16_se_single_kernel, bf16_se_tans)
     ParJob *d_jobs = nullptr;
     int n_jobs = 0;
     ParStream *d_streams = nullptr;
     int n_streams_total = 0;
-    uint32_t *d_buckets = nullptr;
-    uint2 *d_se_tab = nullptr;
-    uint2 *d_m_tabs = nullptr;
+    uint2 *d_buckets = nullptr;
+    uint2 *d_tabs = nullptr;
     uint16_t *d_se_sym = nullptr;
     uint8_t *d_mant = nullptr;
-    uint32_t par_n_streams = 0;
 };
 
 namespace {
@@ -273,13 +269,12 @@ int bs_plan_decode(bs_plan *p, void *stream) {
             e = launch_xc_decode(p->d_tens, p->d_items, p->n_items, p->d_tables, p->d_errs, p->coders, s);
     } else if (p->kind == kPlanPar) {
         if (p->n_internal == 0) return BS_OK;
-        e = cudaMemsetAsync(p->d_errs, 0, 4, s);
+        e = cudaMemsetAsync(p->d_errs, 0, 4ull * p->n_internal, s);
         if (e == cudaSuccess)
-            e = launch_par_jobs(p->d_blob, p->d_jobs, p->n_jobs, p->d_se_tab, p->d_m_tabs, p->d_se_sym,
-                                p->d_mant, p->d_errs, s);
+            e = launch_par_jobs(p->d_jobs, p->n_jobs, p->d_tabs, p->d_se_sym, p->d_mant, p->d_errs, s);
         if (e == cudaSuccess)
             e = launch_par_merge(p->d_streams, p->n_streams_total, p->d_buckets, p->d_se_sym, p->d_mant,
-                                 p->d_out, p->par_n_streams, p->d_errs, s);
+                                 p->d_errs, s);
     } else {
         return fail(BS_E_INVALID_ARG, "unknown plan kind");
     }
@@ -299,7 +294,7 @@ int bs_plan_check(bs_plan *p, void *stream, uint32_t *status_out) {
     bool bad = false;
     std::string msg;
     for (int i = 0; i < p->n_tensors; i++) {
-        int k = p->kind == kPlanXc ? p->user_to_internal[i] : (p->n_internal ? 0 : -1);
+        int k = p->user_to_internal[i];
         uint32_t st = k >= 0 ? p->h_errs[k] : 0u;
         if (status_out) status_out[i] = st;
         if (st) {
@@ -392,79 +387,171 @@ int bs_xc_decode_noalloc(const bs_xc_tensor *tensors, int n_tensors, void *strea
 // --------------------------------------------------------------------------
 // bf16_parallel_v1 (bigsmall/codecs/bf16_parallel.py:15-52 layout)
 // --------------------------------------------------------------------------
-int bs_par_plan_create(const uint8_t *h, uint64_t len, uint64_t n_weights, const void *d_blob, void *d_out,
-                       int device, bs_plan **out_plan) {
-    if (!out_plan) return fail(BS_E_INVALID_ARG, "out_plan is NULL");
-    *out_plan = nullptr;
-    int ndev = 0;
-    if (cudaGetDeviceCount(&ndev) != cudaSuccess || device < 0 || device >= ndev) {
-        cudaGetLastError();
-        return fail(BS_E_INVALID_ARG, "invalid CUDA device " + std::to_string(device));
-    }
-    DeviceGuard guard(device);
-    auto *p = new bs_plan();
-    p->kind = kPlanPar;
-    p->device = device;
-    p->n_tensors = 1;
-    // bf16_parallel.py:268-269: nothing to decode
-    if (n_weights == 0 || len == 0) {
-        p->n_internal = 0;
-        *out_plan = p;
-        return BS_OK;
-    }
-    if (!h) { delete p; return fail(BS_E_INVALID_ARG, "host blob is NULL"); }
-    uint64_t pos = 0;
-    int rc = BS_OK;
-    auto need = [&](uint64_t k) -> bool {
-        if (pos + k > len) { rc = fail(BS_E_TRUNCATED, "bf16_parallel: blob truncated in header"); return false; }
+}  // extern "C"
+
+// --------------------------------------------------------------------------
+// Serial-stream formats: bf16_parallel_v1 and the legacy bf16_se_* codecs.
+// The host parses the framing into independent rANS jobs (one per SE stream
+// and per exponent bucket), per-stream merge records and decode tables; the
+// device runs par_jobs_kernel + par_merge_kernel.
+// --------------------------------------------------------------------------
+namespace {
+
+struct SerialLayout {
+    std::vector<ParJob> jobs;
+    std::vector<ParStream> streams;
+    std::vector<uint2> buckets;          // (exponent, count) per stream, blob order
+    std::vector<uint2> tabs;             // decode tables: 4096 (SE) or 1024 (mantissa) entries each
+    uint64_t n_total = 0;                // values of all tensors (scratch size)
+};
+
+// Bounds-checked little-endian reader over the host copy of a blob.  `take`
+// clamps like a Python slice / BytesIO.read; the others fail on truncation.
+struct Rd {
+    const uint8_t *h;
+    uint64_t len, pos;
+    bool bad = false;
+    bool need(uint64_t k) {
+        if (bad || pos + k > len || pos + k < pos) { bad = true; return false; }
         return true;
-    };
-    // _unpack_header (bf16_parallel.py:138-183)
-    if (!need(4)) { delete p; return rc; }
-    if (memcmp(h, "PAR1", 4) != 0) { delete p; return fail(BS_E_BAD_MAGIC, "bf16_parallel: bad magic"); }
-    pos = 4;
-    if (!need(10)) { delete p; return rc; }
-    const uint64_t n = rd32(h + 4);
-    const uint32_t ns = rd16(h + 8), p_se = rd16(h + 10), p_m = rd16(h + 12);
-    pos = 14;
-    if (p_se != 12 || p_m != 10) {
-        delete p;
+    }
+    uint32_t u8() { if (!need(1)) return 0; return h[pos++]; }
+    uint32_t u16() { if (!need(2)) return 0; uint32_t v = rd16(h + pos); pos += 2; return v; }
+    uint32_t u32() { if (!need(4)) return 0; uint32_t v = rd32(h + pos); pos += 4; return v; }
+    uint64_t take(uint64_t k, uint64_t *got) {
+        const uint64_t at = pos, avail = pos < len ? len - pos : 0;
+        *got = std::min(k, avail);
+        pos += *got;
+        return at;
+    }
+};
+
+// Append a decode table: slot -> {sym | freq << 16, slot - cum[sym]}; slots
+// past the frequency sum map to symbol 0 (rans.build_slot_to_symbol /
+// numba_rans zero-initialised tables).  Frequencies above M are rejected,
+// which keeps the decoder's 32-bit state exact.  Returns the table's first
+// entry, or -1.
+int64_t add_table(SerialLayout &L, const std::vector<uint32_t> &f, uint32_t M) {
+    std::vector<uint32_t> cum(f.size());
+    uint64_t c = 0;
+    for (size_t s = 0; s < f.size(); s++) {
+        if (f[s] > M) return -1;
+        cum[s] = static_cast<uint32_t>(std::min<uint64_t>(c, 0xFFFFFFFFull));
+        c += f[s];
+    }
+    const size_t base = L.tabs.size();
+    if (base + M > 0xFFFFFFFFull) return -1;
+    L.tabs.resize(base + M);
+    for (uint32_t slot = 0; slot < M; slot++) L.tabs[base + slot] = make_uint2(f[0] << 16, slot);
+    for (size_t s = 0; s < f.size(); s++)
+        for (uint64_t j = 0; j < f[s] && cum[s] + j < M; j++)
+            L.tabs[base + cum[s] + j] = make_uint2(static_cast<uint32_t>(s) | (f[s] << 16), static_cast<uint32_t>(j));
+    return static_cast<int64_t>(base);
+}
+
+uint64_t freq_sum(const std::vector<uint32_t> &f) {
+    uint64_t c = 0;
+    for (uint32_t v : f) c += v;
+    return c;
+}
+
+ParJob word_job(uint64_t addr, uint64_t avail, uint64_t n_words, uint64_t n_syms, uint32_t tab_off, uint32_t flags,
+                uint32_t tensor, uint32_t state0 = 0) {
+    ParJob j{};
+    j.data = addr;
+    j.out_off = 0;
+    j.avail = static_cast<uint32_t>(avail);
+    j.n_words = static_cast<uint32_t>(n_words);
+    j.n_syms = static_cast<uint32_t>(n_syms);
+    j.tab_off = tab_off;
+    j.state0 = state0;
+    j.flags = flags;
+    j.tensor = tensor;
+    return j;
+}
+
+// rans.py stream of `got` bytes: state = bytes 0..3, words from byte 4, an odd
+// last byte dropped (shifted in as a zero word)
+ParJob rans_py_job(uint64_t addr, uint64_t got, uint64_t n_syms, uint32_t tab_off, uint32_t flags, uint32_t tensor) {
+    const uint64_t avail = got < 4 ? got : 4 + ((got - 4) & ~1ull);
+    const uint64_t n_words = got < 4 ? got / 2 : 2 + (got - 4 + 1) / 2;
+    return word_job(addr, avail, n_words, n_syms, tab_off, flags | kJobStateInStream, tensor);
+}
+
+// numba_rans stream of `got` bytes: zero-padded to even length, read as u16
+ParJob numba_job(uint64_t addr, uint64_t got, uint64_t n_syms, uint32_t tab_off, uint32_t flags, uint32_t tensor) {
+    return word_job(addr, got, (got + 1) / 2, n_syms, tab_off, flags | kJobStateInStream, tensor);
+}
+
+// One blob being added to a layout: host bytes, device address, output.
+struct SerialBlob {
+    const uint8_t *h;
+    uint64_t len;
+    uint64_t n_weights;
+    uint64_t d_blob;       // device address of byte 0 (0 while only parsing)
+    uint64_t d_out;
+    uint32_t tensor;
+};
+
+// Finish one stream: bucket jobs get their offset in the stream's sorted
+// mantissa run (buckets in ascending exponent order, rans bincount/cumsum).
+int finish_stream(SerialLayout &L, ParStream S, std::vector<std::pair<uint32_t, ParJob>> &bj, const std::string &who) {
+    std::vector<uint64_t> cnt(256, 0);
+    uint64_t total = 0;
+    for (auto &x : bj) { cnt[x.first] = x.second.n_syms; total += x.second.n_syms; }
+    if (total != S.n_in) return fail(BS_E_CORRUPT, who + "bucket counts do not sum to the value count");
+    std::vector<uint64_t> bstart(257, 0);
+    for (int e = 0; e < 256; e++) bstart[e + 1] = bstart[e] + cnt[e];
+    for (auto &x : bj) {
+        x.second.out_off = S.mant_off + bstart[x.first];
+        L.jobs.push_back(x.second);
+    }
+    L.streams.push_back(S);
+    return BS_OK;
+}
+
+// _unpack_header + decode, bigsmall/codecs/bf16_parallel.py:138-183, :262-352
+int parse_par1(SerialLayout &L, const SerialBlob &B) {
+    const uint8_t *h = B.h;
+    const uint64_t len = B.len;
+    Rd r{h, len, 0};
+    const char *T = "bf16_parallel: blob truncated in header";
+    if (len < 4) return fail(BS_E_TRUNCATED, T);
+    if (memcmp(h, "PAR1", 4) != 0) return fail(BS_E_BAD_MAGIC, "bf16_parallel: bad magic");
+    r.pos = 4;
+    const uint64_t n = r.u32();
+    const uint32_t ns = r.u16(), p_se = r.u16(), p_m = r.u16();
+    if (r.bad) return fail(BS_E_TRUNCATED, T);
+    if (p_se != 12 || p_m != 10)
         return fail(BS_E_PRECISION, "bf16_parallel: precision mismatch (header SE=" + std::to_string(p_se) +
                                         " M=" + std::to_string(p_m) + " vs codec SE=12 M=10)");
-    }
-    if (!need(2)) { delete p; return rc; }
-    const uint32_t n_se_nz = rd16(h + pos);
-    pos += 2;
-    if (!need(6ull * n_se_nz)) { delete p; return rc; }
+    const uint32_t n_se_nz = r.u16();
+    if (!r.need(6ull * n_se_nz)) return fail(BS_E_TRUNCATED, T);
     std::vector<uint32_t> se_f(512, 0);
     for (uint32_t i = 0; i < n_se_nz; i++) {
-        uint32_t s = rd16(h + pos + 2 * i);
-        if (s >= 512) { delete p; return fail(BS_E_CORRUPT, "bf16_parallel: SE symbol index out of range"); }
-        se_f[s] = rd32(h + pos + 2ull * n_se_nz + 4 * i);
+        const uint32_t s = rd16(h + r.pos + 2 * i);
+        if (s >= 512) return fail(BS_E_CORRUPT, "bf16_parallel: SE symbol index out of range");
+        se_f[s] = rd32(h + r.pos + 2ull * n_se_nz + 4 * i);
     }
-    pos += 6ull * n_se_nz;
-    if (!need(4)) { delete p; return rc; }
-    const uint32_t n_exps = rd32(h + pos);
-    pos += 4;
-    if (!need(2ull * n_exps)) { delete p; return rc; }
+    r.pos += 6ull * n_se_nz;
+    const uint32_t n_exps = r.u32();
+    if (!r.need(2ull * n_exps)) return fail(BS_E_TRUNCATED, T);
+    const uint64_t exps_pos = r.pos;
+    r.pos += 2ull * n_exps;
     std::vector<int> exp_tab(256, -1);
     std::vector<std::vector<uint32_t>> mfreq;
-    const uint64_t exps_pos = pos;
-    pos += 2ull * n_exps;
     for (uint32_t q = 0; q < n_exps; q++) {
-        uint32_t ev = rd16(h + exps_pos + 2 * q);
-        if (!need(1)) { delete p; return rc; }
-        uint32_t nzc = h[pos];
-        pos += 1;
-        if (!need(5ull * nzc)) { delete p; return rc; }
-        if (ev >= 256) { delete p; return fail(BS_E_CORRUPT, "bf16_parallel: exponent out of range"); }
+        const uint32_t ev = rd16(h + exps_pos + 2 * q);
+        const uint32_t nzc = r.u8();
+        if (!r.need(5ull * nzc)) return fail(BS_E_TRUNCATED, T);
+        if (ev >= 256) return fail(BS_E_CORRUPT, "bf16_parallel: exponent out of range");
         std::vector<uint32_t> mf(128, 0);
         for (uint32_t i = 0; i < nzc; i++) {
-            uint32_t m = h[pos + i];
-            if (m >= 128) { delete p; return fail(BS_E_CORRUPT, "bf16_parallel: mantissa index out of range"); }
-            mf[m] = rd32(h + pos + nzc + 4 * i);
+            const uint32_t m = h[r.pos + i];
+            if (m >= 128) return fail(BS_E_CORRUPT, "bf16_parallel: mantissa index out of range");
+            mf[m] = rd32(h + r.pos + nzc + 4 * i);
         }
-        pos += 5ull * nzc;
+        r.pos += 5ull * nzc;
         if (exp_tab[ev] < 0) {
             exp_tab[ev] = static_cast<int>(mfreq.size());
             mfreq.push_back(mf);
@@ -472,47 +559,23 @@ int bs_par_plan_create(const uint8_t *h, uint64_t len, uint64_t n_weights, const
             mfreq[exp_tab[ev]] = mf;   // later entries overwrite (dict semantics)
         }
     }
-    if (n != n_weights) {
-        delete p;
+    if (n != B.n_weights)
         return fail(BS_E_COUNT_MISMATCH, "bf16_parallel: weight count mismatch (" + std::to_string(n) + " vs " +
-                                             std::to_string(n_weights) + ")");
-    }
-    if (ns == 0) { delete p; return fail(BS_E_CORRUPT, "bf16_parallel: zero streams"); }
-    if (!d_blob || !d_out || !on_device(d_blob, device) || !on_device(d_out, device)) {
-        delete p;
-        return fail(BS_E_INVALID_ARG, "d_blob/d_out must be device memory of device " + std::to_string(device));
-    }
-    const uint64_t header_end = pos;
+                                             std::to_string(B.n_weights) + ")");
+    if (ns == 0) return fail(BS_E_CORRUPT, "bf16_parallel: zero streams");
     const uint64_t n_off = static_cast<uint64_t>(ns) + 1;
-    if (header_end + 4 * n_off > len) { delete p; return fail(BS_E_TRUNCATED, "bf16_parallel: offset table truncated"); }
-    const uint8_t *offt = h + header_end;
-    const uint64_t payload_start = header_end + 4 * n_off;
-
-    // decode tables: slot -> {sym | freq[sym] << 16, cum[sym]}; unassigned slots
-    // map to symbol 0 like rans.build_slot_to_symbol's zero-initialised table
-    auto build_tab = [](const std::vector<uint32_t> &f, uint32_t M, std::vector<uint2> &tab) {
-        std::vector<uint32_t> cum(f.size());
-        uint64_t c = 0;
-        for (size_t s = 0; s < f.size(); s++) { cum[s] = static_cast<uint32_t>(c); c += f[s]; }
-        tab.assign(M, make_uint2(0u | (std::min<uint32_t>(f[0], 0xFFFF) << 16), cum[0]));
-        for (size_t s = 0; s < f.size(); s++)
-            for (uint64_t j = 0; j < f[s] && cum[s] + j < M; j++)
-                tab[cum[s] + j] = make_uint2(static_cast<uint32_t>(s) | (std::min<uint32_t>(f[s], 0xFFFF) << 16), cum[s]);
-    };
-    std::vector<uint2> se_tab, m_tabs;
-    build_tab(se_f, 4096, se_tab);
-    for (auto &mf : mfreq) {
-        std::vector<uint2> t;
-        build_tab(mf, 1024, t);
-        m_tabs.insert(m_tabs.end(), t.begin(), t.end());
+    if (!r.need(4 * n_off)) return fail(BS_E_TRUNCATED, "bf16_parallel: offset table truncated");
+    const uint8_t *offt = h + r.pos;
+    const uint64_t payload_start = r.pos + 4 * n_off;
+    const int64_t se_tab = add_table(L, se_f, 4096);
+    if (se_tab < 0) return fail(BS_E_CORRUPT, "bf16_parallel: SE frequency above M");
+    std::vector<uint32_t> m_tab(mfreq.size());
+    for (size_t t = 0; t < mfreq.size(); t++) {
+        const int64_t o = add_table(L, mfreq[t], 1024);
+        if (o < 0) return fail(BS_E_CORRUPT, "bf16_parallel: mantissa frequency above M");
+        m_tab[t] = static_cast<uint32_t>(o);
     }
-    for (uint32_t v : se_f)
-        if (v > 0xFFFF) { delete p; return fail(BS_E_CORRUPT, "bf16_parallel: SE frequency out of range"); }
-
-    std::vector<ParJob> jobs;
-    std::vector<ParStream> streams;
-    std::vector<uint2> buckets;
-    uint64_t se_cur = 0;
+    uint64_t se_cur = L.n_total;
     for (uint32_t k = 0; k < ns; k++) {
         const uint64_t nin = k < n ? (n - 1 - k) / ns + 1 : 0;
         if (nin == 0) continue;
@@ -520,99 +583,256 @@ int bs_par_plan_create(const uint8_t *h, uint64_t len, uint64_t n_weights, const
         a = std::min(a, len);
         b = std::min(b, len);
         if (b < a) b = a;
-        uint64_t q = a;
+        Rd s{h, b, a};
         const std::string who = "bf16_parallel: stream " + std::to_string(k) + ": ";
-        if (q + 4 > b) { delete p; return fail(BS_E_TRUNCATED, who + "truncated"); }
-        const uint32_t se_len = rd32(h + q);
-        q += 4;
-        const uint64_t se_got = std::min<uint64_t>(se_len, b - q);
-        ParJob sej{q, static_cast<uint32_t>(se_got), static_cast<uint32_t>(nin), se_cur, 0, 1};
-        jobs.push_back(sej);
-        q += se_got;
-        if (q + 4 > b) { delete p; return fail(BS_E_TRUNCATED, who + "truncated"); }
-        const uint32_t nze = rd32(h + q);
-        q += 4;
-        if (q + 2ull * nze > b) { delete p; return fail(BS_E_TRUNCATED, who + "truncated"); }
-        const uint64_t sx = q;
-        q += 2ull * nze;
+        const uint32_t se_len = s.u32();
+        if (s.bad) return fail(BS_E_TRUNCATED, who + "truncated");
+        uint64_t got;
+        const uint64_t se_at = s.take(se_len, &got);
+        L.jobs.push_back(rans_py_job(B.d_blob + se_at, got, nin, static_cast<uint32_t>(se_tab), kJobSe, B.tensor));
+        L.jobs.back().out_off = se_cur;
+        const uint32_t nze = s.u32();
+        if (!s.need(2ull * nze)) return fail(BS_E_TRUNCATED, who + "truncated");
+        const uint64_t sx = s.pos;
+        s.pos += 2ull * nze;
         ParStream S{};
         S.se_off = se_cur;
         S.mant_off = se_cur;
+        S.out = B.d_out;
         S.n_in = static_cast<uint32_t>(nin);
         S.k = k;
-        S.bucket_first = static_cast<uint32_t>(buckets.size());
+        S.stride = ns;
+        S.bucket_first = static_cast<uint32_t>(L.buckets.size());
         S.n_buckets = nze;
-        std::vector<uint64_t> cnt(256, 0);
+        S.tensor = B.tensor;
         std::vector<uint8_t> seen(256, 0);
         std::vector<std::pair<uint32_t, ParJob>> bj;
-        uint64_t total = 0;
         for (uint32_t qq = 0; qq < nze; qq++) {
             const uint32_t ev = rd16(h + sx + 2ull * qq);
-            if (q + 8 > b) { delete p; return fail(BS_E_TRUNCATED, who + "truncated"); }
-            const uint32_t count = rd32(h + q), blen = rd32(h + q + 4);
-            q += 8;
-            const uint64_t got = std::min<uint64_t>(blen, b - q);
-            if (ev >= 256 || exp_tab[ev] < 0) { delete p; return fail(BS_E_CORRUPT, who + "bucket exponent has no table"); }
-            if (seen[ev]) { delete p; return fail(BS_E_CORRUPT, who + "duplicate bucket exponent"); }
+            const uint32_t count = s.u32(), blen = s.u32();
+            if (s.bad) return fail(BS_E_TRUNCATED, who + "truncated");
+            const uint64_t at = s.take(blen, &got);
+            if (ev >= 256 || exp_tab[ev] < 0) return fail(BS_E_CORRUPT, who + "bucket exponent has no table");
+            if (seen[ev]) return fail(BS_E_CORRUPT, who + "duplicate bucket exponent");
             seen[ev] = 1;
-            cnt[ev] = count;
-            total += count;
-            ParJob mj{q, static_cast<uint32_t>(got), count, 0, static_cast<uint32_t>(exp_tab[ev]) + 1, 0};
-            bj.push_back({ev, mj});
-            buckets.push_back(make_uint2(ev, count));
-            q += got;
+            bj.push_back({ev, rans_py_job(B.d_blob + at, got, count, m_tab[exp_tab[ev]], 0, B.tensor)});
+            L.buckets.push_back(make_uint2(ev, count));
         }
-        if (total != nin) { delete p; return fail(BS_E_CORRUPT, who + "bucket counts do not sum to the stream size"); }
-        std::vector<uint64_t> bstart(257, 0);
-        for (int e = 0; e < 256; e++) bstart[e + 1] = bstart[e] + cnt[e];
-        for (auto &x : bj) {
-            x.second.out_off = S.mant_off + bstart[x.first];
-            jobs.push_back(x.second);
-        }
-        streams.push_back(S);
+        const int rc = finish_stream(L, S, bj, who);
+        if (rc) return rc;
         se_cur += nin;
     }
-    std::stable_sort(jobs.begin(), jobs.end(), [](const ParJob &x, const ParJob &y) { return x.n_syms > y.n_syms; });
-    if (jobs.size() > 0x7FFFFFFFull || streams.size() > 0x7FFFFFFFull) {
-        delete p;
+    L.n_total += n;
+    return BS_OK;
+}
+
+// One legacy tensor = one stream: SE job + bucket jobs, contiguous output.
+ParStream legacy_stream(SerialLayout &L, const SerialBlob &B, uint64_t n, uint32_t n_buckets) {
+    ParStream S{};
+    S.se_off = L.n_total;
+    S.mant_off = L.n_total;
+    S.out = B.d_out;
+    S.n_in = static_cast<uint32_t>(n);
+    S.k = 0;
+    S.stride = 1;
+    S.bucket_first = static_cast<uint32_t>(L.buckets.size());
+    S.n_buckets = n_buckets;
+    S.tensor = B.tensor;
+    return S;
+}
+
+// bigsmall/codecs/single_kernel.py:432-580 _decode_full_kernel framing:
+// [u32 n][u16 n_se_nz][u16 sym x n_se_nz][u32 freq x n_se_nz][u32 state][u32 n_words][u16 x n_words]
+// [u32 n_buckets] then per bucket [u16 e][u8 mnz][u8 sym x mnz][u32 freq x mnz][u32 state][u32 count]
+// [u32 n_words][u16 x n_words].  Tables must sum to M (the reference would
+// leave slots uninitialised otherwise).
+int parse_sk(SerialLayout &L, const SerialBlob &B) {
+    const uint8_t *h = B.h;
+    Rd r{h, B.len, 0};
+    const char *T = "bf16_se_single_kernel: blob truncated";
+    const uint64_t n = r.u32();
+    if (r.bad) return fail(BS_E_TRUNCATED, T);
+    if (n != B.n_weights)
+        return fail(BS_E_COUNT_MISMATCH, "bf16_se_single_kernel: weight count mismatch (" + std::to_string(n) +
+                                             " vs " + std::to_string(B.n_weights) + ")");
+    const uint32_t n_se_nz = r.u16();
+    if (!r.need(6ull * n_se_nz)) return fail(BS_E_TRUNCATED, T);
+    std::vector<uint32_t> se_f(512, 0);
+    for (uint32_t i = 0; i < n_se_nz; i++) {
+        const uint32_t s = rd16(h + r.pos + 2 * i);
+        if (s >= 512) return fail(BS_E_CORRUPT, "bf16_se_single_kernel: SE symbol out of range");
+        se_f[s] = rd32(h + r.pos + 2ull * n_se_nz + 4 * i);
+    }
+    r.pos += 6ull * n_se_nz;
+    if (freq_sum(se_f) != 4096) return fail(BS_E_CORRUPT, "bf16_se_single_kernel: SE frequencies do not sum to 4096");
+    const int64_t se_tab = add_table(L, se_f, 4096);
+    if (se_tab < 0) return fail(BS_E_CORRUPT, "bf16_se_single_kernel: SE frequency above M");
+    const uint32_t st = r.u32(), nc = r.u32();
+    if (!r.need(2ull * nc)) return fail(BS_E_TRUNCATED, T);
+    ParJob se = word_job(B.d_blob + r.pos, 2ull * nc, nc, n, static_cast<uint32_t>(se_tab), kJobSe, B.tensor, st);
+    se.out_off = L.n_total;
+    L.jobs.push_back(se);
+    r.pos += 2ull * nc;
+    const uint32_t nb = r.u32();
+    if (r.bad) return fail(BS_E_TRUNCATED, T);
+    ParStream S = legacy_stream(L, B, n, nb);
+    std::vector<uint8_t> seen(256, 0);
+    std::vector<std::pair<uint32_t, ParJob>> bj;
+    for (uint32_t q = 0; q < nb; q++) {
+        const uint32_t e = r.u16(), mnz = r.u8();
+        if (!r.need(5ull * mnz)) return fail(BS_E_TRUNCATED, T);
+        if (e >= 256) return fail(BS_E_CORRUPT, "bf16_se_single_kernel: exponent out of range");
+        std::vector<uint32_t> mf(128, 0);
+        for (uint32_t i = 0; i < mnz; i++) {
+            const uint32_t m = h[r.pos + i];
+            if (m >= 128) return fail(BS_E_CORRUPT, "bf16_se_single_kernel: mantissa symbol out of range");
+            mf[m] = rd32(h + r.pos + mnz + 4 * i);
+        }
+        r.pos += 5ull * mnz;
+        if (freq_sum(mf) != 1024) return fail(BS_E_CORRUPT, "bf16_se_single_kernel: mantissa frequencies do not sum to 1024");
+        const uint32_t mst = r.u32(), bsize = r.u32(), mnc = r.u32();
+        if (!r.need(2ull * mnc)) return fail(BS_E_TRUNCATED, T);
+        if (seen[e]) return fail(BS_E_CORRUPT, "bf16_se_single_kernel: duplicate bucket exponent");
+        seen[e] = 1;
+        const int64_t t = add_table(L, mf, 1024);
+        if (t < 0) return fail(BS_E_CORRUPT, "bf16_se_single_kernel: mantissa frequency above M");
+        bj.push_back({e, word_job(B.d_blob + r.pos, 2ull * mnc, mnc, bsize, static_cast<uint32_t>(t), 0, B.tensor, mst)});
+        L.buckets.push_back(make_uint2(e, bsize));
+        r.pos += 2ull * mnc;
+    }
+    const int rc = finish_stream(L, S, bj, "bf16_se_single_kernel: ");
+    if (rc == BS_OK) L.n_total += n;
+    return rc;
+}
+
+// bigsmall/codecs/bf16_tans.py:121-167 framing (streams are numba_rans.py
+// rANS streams, :168-217): [u32 n][u16 se_nz][u16 sym x se_nz][u32 freq x se_nz]
+// [u32 cw_len][SE stream][u32 m_len][m section]; m section = [u32 n_exps]
+// [u16 e x n_exps] then per exponent [u32 count][u8 nnz][u8 sym x nnz]
+// [u32 freq x nnz][u32 len][stream].  Payload reads clamp like BytesIO.read.
+int parse_setans(SerialLayout &L, const SerialBlob &B) {
+    const uint8_t *h = B.h;
+    Rd r{h, B.len, 0};
+    const char *T = "bf16_se_tans: blob truncated";
+    const uint64_t n = r.u32();
+    if (r.bad) return fail(BS_E_TRUNCATED, T);
+    if (n != B.n_weights)
+        return fail(BS_E_COUNT_MISMATCH, "bf16_se_tans: weight count mismatch (" + std::to_string(n) + " vs " +
+                                             std::to_string(B.n_weights) + ")");
+    const uint32_t se_nz = r.u16();
+    if (!r.need(6ull * se_nz)) return fail(BS_E_TRUNCATED, T);
+    std::vector<uint32_t> se_f(512, 0);
+    for (uint32_t i = 0; i < se_nz; i++) {
+        const uint32_t s = rd16(h + r.pos + 2 * i);
+        if (s >= 512) return fail(BS_E_CORRUPT, "bf16_se_tans: SE symbol out of range");
+        se_f[s] = rd32(h + r.pos + 2ull * se_nz + 4 * i);
+    }
+    r.pos += 6ull * se_nz;
+    const uint32_t cwl = r.u32();
+    if (r.bad) return fail(BS_E_TRUNCATED, T);
+    uint64_t got;
+    const uint64_t cw = r.take(cwl, &got);
+    if (got < 4) return fail(BS_E_TRUNCATED, "bf16_se_tans: SE stream shorter than its state");
+    const int64_t se_tab = add_table(L, se_f, 4096);
+    if (se_tab < 0) return fail(BS_E_CORRUPT, "bf16_se_tans: SE frequency above M");
+    ParJob se = numba_job(B.d_blob + cw, got, n, static_cast<uint32_t>(se_tab), kJobSe, B.tensor);
+    se.out_off = L.n_total;
+    L.jobs.push_back(se);
+    const uint32_t mbl = r.u32();
+    if (r.bad) return fail(BS_E_TRUNCATED, T);
+    const uint64_t mb = r.take(mbl, &got);
+    Rd m{h, mb + got, mb};
+    const uint32_t ne = m.u32();
+    if (!m.need(2ull * ne)) return fail(BS_E_TRUNCATED, T);
+    const uint64_t ex = m.pos;
+    m.pos += 2ull * ne;
+    ParStream S = legacy_stream(L, B, n, ne);
+    std::vector<uint8_t> seen(256, 0);
+    std::vector<std::pair<uint32_t, ParJob>> bj;
+    for (uint32_t q = 0; q < ne; q++) {
+        const uint32_t ev = rd16(h + ex + 2ull * q);
+        const uint32_t nb = m.u32(), nnz = m.u8();
+        if (!m.need(5ull * nnz)) return fail(BS_E_TRUNCATED, T);
+        std::vector<uint32_t> mf(128, 0);
+        bool bad_sym = false;
+        for (uint32_t i = 0; i < nnz; i++) {
+            const uint32_t s = h[m.pos + i];
+            if (s >= 128) bad_sym = true;
+            else mf[s] = rd32(h + m.pos + nnz + 4 * i);
+        }
+        m.pos += 5ull * nnz;
+        const uint32_t cl = m.u32();
+        if (m.bad) return fail(BS_E_TRUNCATED, T);
+        uint64_t cgot;
+        const uint64_t c2 = m.take(cl, &cgot);
+        if (ev >= 256 || bad_sym) return fail(BS_E_CORRUPT, "bf16_se_tans: bucket symbol out of range");
+        if (seen[ev]) return fail(BS_E_CORRUPT, "bf16_se_tans: duplicate bucket exponent");
+        seen[ev] = 1;
+        if (nb > 0 && cgot < 4) return fail(BS_E_TRUNCATED, "bf16_se_tans: bucket stream shorter than its state");
+        const int64_t t = add_table(L, mf, 1024);
+        if (t < 0) return fail(BS_E_CORRUPT, "bf16_se_tans: mantissa frequency above M");
+        bj.push_back({ev, numba_job(B.d_blob + c2, cgot, nb, static_cast<uint32_t>(t), 0, B.tensor)});
+        L.buckets.push_back(make_uint2(ev, nb));
+    }
+    const int rc = finish_stream(L, S, bj, "bf16_se_tans: ");
+    if (rc == BS_OK) L.n_total += n;
+    return rc;
+}
+
+int parse_serial(int codec, SerialLayout &L, const SerialBlob &B) {
+    switch (codec) {
+        case BS_SE_SINGLE_KERNEL: return parse_sk(L, B);
+        case BS_SE_TANS: return parse_setans(L, B);
+        default: return fail(BS_E_INVALID_ARG, "unknown legacy codec " + std::to_string(codec));
+    }
+}
+
+// Upload a parsed layout into a new plan (kind kPlanPar) over n_tensors user
+// tensors; u2i maps them to status words (-1: nothing to decode).
+int make_serial_plan(SerialLayout &L, int device, int n_tensors, std::vector<int> u2i, int n_internal,
+                     bs_plan **out_plan) {
+    std::stable_sort(L.jobs.begin(), L.jobs.end(), [](const ParJob &x, const ParJob &y) { return x.n_syms > y.n_syms; });
+    if (L.jobs.size() > 0x7FFFFFFFull || L.streams.size() > 0x7FFFFFFFull)
         return fail(BS_E_INVALID_ARG, "too many streams");
+    auto *p = new bs_plan();
+    p->kind = kPlanPar;
+    p->device = device;
+    p->n_tensors = n_tensors;
+    p->user_to_internal = std::move(u2i);
+    p->n_internal = n_internal;
+    if (n_internal == 0) {
+        *out_plan = p;
+        return BS_OK;
     }
     Carve cv;
-    const uint64_t o_j = cv.take(sizeof(ParJob) * jobs.size());
-    const uint64_t o_s = cv.take(sizeof(ParStream) * streams.size());
-    const uint64_t o_b = cv.take(sizeof(uint2) * std::max<size_t>(1, buckets.size()));
-    const uint64_t o_st = cv.take(sizeof(uint2) * se_tab.size());
-    const uint64_t o_mt = cv.take(sizeof(uint2) * std::max<size_t>(1, m_tabs.size()));
-    const uint64_t o_ss = cv.take(2 * n);
-    const uint64_t o_m = cv.take(n);
-    const uint64_t o_e = cv.take(4);
-    rc = alloc_plan_mem(p, cv.off);
+    const uint64_t o_j = cv.take(sizeof(ParJob) * L.jobs.size());
+    const uint64_t o_s = cv.take(sizeof(ParStream) * L.streams.size());
+    const uint64_t o_b = cv.take(sizeof(uint2) * std::max<size_t>(1, L.buckets.size()));
+    const uint64_t o_t = cv.take(sizeof(uint2) * std::max<size_t>(1, L.tabs.size()));
+    const uint64_t o_ss = cv.take(2 * L.n_total);
+    const uint64_t o_m = cv.take(L.n_total);
+    const uint64_t o_e = cv.take(4ull * n_internal);
+    int rc = alloc_plan_mem(p, cv.off);
     if (rc) { free_plan(p); return rc; }
     auto *base = static_cast<uint8_t *>(p->d_mem);
-    p->d_blob = static_cast<const uint8_t *>(d_blob);
-    p->d_out = static_cast<uint16_t *>(d_out);
     p->d_jobs = reinterpret_cast<ParJob *>(base + o_j);
-    p->n_jobs = static_cast<int>(jobs.size());
+    p->n_jobs = static_cast<int>(L.jobs.size());
     p->d_streams = reinterpret_cast<ParStream *>(base + o_s);
-    p->n_streams_total = static_cast<int>(streams.size());
-    p->d_buckets = reinterpret_cast<uint32_t *>(base + o_b);
-    p->d_se_tab = reinterpret_cast<uint2 *>(base + o_st);
-    p->d_m_tabs = reinterpret_cast<uint2 *>(base + o_mt);
+    p->n_streams_total = static_cast<int>(L.streams.size());
+    p->d_buckets = reinterpret_cast<uint2 *>(base + o_b);
+    p->d_tabs = reinterpret_cast<uint2 *>(base + o_t);
     p->d_se_sym = reinterpret_cast<uint16_t *>(base + o_ss);
     p->d_mant = base + o_m;
     p->d_errs = reinterpret_cast<uint32_t *>(base + o_e);
-    p->par_n_streams = ns;
-    p->n_internal = 1;
     cudaError_t e = cudaSuccess;
     auto up = [&](void *dst, const void *src, size_t bytes) {
         if (e == cudaSuccess && bytes) e = cudaMemcpy(dst, src, bytes, cudaMemcpyHostToDevice);
     };
-    up(p->d_jobs, jobs.data(), sizeof(ParJob) * jobs.size());
-    up(p->d_streams, streams.data(), sizeof(ParStream) * streams.size());
-    up(p->d_buckets, buckets.data(), sizeof(uint2) * buckets.size());
-    up(p->d_se_tab, se_tab.data(), sizeof(uint2) * se_tab.size());
-    up(p->d_m_tabs, m_tabs.data(), sizeof(uint2) * m_tabs.size());
-    if (e == cudaSuccess) e = cudaMallocHost(&p->h_errs, 4);
+    up(p->d_jobs, L.jobs.data(), sizeof(ParJob) * L.jobs.size());
+    up(p->d_streams, L.streams.data(), sizeof(ParStream) * L.streams.size());
+    up(p->d_buckets, L.buckets.data(), sizeof(uint2) * L.buckets.size());
+    up(p->d_tabs, L.tabs.data(), sizeof(uint2) * L.tabs.size());
+    if (e == cudaSuccess) e = cudaMallocHost(&p->h_errs, 4ull * n_internal);
     if (e != cudaSuccess) {
         rc = cuda_fail(e, "plan upload");
         free_plan(p);
@@ -620,6 +840,86 @@ int bs_par_plan_create(const uint8_t *h, uint64_t len, uint64_t n_weights, const
     }
     *out_plan = p;
     return BS_OK;
+}
+
+int check_device(int device) {
+    int ndev = 0;
+    if (cudaGetDeviceCount(&ndev) != cudaSuccess || device < 0 || device >= ndev) {
+        cudaGetLastError();
+        return fail(BS_E_INVALID_ARG, "invalid CUDA device " + std::to_string(device));
+    }
+    return BS_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int bs_par_plan_create(const uint8_t *h, uint64_t len, uint64_t n_weights, const void *d_blob, void *d_out,
+                       int device, bs_plan **out_plan) {
+    if (!out_plan) return fail(BS_E_INVALID_ARG, "out_plan is NULL");
+    *out_plan = nullptr;
+    int rc = check_device(device);
+    if (rc) return rc;
+    DeviceGuard guard(device);
+    SerialLayout L;
+    // bf16_parallel.py:268-269: nothing to decode
+    if (n_weights == 0 || len == 0) return make_serial_plan(L, device, 1, {-1}, 0, out_plan);
+    if (!h) return fail(BS_E_INVALID_ARG, "host blob is NULL");
+    if (!d_blob || !d_out || !on_device(d_blob, device) || !on_device(d_out, device))
+        return fail(BS_E_INVALID_ARG, "d_blob/d_out must be device memory of device " + std::to_string(device));
+    SerialBlob B{h, len, n_weights, reinterpret_cast<uint64_t>(d_blob), reinterpret_cast<uint64_t>(d_out), 0};
+    rc = parse_par1(L, B);
+    if (rc) return rc;
+    return make_serial_plan(L, device, 1, {0}, 1, out_plan);
+}
+
+int bs_se_parse(int codec, const uint8_t *h, uint64_t len, uint64_t n_weights, uint32_t *n_jobs_out) {
+    if (n_jobs_out) *n_jobs_out = 0;
+    if (codec != BS_SE_SINGLE_KERNEL && codec != BS_SE_TANS)
+        return fail(BS_E_INVALID_ARG, "unknown legacy codec " + std::to_string(codec));
+    if (n_weights == 0 || len == 0) return BS_OK;
+    if (!h) return fail(BS_E_INVALID_ARG, "host blob is NULL");
+    SerialLayout L;
+    SerialBlob B{h, len, n_weights, 0, 0, 0};
+    const int rc = parse_serial(codec, L, B);
+    if (rc == BS_OK && n_jobs_out) *n_jobs_out = static_cast<uint32_t>(L.jobs.size());
+    return rc;
+}
+
+int bs_se_plan_create_many(const bs_se_blob *blobs, int n_blobs, int device, bs_plan **out_plan) {
+    if (!out_plan) return fail(BS_E_INVALID_ARG, "out_plan is NULL");
+    *out_plan = nullptr;
+    if (n_blobs < 0 || (n_blobs > 0 && !blobs)) return fail(BS_E_INVALID_ARG, "bad blob array");
+    int rc = check_device(device);
+    if (rc) return rc;
+    DeviceGuard guard(device);
+    SerialLayout L;
+    std::vector<int> u2i(n_blobs, -1);
+    int n_internal = 0;
+    for (int i = 0; i < n_blobs; i++) {
+        const bs_se_blob &b = blobs[i];
+        const std::string who = "blob " + std::to_string(i) + ": ";
+        if (b.codec != BS_SE_SINGLE_KERNEL && b.codec != BS_SE_TANS)
+            return fail(BS_E_INVALID_ARG, who + "unknown legacy codec " + std::to_string(b.codec));
+        // single_kernel.py:603-613 / bf16_tans.py:121-125: nothing to decode
+        if (b.n_weights == 0 || b.blob_bytes == 0) continue;
+        if (!b.h_blob) return fail(BS_E_INVALID_ARG, who + "host blob is NULL");
+        if (!b.d_blob || !b.d_out || !on_device(b.d_blob, device) || !on_device(b.d_out, device))
+            return fail(BS_E_INVALID_ARG, who + "d_blob/d_out must be device memory of device " + std::to_string(device));
+        SerialBlob B{b.h_blob, b.blob_bytes, b.n_weights, reinterpret_cast<uint64_t>(b.d_blob),
+                     reinterpret_cast<uint64_t>(b.d_out), static_cast<uint32_t>(n_internal)};
+        rc = parse_serial(b.codec, L, B);
+        if (rc) return rc;
+        u2i[i] = n_internal++;
+    }
+    return make_serial_plan(L, device, n_blobs, u2i, n_internal, out_plan);
+}
+
+int bs_se_plan_create(int codec, const uint8_t *h, uint64_t len, uint64_t n_weights, const void *d_blob,
+                      void *d_out, int device, bs_plan **out_plan) {
+    const bs_se_blob b{codec, h, len, n_weights, d_blob, d_out};
+    return bs_se_plan_create_many(&b, 1, device, out_plan);
 }
 
 // --------------------------------------------------------------------------

@@ -65,23 +65,43 @@ struct XcItem {
 
 // ---- bf16_parallel_v1 job descriptors --------------------------------------
 // One serial rANS stream (bigsmall/codecs/rans.py:165-207 semantics).
+// One serial rANS stream (L = 2^16, 16-bit little-endian renorm words).  The
+// three reference readers differ only in where the state comes from and in
+// how an odd trailing byte reads; both are folded into (avail, n_words):
+// word k = byte 2k | byte 2k+1 << 8 with bytes at or past `avail` reading 0,
+// and the decoder may read words [first, n_words).
+//   bf16_parallel_v1 (rans.py:165-207): state = words 0,1; an odd last byte is
+//     dropped (avail rounded down to even) but still counts as a zero word.
+//   bf16_se_tans (numba_rans.py:168-217): state = words 0,1; an odd last byte
+//     is the low byte of the last word (avail = the stream length).
+//   bf16_se_single_kernel (single_kernel.py:160-190): state stored separately,
+//     exactly n_words whole words.
 struct ParJob {
-    uint64_t data_off;    // byte offset of the stream in the blob
-    uint32_t data_len;    // stream bytes actually present (python slice clamps)
-    uint32_t n_syms;      // symbols to decode
+    uint64_t data;        // device address of word 0
     uint64_t out_off;     // element offset in the u16 (SE) or u8 (mantissa) scratch
-    uint32_t table;       // 0 = SE table, 1 + e = mantissa table of exponent e
-    uint32_t is_se;
+    uint32_t avail;       // stream bytes present (python slices clamp)
+    uint32_t n_words;     // words the renorm may read, counting the state words
+    uint32_t n_syms;      // symbols to decode
+    uint32_t tab_off;     // first entry of its decode table in the plan's table array
+    uint32_t state0;      // initial state unless kJobStateInStream
+    uint32_t flags;       // kJobSe | kJobStateInStream
+    uint32_t tensor;      // index of the plan tensor (its status word)
+    uint32_t pad_;
 };
+constexpr uint32_t kJobSe = 1u;            // u16 (sign,exp) output, P = 12; else u8 mantissa, P = 10
+constexpr uint32_t kJobStateInStream = 2u; // state = word 0 | word 1 << 16, renorm from word 2
 
-// One PAR1 stream's merge parameters.
+// One stream's merge parameters (a PAR1 stream, or a whole legacy tensor).
 struct ParStream {
     uint64_t se_off;      // offset of its SE symbols in the u16 scratch
     uint64_t mant_off;    // offset of its sorted mantissas in the u8 scratch
+    uint64_t out;         // device address of element 0 of its tensor's output
     uint32_t n_in;        // elements in the stream
-    uint32_t k;           // stream index (element k + i * n_streams)
-    uint32_t bucket_first;// index of its first bucket count in ParPlan::bucket_counts
+    uint32_t k;           // stream index: its i-th value is element k + i * stride
+    uint32_t stride;      // PAR1: the stream count; legacy formats: 1
+    uint32_t bucket_first;// index of its first (exponent, count) record
     uint32_t n_buckets;
+    uint32_t tensor;      // index of the plan tensor (its status word)
 };
 
 }  // namespace bsg
@@ -102,13 +122,11 @@ cudaError_t launch_xc_noalloc(const XcTensorDev *h_tens, const uint32_t *range_c
                               uint32_t *h_status);
 uint64_t xc_noalloc_scratch_bytes();
 
-cudaError_t launch_par_jobs(const uint8_t *d_blob, const ParJob *d_jobs, int n_jobs,
-                            const uint2 *d_se_tab, const uint2 *d_m_tabs, uint16_t *d_se_sym,
-                            uint8_t *d_mant, uint32_t *d_err, cudaStream_t s);
-cudaError_t launch_par_merge(const ParStream *d_streams, int n_streams_total,
-                             const uint32_t *d_bucket_exp_counts, const uint16_t *d_se_sym,
-                             const uint8_t *d_mant, uint16_t *d_out, uint32_t n_streams,
-                             uint32_t *d_err, cudaStream_t s);
+cudaError_t launch_par_jobs(const ParJob *d_jobs, int n_jobs, const uint2 *d_tabs, uint16_t *d_se_sym,
+                            uint8_t *d_mant, uint32_t *d_errs, cudaStream_t s);
+cudaError_t launch_par_merge(const ParStream *d_streams, int n_streams_total, const uint2 *d_buckets,
+                             const uint16_t *d_se_sym, const uint8_t *d_mant, uint32_t *d_errs,
+                             cudaStream_t s);
 
 cudaError_t launch_xc_encode(const uint16_t *d_in, uint64_t n, int coder, int prec,
                              uint32_t chunk_elems, uint8_t *d_out, uint64_t out_cap,

@@ -21,7 +21,7 @@ import numpy as np
 
 from . import codec_registry
 from . import container as _ct
-from .codecs import bf16_parallel, exp_chunked
+from .codecs import bf16_parallel, exp_chunked, se_legacy
 from .loader import ContainerImage, DeviceLoader, _unknown_codec
 
 _DTYPE_TO_NUMPY = {
@@ -47,6 +47,8 @@ def _decode_blob(t: dict, blob: bytes) -> Optional[bytes]:
         return exp_chunked.decode(bytes(blob), extras, n_weights)
     if codec == bf16_parallel.CODEC:
         return bf16_parallel.decode(bytes(blob), extras, n_weights)
+    if codec in se_legacy.CODECS:
+        return se_legacy.decoder_for(codec)(bytes(blob), extras, n_weights)
     pair = codec_registry.get_codec(codec)
     if pair is not None:
         return pair[1](bytes(blob), extras, n_weights)

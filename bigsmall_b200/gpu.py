@@ -187,6 +187,64 @@ class ParPlan(_Plan):
         super().__init__(h, dev, [d_blob, out], 1)
 
 
+SE_CODECS = {"bf16_se_single_kernel": _lib.SE_SINGLE_KERNEL, "bf16_se_tans": _lib.SE_TANS}
+
+
+class SePlan(_Plan):
+    """Decode plan for blobs of the legacy serial formats (bf16_se_single_kernel,
+    bf16_se_tans).
+
+    ``entries``: iterable of ``(codec, host_blob, d_blob, out, n_weights)``;
+    the framing is parsed from ``host_blob`` (bytes identical to ``d_blob``,
+    a 1-D uint8 CUDA tensor).  Every serial stream of every entry runs
+    concurrently on the device, then the exponent un-sort, so the plan takes
+    the time of its longest (sign,exp) stream."""
+
+    def __init__(self, entries: Iterable[tuple], device: Optional[int] = None):
+        entries = list(entries)
+        arr = (_lib.SeBlob * max(1, len(entries)))()
+        keep, dev = [], device
+        for i, (codec, host_blob, d_blob, out, n_weights) in enumerate(entries):
+            if codec not in SE_CODECS:
+                raise ValueError(f"not a legacy serial codec: {codec!r}")
+            _as_cuda(out, "out")
+            if out.element_size() != 2:
+                raise TypeError("out must be a 16-bit tensor (bfloat16)")
+            if out.numel() < n_weights:
+                raise ValueError("out is smaller than n_weights")
+            hb = bytes(host_blob)
+            if n_weights and hb:
+                _as_cuda(d_blob, "d_blob")
+            d = _dev_index(out)
+            if dev is None:
+                dev = d
+            if d != dev or (d_blob is not None and d_blob.numel() and _dev_index(d_blob) != dev):
+                raise ValueError("all tensors of a plan must live on one device")
+            cbuf = ctypes.create_string_buffer(hb, len(hb)) if hb else None
+            arr[i].codec = SE_CODECS[codec]
+            arr[i].h_blob = ctypes.cast(cbuf, ctypes.c_void_p) if cbuf is not None else None
+            arr[i].blob_bytes = len(hb)
+            arr[i].n_weights = int(n_weights)
+            arr[i].d_blob = d_blob.data_ptr() if d_blob is not None and d_blob.numel() else None
+            arr[i].d_out = out.data_ptr() if out.numel() else None
+            keep += [cbuf, d_blob, out]
+        if dev is None:
+            dev = torch.cuda.current_device()
+        h = ctypes.c_void_p()
+        L = _lib.load()
+        _lib.check(L.bs_se_plan_create_many(arr, len(entries), dev, ctypes.byref(h)), "bs_se_plan_create_many")
+        super().__init__(h, dev, [k for k in keep if k is not None and not isinstance(k, ctypes.Array)],
+                         len(entries))
+
+
+def decode_se_into(codec: str, host_blob: bytes, d_blob: torch.Tensor, out: torch.Tensor, n_weights: int,
+                   stream=None) -> torch.Tensor:
+    """Decode one legacy serial blob (device) into ``out`` (device)."""
+    with SePlan([(codec, host_blob, d_blob, out, n_weights)]) as p:
+        p.run(stream)
+    return out
+
+
 def decode_xc_into(blob: torch.Tensor, out: torch.Tensor, chunk_elems: int,
                    stream=None, check: bool = True, coder=None) -> torch.Tensor:
     """Decode one bf16_exp_chunked_v1 blob (device) into ``out`` (device)."""
@@ -299,6 +357,6 @@ def sync(device=None) -> None:
 
 
 __all__: Sequence[str] = [
-    "DEFAULT_CHUNK_ELEMS", "DEFAULT_PREC", "DEFAULT_CODER", "XcPlan", "ParPlan", "XcEncoder", "decode_xc_into",
+    "DEFAULT_CHUNK_ELEMS", "DEFAULT_PREC", "DEFAULT_CODER", "SePlan", "decode_se_into", "SE_CODECS", "XcPlan", "ParPlan", "XcEncoder", "decode_xc_into",
     "decode_par_into", "encode_xc", "encode_bound", "encode_workspace", "xc_extras", "aligned_view",
 ]

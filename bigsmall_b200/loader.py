@@ -10,7 +10,8 @@ on the compute stream as soon as its bytes have landed (:class:`DeviceLoader`),
 so PCIe transfer of group i+1 overlaps the decode of group i.
 
 Codecs handled on the device: ``bf16_exp_chunked_v1`` (batched per group),
-``bf16_parallel_v1``, ``raw`` and ``tied_ref``.  Any other codec raises
+``bf16_parallel_v1``, the legacy serial ``bf16_se_single_kernel`` and
+``bf16_se_tans``, ``raw`` and ``tied_ref``.  Any other codec raises
 ``BigSmallVersionError`` exactly like the reference's dispatcher
 (``bigsmall/decoder.py:89-97``); nothing is decoded on the CPU.
 """
@@ -26,7 +27,8 @@ from . import container as _ct
 from . import gpu
 from .exceptions import BigSmallVersionError
 
-DEVICE_CODECS = ("bf16_exp_chunked_v1", "bf16_parallel_v1", "raw", "tied_ref")
+DEVICE_CODECS = ("bf16_exp_chunked_v1", "bf16_parallel_v1", "bf16_se_single_kernel", "bf16_se_tans", "raw",
+                 "tied_ref")
 
 TORCH_DTYPES = {
     "BF16": torch.bfloat16, "bfloat16": torch.bfloat16, "F16": torch.float16, "float16": torch.float16,
@@ -196,7 +198,7 @@ class DeviceLoader:
         for g in groups:
             g.host_spans = [(layout[p.name][0], layout[p.name][1], layout[p.name][2])
                             for p in g.parts if p.meta["codec"] != "tied_ref"]
-            xc_entries, xc_coders = [], []
+            xc_entries, xc_coders, se_entries = [], [], []
             for p in g.parts:
                 m = p.meta
                 _, d, nb = layout[p.name]
@@ -210,11 +212,17 @@ class DeviceLoader:
                     n = _ct.n_elements(m["shape"])
                     out = self.out[p.name].reshape(-1).view(torch.int16)
                     g.plans.append(gpu.ParPlan(bytes(self.image.blob_host(p.name)), blob, out, n))
+                elif m["codec"] in gpu.SE_CODECS:
+                    n = _ct.n_elements(m["shape"])
+                    out = self.out[p.name].reshape(-1).view(torch.int16)
+                    se_entries.append((m["codec"], bytes(self.image.blob_host(p.name)), blob, out, n))
                 elif m["codec"] == "raw":
                     dst = self.out[p.name].reshape(-1).view(torch.uint8)
                     if dst.numel() != nb:
                         raise ValueError(f"raw tensor {p.name}: {nb} bytes for {dst.numel()}")
                     g.copies.append((dst, blob))
+            if se_entries:   # legacy serial tensors of the group: one plan, streams concurrent
+                g.plans.append(gpu.SePlan(se_entries, device=self.device.index))
             if xc_entries:
                 g.plans.insert(0, gpu.XcPlan(xc_entries, device=self.device.index, coders=xc_coders))
             g.event = torch.cuda.Event()
@@ -378,7 +386,7 @@ class ResidentContainer:
 
     def bundle(self, outputs: dict) -> Bundle:
         """outputs: {name: device tensor of the tensor's shape/dtype}."""
-        xc, coders, plans, copies = [], [], [], []
+        xc, coders, se, plans, copies = [], [], [], [], []
         for name, out in outputs.items():
             real = self.resolve(name)
             m = self.image.tensors[real]
@@ -390,8 +398,13 @@ class ResidentContainer:
             elif m["codec"] == "bf16_parallel_v1":
                 plans.append(gpu.ParPlan(bytes(self.image.blob_host(real)), blob, flat.view(torch.int16),
                                          _ct.n_elements(m["shape"])))
+            elif m["codec"] in gpu.SE_CODECS:
+                se.append((m["codec"], bytes(self.image.blob_host(real)), blob, flat.view(torch.int16),
+                           _ct.n_elements(m["shape"])))
             else:   # raw
                 copies.append((flat.view(torch.uint8), blob))
+        if se:
+            plans.append(gpu.SePlan(se, device=self.device.index))
         if xc:
             plans.insert(0, gpu.XcPlan(xc, device=self.device.index, coders=coders))
         return Bundle(plans, copies)

@@ -133,6 +133,36 @@ int bs_par_plan_create(const uint8_t *h_blob, uint64_t blob_bytes,
                        uint64_t n_weights, const void *d_blob, void *d_out,
                        int device, bs_plan **out_plan);
 
+/* ---- legacy serial formats (bf16_se_single_kernel, bf16_se_tans) --------- */
+/* One serial (sign,exp) rANS stream per tensor plus one rANS stream per
+ * exponent bucket of mantissas, un-sorted by exponent: the device runs every
+ * stream of the tensor concurrently (one CTA each) and then the un-sort, so a
+ * tensor decodes in the time of its (sign,exp) stream.  Same plan object and
+ * calls as bf16_parallel_v1 (bs_plan_decode / bs_plan_check / bs_plan_destroy).
+ * Replaces: bigsmall/codecs/single_kernel.py:432-613 (decode) and
+ *           bigsmall/codecs/bf16_tans.py:121-167 + numba_rans.py:168-217. */
+#define BS_SE_SINGLE_KERNEL 1
+#define BS_SE_TANS          2
+int bs_se_plan_create(int codec, const uint8_t *h_blob, uint64_t blob_bytes,
+                      uint64_t n_weights, const void *d_blob, void *d_out,
+                      int device, bs_plan **out_plan);
+/* Many legacy tensors in one plan: all their serial streams run concurrently,
+ * so a batch decodes in the time of its longest (sign,exp) stream; one status
+ * word per blob.  `h_blob` holds the same bytes as `d_blob`. */
+typedef struct bs_se_blob {
+    int            codec;        /* BS_SE_SINGLE_KERNEL or BS_SE_TANS */
+    const uint8_t *h_blob;
+    uint64_t       blob_bytes;
+    uint64_t       n_weights;
+    const void    *d_blob;
+    void          *d_out;        /* n_weights bf16 values */
+} bs_se_blob;
+int bs_se_plan_create_many(const bs_se_blob *blobs, int n_blobs, int device, bs_plan **out_plan);
+/* Host-only framing check of a legacy blob (no device work): BS_OK and the
+ * number of serial streams, or the status bs_se_plan_create would return. */
+int bs_se_parse(int codec, const uint8_t *h_blob, uint64_t blob_bytes,
+                uint64_t n_weights, uint32_t *n_streams_out);
+
 /* ---- bf16_exp_chunked_v1 encode (KV-cache compression) ------------------ */
 /* Worst-case blob size, and scratch size for one tensor with a given coder. */
 int bs_xc_encode_bound(uint64_t n_elems, uint32_t chunk_elems, uint64_t *bytes);
