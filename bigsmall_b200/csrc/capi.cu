@@ -88,8 +88,14 @@ struct bs_plan {
     int n_streams_total = 0;
     uint2 *d_buckets = nullptr;
     uint2 *d_tabs = nullptr;
+    uint16_t *d_syms = nullptr;
     uint16_t *d_se_sym = nullptr;
     uint8_t *d_mant = nullptr;
+    SegStream *d_ss = nullptr;      // legacy tensors: segmented un-sort
+    int n_ss = 0;
+    uint32_t *d_seg_stream = nullptr;
+    int n_segs = 0;
+    uint32_t *d_hist = nullptr;
 };
 
 namespace {
@@ -271,10 +277,13 @@ int bs_plan_decode(bs_plan *p, void *stream) {
         if (p->n_internal == 0) return BS_OK;
         e = cudaMemsetAsync(p->d_errs, 0, 4ull * p->n_internal, s);
         if (e == cudaSuccess)
-            e = launch_par_jobs(p->d_jobs, p->n_jobs, p->d_tabs, p->d_se_sym, p->d_mant, p->d_errs, s);
+            e = launch_par_jobs(p->d_jobs, p->n_jobs, p->d_tabs, p->d_syms, p->d_se_sym, p->d_mant, p->d_errs, s);
         if (e == cudaSuccess)
             e = launch_par_merge(p->d_streams, p->n_streams_total, p->d_buckets, p->d_se_sym, p->d_mant,
                                  p->d_errs, s);
+        if (e == cudaSuccess)
+            e = launch_seg_merge(p->d_ss, p->n_ss, p->d_seg_stream, p->n_segs, p->d_hist, p->d_buckets,
+                                 p->d_se_sym, p->d_mant, p->d_errs, s);
     } else {
         return fail(BS_E_INVALID_ARG, "unknown plan kind");
     }
@@ -399,9 +408,12 @@ namespace {
 
 struct SerialLayout {
     std::vector<ParJob> jobs;
-    std::vector<ParStream> streams;
+    std::vector<ParStream> streams;      // PAR1 streams (warp-per-stream un-sort)
+    std::vector<SegStream> segs;         // legacy tensors (segmented un-sort)
+    std::vector<uint32_t> seg_stream;    // per segment: index into segs
     std::vector<uint2> buckets;          // (exponent, count) per stream, blob order
-    std::vector<uint2> tabs;             // decode tables: 4096 (SE) or 1024 (mantissa) entries each
+    std::vector<uint2> tabs;             // decode tables {freq, slot - cum}: 4096 (SE) or 1024 entries each
+    std::vector<uint16_t> syms;          // slot -> symbol, same indexing as tabs
     uint64_t n_total = 0;                // values of all tensors (scratch size)
 };
 
@@ -426,12 +438,13 @@ struct Rd {
     }
 };
 
-// Append a decode table: slot -> {sym | freq << 16, slot - cum[sym]}; slots
-// past the frequency sum map to symbol 0 (rans.build_slot_to_symbol /
+// Append a decode table: slot -> {freq[sym], slot - cum[sym]} and slot -> sym;
+// slots past the frequency sum map to symbol 0 (rans.build_slot_to_symbol /
 // numba_rans zero-initialised tables).  Frequencies above M are rejected,
 // which keeps the decoder's 32-bit state exact.  Returns the table's first
-// entry, or -1.
-int64_t add_table(SerialLayout &L, const std::vector<uint32_t> &f, uint32_t M) {
+// entry, or -1; *zero_slot tells whether some slot has frequency 0 (its step
+// can need a second renorm word).
+int64_t add_table(SerialLayout &L, const std::vector<uint32_t> &f, uint32_t M, bool *zero_slot = nullptr) {
     std::vector<uint32_t> cum(f.size());
     uint64_t c = 0;
     for (size_t s = 0; s < f.size(); s++) {
@@ -442,11 +455,32 @@ int64_t add_table(SerialLayout &L, const std::vector<uint32_t> &f, uint32_t M) {
     const size_t base = L.tabs.size();
     if (base + M > 0xFFFFFFFFull) return -1;
     L.tabs.resize(base + M);
-    for (uint32_t slot = 0; slot < M; slot++) L.tabs[base + slot] = make_uint2(f[0] << 16, slot);
+    L.syms.resize(base + M);
+    for (uint32_t slot = 0; slot < M; slot++) {
+        L.tabs[base + slot] = make_uint2(f[0], slot);
+        L.syms[base + slot] = 0;
+    }
     for (size_t s = 0; s < f.size(); s++)
-        for (uint64_t j = 0; j < f[s] && cum[s] + j < M; j++)
-            L.tabs[base + cum[s] + j] = make_uint2(static_cast<uint32_t>(s) | (f[s] << 16), static_cast<uint32_t>(j));
+        for (uint64_t j = 0; j < f[s] && cum[s] + j < M; j++) {
+            L.tabs[base + cum[s] + j] = make_uint2(f[s], static_cast<uint32_t>(j));
+            L.syms[base + cum[s] + j] = static_cast<uint16_t>(s);
+        }
+    if (zero_slot) *zero_slot = c < M && f[0] == 0;
     return static_cast<int64_t>(base);
+}
+
+// state a stream-state job starts from (word 0 | word 1 << 16, bytes past
+// `avail` read as zero)
+uint32_t stream_state(const uint8_t *h, uint64_t avail) {
+    uint32_t v = 0;
+    for (uint64_t i = 0; i < 4; i++) v |= (i < avail ? static_cast<uint32_t>(h[i]) : 0u) << (8 * i);
+    return v;
+}
+
+// mark jobs whose steps can need two renorm words (kJobSlowRenorm)
+void mark_slow(ParJob &j, const uint8_t *h_job, bool zero_slot) {
+    const uint32_t st = (j.flags & kJobStateInStream) ? stream_state(h_job, j.avail) : j.state0;
+    if (zero_slot || st < kRansL) j.flags |= kJobSlowRenorm;
 }
 
 uint64_t freq_sum(const std::vector<uint32_t> &f) {
@@ -567,13 +601,17 @@ int parse_par1(SerialLayout &L, const SerialBlob &B) {
     if (!r.need(4 * n_off)) return fail(BS_E_TRUNCATED, "bf16_parallel: offset table truncated");
     const uint8_t *offt = h + r.pos;
     const uint64_t payload_start = r.pos + 4 * n_off;
-    const int64_t se_tab = add_table(L, se_f, 4096);
+    bool se_zero = false;
+    const int64_t se_tab = add_table(L, se_f, 4096, &se_zero);
     if (se_tab < 0) return fail(BS_E_CORRUPT, "bf16_parallel: SE frequency above M");
     std::vector<uint32_t> m_tab(mfreq.size());
+    std::vector<uint8_t> m_zero(mfreq.size());
     for (size_t t = 0; t < mfreq.size(); t++) {
-        const int64_t o = add_table(L, mfreq[t], 1024);
+        bool z = false;
+        const int64_t o = add_table(L, mfreq[t], 1024, &z);
         if (o < 0) return fail(BS_E_CORRUPT, "bf16_parallel: mantissa frequency above M");
         m_tab[t] = static_cast<uint32_t>(o);
+        m_zero[t] = z;
     }
     uint64_t se_cur = L.n_total;
     for (uint32_t k = 0; k < ns; k++) {
@@ -591,6 +629,7 @@ int parse_par1(SerialLayout &L, const SerialBlob &B) {
         const uint64_t se_at = s.take(se_len, &got);
         L.jobs.push_back(rans_py_job(B.d_blob + se_at, got, nin, static_cast<uint32_t>(se_tab), kJobSe, B.tensor));
         L.jobs.back().out_off = se_cur;
+        mark_slow(L.jobs.back(), h + se_at, se_zero);
         const uint32_t nze = s.u32();
         if (!s.need(2ull * nze)) return fail(BS_E_TRUNCATED, who + "truncated");
         const uint64_t sx = s.pos;
@@ -616,6 +655,7 @@ int parse_par1(SerialLayout &L, const SerialBlob &B) {
             if (seen[ev]) return fail(BS_E_CORRUPT, who + "duplicate bucket exponent");
             seen[ev] = 1;
             bj.push_back({ev, rans_py_job(B.d_blob + at, got, count, m_tab[exp_tab[ev]], 0, B.tensor)});
+            mark_slow(bj.back().second, h + at, m_zero[exp_tab[ev]]);
             L.buckets.push_back(make_uint2(ev, count));
         }
         const int rc = finish_stream(L, S, bj, who);
@@ -626,19 +666,35 @@ int parse_par1(SerialLayout &L, const SerialBlob &B) {
     return BS_OK;
 }
 
-// One legacy tensor = one stream: SE job + bucket jobs, contiguous output.
-ParStream legacy_stream(SerialLayout &L, const SerialBlob &B, uint64_t n, uint32_t n_buckets) {
-    ParStream S{};
+// One legacy tensor: SE job + bucket jobs, contiguous output, segmented
+// un-sort.  Bucket jobs land at their exponent's start in the tensor's sorted
+// mantissa run (ascending exponents, rans bincount/cumsum).
+int finish_legacy(SerialLayout &L, const SerialBlob &B, uint64_t n, uint32_t bucket_first,
+                  std::vector<std::pair<uint32_t, ParJob>> &bj, const std::string &who) {
+    std::vector<uint64_t> cnt(256, 0);
+    uint64_t total = 0;
+    for (auto &x : bj) { cnt[x.first] = x.second.n_syms; total += x.second.n_syms; }
+    if (total != n) return fail(BS_E_CORRUPT, who + "bucket counts do not sum to the value count");
+    std::vector<uint64_t> bstart(257, 0);
+    for (int e = 0; e < 256; e++) bstart[e + 1] = bstart[e] + cnt[e];
+    for (auto &x : bj) {
+        x.second.out_off = L.n_total + bstart[x.first];
+        L.jobs.push_back(x.second);
+    }
+    SegStream S{};
     S.se_off = L.n_total;
     S.mant_off = L.n_total;
     S.out = B.d_out;
-    S.n_in = static_cast<uint32_t>(n);
-    S.k = 0;
-    S.stride = 1;
-    S.bucket_first = static_cast<uint32_t>(L.buckets.size());
-    S.n_buckets = n_buckets;
+    S.n = n;
+    S.seg_first = static_cast<uint32_t>(L.seg_stream.size());
+    S.n_segs = static_cast<uint32_t>((n + kSegElems - 1) / kSegElems);
+    S.bucket_first = bucket_first;
+    S.n_buckets = static_cast<uint32_t>(L.buckets.size()) - bucket_first;
     S.tensor = B.tensor;
-    return S;
+    for (uint32_t j = 0; j < S.n_segs; j++) L.seg_stream.push_back(static_cast<uint32_t>(L.segs.size()));
+    L.segs.push_back(S);
+    L.n_total += n;
+    return BS_OK;
 }
 
 // bigsmall/codecs/single_kernel.py:432-580 _decode_full_kernel framing:
@@ -665,17 +721,19 @@ int parse_sk(SerialLayout &L, const SerialBlob &B) {
     }
     r.pos += 6ull * n_se_nz;
     if (freq_sum(se_f) != 4096) return fail(BS_E_CORRUPT, "bf16_se_single_kernel: SE frequencies do not sum to 4096");
-    const int64_t se_tab = add_table(L, se_f, 4096);
+    bool se_zero = false;
+    const int64_t se_tab = add_table(L, se_f, 4096, &se_zero);
     if (se_tab < 0) return fail(BS_E_CORRUPT, "bf16_se_single_kernel: SE frequency above M");
     const uint32_t st = r.u32(), nc = r.u32();
     if (!r.need(2ull * nc)) return fail(BS_E_TRUNCATED, T);
     ParJob se = word_job(B.d_blob + r.pos, 2ull * nc, nc, n, static_cast<uint32_t>(se_tab), kJobSe, B.tensor, st);
     se.out_off = L.n_total;
+    mark_slow(se, h + r.pos, se_zero);
     L.jobs.push_back(se);
     r.pos += 2ull * nc;
     const uint32_t nb = r.u32();
     if (r.bad) return fail(BS_E_TRUNCATED, T);
-    ParStream S = legacy_stream(L, B, n, nb);
+    const uint32_t bucket_first = static_cast<uint32_t>(L.buckets.size());
     std::vector<uint8_t> seen(256, 0);
     std::vector<std::pair<uint32_t, ParJob>> bj;
     for (uint32_t q = 0; q < nb; q++) {
@@ -694,15 +752,15 @@ int parse_sk(SerialLayout &L, const SerialBlob &B) {
         if (!r.need(2ull * mnc)) return fail(BS_E_TRUNCATED, T);
         if (seen[e]) return fail(BS_E_CORRUPT, "bf16_se_single_kernel: duplicate bucket exponent");
         seen[e] = 1;
-        const int64_t t = add_table(L, mf, 1024);
+        bool z = false;
+        const int64_t t = add_table(L, mf, 1024, &z);
         if (t < 0) return fail(BS_E_CORRUPT, "bf16_se_single_kernel: mantissa frequency above M");
         bj.push_back({e, word_job(B.d_blob + r.pos, 2ull * mnc, mnc, bsize, static_cast<uint32_t>(t), 0, B.tensor, mst)});
+        mark_slow(bj.back().second, h + r.pos, z);
         L.buckets.push_back(make_uint2(e, bsize));
         r.pos += 2ull * mnc;
     }
-    const int rc = finish_stream(L, S, bj, "bf16_se_single_kernel: ");
-    if (rc == BS_OK) L.n_total += n;
-    return rc;
+    return finish_legacy(L, B, n, bucket_first, bj, "bf16_se_single_kernel: ");
 }
 
 // bigsmall/codecs/bf16_tans.py:121-167 framing (streams are numba_rans.py
@@ -733,10 +791,12 @@ int parse_setans(SerialLayout &L, const SerialBlob &B) {
     uint64_t got;
     const uint64_t cw = r.take(cwl, &got);
     if (got < 4) return fail(BS_E_TRUNCATED, "bf16_se_tans: SE stream shorter than its state");
-    const int64_t se_tab = add_table(L, se_f, 4096);
+    bool se_zero = false;
+    const int64_t se_tab = add_table(L, se_f, 4096, &se_zero);
     if (se_tab < 0) return fail(BS_E_CORRUPT, "bf16_se_tans: SE frequency above M");
     ParJob se = numba_job(B.d_blob + cw, got, n, static_cast<uint32_t>(se_tab), kJobSe, B.tensor);
     se.out_off = L.n_total;
+    mark_slow(se, h + cw, se_zero);
     L.jobs.push_back(se);
     const uint32_t mbl = r.u32();
     if (r.bad) return fail(BS_E_TRUNCATED, T);
@@ -746,7 +806,7 @@ int parse_setans(SerialLayout &L, const SerialBlob &B) {
     if (!m.need(2ull * ne)) return fail(BS_E_TRUNCATED, T);
     const uint64_t ex = m.pos;
     m.pos += 2ull * ne;
-    ParStream S = legacy_stream(L, B, n, ne);
+    const uint32_t bucket_first = static_cast<uint32_t>(L.buckets.size());
     std::vector<uint8_t> seen(256, 0);
     std::vector<std::pair<uint32_t, ParJob>> bj;
     for (uint32_t q = 0; q < ne; q++) {
@@ -769,14 +829,14 @@ int parse_setans(SerialLayout &L, const SerialBlob &B) {
         if (seen[ev]) return fail(BS_E_CORRUPT, "bf16_se_tans: duplicate bucket exponent");
         seen[ev] = 1;
         if (nb > 0 && cgot < 4) return fail(BS_E_TRUNCATED, "bf16_se_tans: bucket stream shorter than its state");
-        const int64_t t = add_table(L, mf, 1024);
+        bool z = false;
+        const int64_t t = add_table(L, mf, 1024, &z);
         if (t < 0) return fail(BS_E_CORRUPT, "bf16_se_tans: mantissa frequency above M");
         bj.push_back({ev, numba_job(B.d_blob + c2, cgot, nb, static_cast<uint32_t>(t), 0, B.tensor)});
+        mark_slow(bj.back().second, h + c2, z);
         L.buckets.push_back(make_uint2(ev, nb));
     }
-    const int rc = finish_stream(L, S, bj, "bf16_se_tans: ");
-    if (rc == BS_OK) L.n_total += n;
-    return rc;
+    return finish_legacy(L, B, n, bucket_first, bj, "bf16_se_tans: ");
 }
 
 int parse_serial(int codec, SerialLayout &L, const SerialBlob &B) {
@@ -792,7 +852,7 @@ int parse_serial(int codec, SerialLayout &L, const SerialBlob &B) {
 int make_serial_plan(SerialLayout &L, int device, int n_tensors, std::vector<int> u2i, int n_internal,
                      bs_plan **out_plan) {
     std::stable_sort(L.jobs.begin(), L.jobs.end(), [](const ParJob &x, const ParJob &y) { return x.n_syms > y.n_syms; });
-    if (L.jobs.size() > 0x7FFFFFFFull || L.streams.size() > 0x7FFFFFFFull)
+    if (L.jobs.size() > 0x7FFFFFFFull || L.streams.size() > 0x7FFFFFFFull || L.seg_stream.size() > 0x7FFFFFFFull)
         return fail(BS_E_INVALID_ARG, "too many streams");
     auto *p = new bs_plan();
     p->kind = kPlanPar;
@@ -809,6 +869,10 @@ int make_serial_plan(SerialLayout &L, int device, int n_tensors, std::vector<int
     const uint64_t o_s = cv.take(sizeof(ParStream) * L.streams.size());
     const uint64_t o_b = cv.take(sizeof(uint2) * std::max<size_t>(1, L.buckets.size()));
     const uint64_t o_t = cv.take(sizeof(uint2) * std::max<size_t>(1, L.tabs.size()));
+    const uint64_t o_sy = cv.take(sizeof(uint16_t) * std::max<size_t>(1, L.syms.size()));
+    const uint64_t o_sg = cv.take(sizeof(SegStream) * L.segs.size());
+    const uint64_t o_sgs = cv.take(sizeof(uint32_t) * L.seg_stream.size());
+    const uint64_t o_h = cv.take(256ull * sizeof(uint32_t) * L.seg_stream.size());
     const uint64_t o_ss = cv.take(2 * L.n_total);
     const uint64_t o_m = cv.take(L.n_total);
     const uint64_t o_e = cv.take(4ull * n_internal);
@@ -821,6 +885,12 @@ int make_serial_plan(SerialLayout &L, int device, int n_tensors, std::vector<int
     p->n_streams_total = static_cast<int>(L.streams.size());
     p->d_buckets = reinterpret_cast<uint2 *>(base + o_b);
     p->d_tabs = reinterpret_cast<uint2 *>(base + o_t);
+    p->d_syms = reinterpret_cast<uint16_t *>(base + o_sy);
+    p->d_ss = reinterpret_cast<SegStream *>(base + o_sg);
+    p->n_ss = static_cast<int>(L.segs.size());
+    p->d_seg_stream = reinterpret_cast<uint32_t *>(base + o_sgs);
+    p->n_segs = static_cast<int>(L.seg_stream.size());
+    p->d_hist = reinterpret_cast<uint32_t *>(base + o_h);
     p->d_se_sym = reinterpret_cast<uint16_t *>(base + o_ss);
     p->d_mant = base + o_m;
     p->d_errs = reinterpret_cast<uint32_t *>(base + o_e);
@@ -832,6 +902,9 @@ int make_serial_plan(SerialLayout &L, int device, int n_tensors, std::vector<int
     up(p->d_streams, L.streams.data(), sizeof(ParStream) * L.streams.size());
     up(p->d_buckets, L.buckets.data(), sizeof(uint2) * L.buckets.size());
     up(p->d_tabs, L.tabs.data(), sizeof(uint2) * L.tabs.size());
+    up(p->d_syms, L.syms.data(), sizeof(uint16_t) * L.syms.size());
+    up(p->d_ss, L.segs.data(), sizeof(SegStream) * L.segs.size());
+    up(p->d_seg_stream, L.seg_stream.data(), sizeof(uint32_t) * L.seg_stream.size());
     if (e == cudaSuccess) e = cudaMallocHost(&p->h_errs, 4ull * n_internal);
     if (e != cudaSuccess) {
         rc = cuda_fail(e, "plan upload");

@@ -90,6 +90,26 @@ struct ParJob {
 };
 constexpr uint32_t kJobSe = 1u;            // u16 (sign,exp) output, P = 12; else u8 mantissa, P = 10
 constexpr uint32_t kJobStateInStream = 2u; // state = word 0 | word 1 << 16, renorm from word 2
+constexpr uint32_t kJobSlowRenorm = 4u;    // a step may need two renorm words (initial state below
+                                           // L, or a table slot with frequency 0)
+
+// Un-sort of one legacy tensor (a single stride-1 stream), split into
+// segments of kSegElems values so that every segment's exponent ranks are
+// computed by its own warp (histogram, per-exponent scan across segments,
+// ranked gather).
+constexpr uint32_t kSegElems = 16384;
+struct SegStream {
+    uint64_t se_off;      // its SE symbols in the u16 scratch
+    uint64_t mant_off;    // its sorted mantissas in the u8 scratch
+    uint64_t out;         // device address of element 0
+    uint64_t n;           // values
+    uint32_t seg_first;   // its first segment in the plan's segment list
+    uint32_t n_segs;
+    uint32_t bucket_first;
+    uint32_t n_buckets;
+    uint32_t tensor;
+    uint32_t pad_;
+};
 
 // One stream's merge parameters (a PAR1 stream, or a whole legacy tensor).
 struct ParStream {
@@ -122,8 +142,11 @@ cudaError_t launch_xc_noalloc(const XcTensorDev *h_tens, const uint32_t *range_c
                               uint32_t *h_status);
 uint64_t xc_noalloc_scratch_bytes();
 
-cudaError_t launch_par_jobs(const ParJob *d_jobs, int n_jobs, const uint2 *d_tabs, uint16_t *d_se_sym,
-                            uint8_t *d_mant, uint32_t *d_errs, cudaStream_t s);
+cudaError_t launch_par_jobs(const ParJob *d_jobs, int n_jobs, const uint2 *d_tabs, const uint16_t *d_syms,
+                            uint16_t *d_se_sym, uint8_t *d_mant, uint32_t *d_errs, cudaStream_t s);
+cudaError_t launch_seg_merge(const SegStream *d_ss, int n_ss, const uint32_t *d_seg_stream, int n_segs,
+                             uint32_t *d_hist, const uint2 *d_buckets, const uint16_t *d_se_sym,
+                             const uint8_t *d_mant, uint32_t *d_errs, cudaStream_t s);
 cudaError_t launch_par_merge(const ParStream *d_streams, int n_streams_total, const uint2 *d_buckets,
                              const uint16_t *d_se_sym, const uint8_t *d_mant, uint32_t *d_errs,
                              cudaStream_t s);

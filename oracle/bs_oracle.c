@@ -1408,6 +1408,11 @@ int bso_sk_decode_many(const uint8_t *const *blobs, const int64_t *lens, const i
     return run_pool(bso_sk_decode, blobs, lens, n_weights, outs, count, threads);
 }
 
+int bso_tans_decode_many(const uint8_t *const *blobs, const int64_t *lens, const int64_t *n_weights,
+                         uint16_t *const *outs, int count, int threads) {
+    return run_pool(bso_tans_decode, blobs, lens, n_weights, outs, count, threads);
+}
+
 int bso_xc_decode_many(const uint8_t *const *blobs, const int64_t *lens, const int64_t *n_weights,
                        uint16_t *const *outs, int count, int threads) {
     return run_pool(bso_xc_decode, blobs, lens, n_weights, outs, count, threads);

@@ -81,6 +81,8 @@ int bso_xc_decode(const uint8_t *blob, int64_t len, int64_t n_weights,
                   uint16_t *out);
 /* Quantised exponent frequencies the format uses (for tests). */
 int bso_xc_quantise(const int64_t *counts, int prec, uint16_t *freqs);
+int bso_tans_decode_many(const uint8_t *const *blobs, const int64_t *lens,
+                         const int64_t *n_weights, uint16_t *const *outs, int count, int threads);
 int bso_xc_decode_many(const uint8_t *const *blobs, const int64_t *lens,
                        const int64_t *n_weights, uint16_t *const *outs,
                        int count, int threads);

@@ -64,6 +64,7 @@ def lib():
         "bso_tans_bound": (I64, [I64]),
         "bso_tans_encode": (I64, [P, I64, P, I64]),
         "bso_tans_decode": (I32, [P, I64, I64, P]),
+        "bso_tans_decode_many": (I32, [P, P, P, P, I32, I32]),
         "bso_xc_bound": (I64, [I64, U32]),
         "bso_xc_encode": (I64, [P, I64, I32, I32, U32, P, I64]),
         "bso_xc_decode": (I32, [P, I64, I64, P]),
@@ -188,7 +189,7 @@ def xc_quantise(counts, prec: int = 12) -> np.ndarray:
 
 
 def decode_many(kind: str, blobs, n_weights, threads: int) -> list[np.ndarray]:
-    """Decode many blobs on `threads` host threads (kind 'sk' or 'xc')."""
+    """Decode many blobs on `threads` host threads (kind 'sk', 'tans' or 'xc')."""
     arrs = [_blob(b) for b in blobs]
     outs = [np.empty(max(int(n), 1), dtype=np.uint16) for n in n_weights]
     cnt = len(arrs)
