@@ -55,6 +55,33 @@ struct XcTensorDev {
     uint32_t pad_;
 };
 
+// Exact unsigned division by an invariant divisor (Granlund & Montgomery,
+// "Division by Invariant Integers using Multiplication", PLDI 1994, Fig. 4.1,
+// N = 32): with l = ceil(log2 d) and m' = floor(2^32 (2^l - d) / d) + 1,
+// q = (t + ((n - t) >> min(l, 1))) >> max(l - 1, 0), t = mulhi(m', n), equals
+// floor(n / d) for every 32-bit n and 1 <= d < 2^32.  The rANS encoders divide
+// the state by a symbol frequency once per value; this replaces that divide.
+struct RcpDiv {
+    uint32_t m;
+    uint32_t sh1, sh2;
+};
+
+__host__ __device__ inline RcpDiv rcp_div_make(uint32_t d) {
+    uint32_t l = 0;
+    while ((1ull << l) < d) l++;
+    const uint64_t m = ((1ull << 32) * ((1ull << l) - d)) / d + 1;
+    return RcpDiv{static_cast<uint32_t>(m), l ? 1u : 0u, l ? l - 1 : 0u};
+}
+
+__host__ __device__ inline uint32_t rcp_div(uint32_t n, uint32_t m, uint32_t sh1, uint32_t sh2) {
+#ifdef __CUDA_ARCH__
+    const uint32_t t = __umulhi(m, n);
+#else
+    const uint32_t t = static_cast<uint32_t>((static_cast<uint64_t>(m) * n) >> 32);
+#endif
+    return (t + ((n - t) >> sh1)) >> sh2;
+}
+
 // A work item: up to kXcWarps consecutive chunks of one tensor, one CTA.
 struct XcItem {
     uint32_t tensor;

@@ -27,13 +27,14 @@
 namespace bsg {
 
 namespace {
-constexpr int kEncWarps = 8;
+constexpr int kEncWarps = 4;            // chunks (warps) per CTA: small tensors still spread over SMs
 constexpr uint64_t kWsCounts = 0;       // u64[256] exponent histogram
 constexpr uint64_t kWsTab = 2048;       // u32[256]: freq | cum << 16
 constexpr uint64_t kWsFlags = 3072;     // u32 flags
 constexpr uint64_t kWsAux = 3076;       // u32 pair coder: window base e_lo
 constexpr uint64_t kWsPairCounts = 4096;   // u64[256] pair-symbol histogram
-constexpr uint64_t kWsRec = 6144;       // u32[n_chunks] words per record, then u32[n_chunks] escapes
+constexpr uint64_t kWsRcp = 6144;       // uint4[256]: {m', sh1 | sh2 << 8, freq | cum << 16, M - freq}
+constexpr uint64_t kWsRec = 10240;      // u32[n_chunks] words per record, then u32[n_chunks] escapes
 
 inline uint64_t rup(uint64_t x, uint64_t a) { return (x + a - 1) / a * a; }
 inline uint64_t slot_bytes(uint32_t ce) { return rup(kXcPairRecHdr + 2ull * ce, 16); }
@@ -176,6 +177,13 @@ __global__ void __launch_bounds__(256) xc_enc_setup_kernel(const unsigned long l
     if (tab_end + tid < plane_off) out[tab_end + tid] = 0;
     if (plane_off + n + tid < chunks_off) out[plane_off + n + tid] = 0;
     enc_tab[tid] = static_cast<uint32_t>(f[tid]) | (s_cum[tid] << 16);
+    {
+        // per-symbol divide-by-frequency constants for the rANS encoders
+        const uint32_t fs = static_cast<uint32_t>(f[tid]);
+        const RcpDiv r = rcp_div_make(fs ? fs : 1u);
+        reinterpret_cast<uint4 *>(enc_tab + (kWsRcp - kWsTab) / 4)[tid] =
+            make_uint4(r.m, r.sh1 | (r.sh2 << 8), fs | (s_cum[tid] << 16), static_cast<uint32_t>(M) - fs);
+    }
     if (coder != BS_CODER_TANS) return;
     // tANS: spread the symbols over the 2^P states with Collet's step (the k-th
     // placement in symbol order lands on (k * step) mod M), then list each
@@ -260,10 +268,10 @@ __global__ void __launch_bounds__(256) xc_enc_pair_hist_kernel(const uint16_t *_
 // 3c. per-chunk reverse rANS over exponent pairs, then the escape list ------
 __global__ void __launch_bounds__(kEncWarps * 32) xc_enc_chunks_pair_kernel(
     const uint16_t *__restrict__ in, uint64_t n, uint32_t ce, uint32_t nc, int prec,
-    const uint32_t *__restrict__ enc_tab, const uint32_t *aux, uint8_t *__restrict__ slots, uint64_t slot_b,
+    const uint4 *__restrict__ rcp_tab, const uint32_t *aux, uint8_t *__restrict__ slots, uint64_t slot_b,
     uint32_t *__restrict__ rec_words, uint32_t *__restrict__ rec_esc) {
-    __shared__ uint32_t s_tab[256];
-    s_tab[threadIdx.x] = enc_tab[threadIdx.x];
+    __shared__ uint4 s_tab[256];
+    for (uint32_t i = threadIdx.x; i < 256; i += blockDim.x) s_tab[i] = rcp_tab[i];
     __syncthreads();
     const uint32_t e_lo = *aux;
     const uint32_t lane = threadIdx.x & 31;
@@ -281,9 +289,10 @@ __global__ void __launch_bounds__(kEncWarps * 32) xc_enc_chunks_pair_kernel(
     uint32_t x = kRansL, cur = 0;
     const uint32_t G = cn >> 8, rem = cn & 255;
 
+    // x <- (x / f) << P | (x mod f) + cum  ==  x + cum + (x / f) (M - f)
     auto enc = [&](uint32_t sym, bool active) {
-        const uint32_t t = s_tab[sym];
-        const uint32_t f = t & 0xFFFF, cf = t >> 16;
+        const uint4 t = s_tab[sym];
+        const uint32_t f = t.z & 0xFFFF, cf = t.z >> 16;
         const bool emit = active && (static_cast<uint64_t>(x) >= (static_cast<uint64_t>(f) << (32 - P)));
         const uint32_t m = __ballot_sync(kFull, emit);
         if (emit) {
@@ -292,8 +301,8 @@ __global__ void __launch_bounds__(kEncWarps * 32) xc_enc_chunks_pair_kernel(
         }
         cur += __popc(m);
         if (active) {
-            const uint32_t q = x / f;
-            x = (q << P) + (x - q * f) + cf;
+            const uint32_t q = rcp_div(x, t.x, t.y & 0xFF, t.y >> 8);
+            x = x + cf + q * t.w;
         }
     };
     if (rem) {
@@ -306,8 +315,15 @@ __global__ void __launch_bounds__(kEncWarps * 32) xc_enc_chunks_pair_kernel(
             enc(a * 16 + b, act);
         }
     }
+    // groups run backwards; the next two groups' values are in flight
+    auto grp = [&](int g) { return reinterpret_cast<const uint4 *>(src + g * 256 + lane * 8)[0]; };
+    uint4 n1 = make_uint4(0, 0, 0, 0), n2 = n1;
+    if (G > 0) n1 = grp(static_cast<int>(G) - 1);
+    if (G > 1) n2 = grp(static_cast<int>(G) - 2);
     for (int g = static_cast<int>(G) - 1; g >= 0; g--) {
-        const uint4 v = reinterpret_cast<const uint4 *>(src + g * 256 + lane * 8)[0];
+        const uint4 v = n1;
+        n1 = n2;
+        if (g >= 2) n2 = grp(g - 2);
         enc(pair_a(v.w & 0xFFFF, e_lo) * 16 + pair_a(v.w >> 16, e_lo), true);
         enc(pair_a(v.z & 0xFFFF, e_lo) * 16 + pair_a(v.z >> 16, e_lo), true);
         enc(pair_a(v.y & 0xFFFF, e_lo) * 16 + pair_a(v.y >> 16, e_lo), true);
@@ -329,8 +345,12 @@ __global__ void __launch_bounds__(kEncWarps * 32) xc_enc_chunks_pair_kernel(
             epos += __popc(ba) + __popc(bb);
         }
     };
+    n1 = G > 0 ? grp(0) : make_uint4(0, 0, 0, 0);
+    n2 = G > 1 ? grp(1) : make_uint4(0, 0, 0, 0);
     for (uint32_t g = 0; g < G; g++) {
-        const uint4 v = reinterpret_cast<const uint4 *>(src + g * 256 + lane * 8)[0];
+        const uint4 v = n1;
+        n1 = n2;
+        if (g + 2 < G) n2 = grp(static_cast<int>(g) + 2);
         esc_step(v.x, true, true);
         esc_step(v.y, true, true);
         esc_step(v.z, true, true);
@@ -355,10 +375,10 @@ __global__ void __launch_bounds__(kEncWarps * 32) xc_enc_chunks_pair_kernel(
 // 3. per-chunk reverse rANS ---------------------------------------------------
 __global__ void __launch_bounds__(kEncWarps * 32) xc_enc_chunks_kernel(
     const uint16_t *__restrict__ in, uint64_t n, uint32_t ce, uint32_t nc, int prec,
-    const uint32_t *__restrict__ enc_tab, uint8_t *__restrict__ slots, uint64_t slot_b,
+    const uint4 *__restrict__ rcp_tab, uint8_t *__restrict__ slots, uint64_t slot_b,
     uint32_t *__restrict__ rec_words) {
-    __shared__ uint32_t s_tab[256];
-    s_tab[threadIdx.x] = enc_tab[threadIdx.x];
+    __shared__ uint4 s_tab[256];
+    for (uint32_t i = threadIdx.x; i < 256; i += blockDim.x) s_tab[i] = rcp_tab[i];
     __syncthreads();
     const uint32_t lane = threadIdx.x & 31;
     const uint32_t c = blockIdx.x * kEncWarps + (threadIdx.x >> 5);
@@ -374,10 +394,11 @@ __global__ void __launch_bounds__(kEncWarps * 32) xc_enc_chunks_kernel(
     uint32_t cur = 0;
     const uint32_t G = cn >> 8, rem = cn & 255;
 
+    // x <- (x / f) << P | (x mod f) + cum  ==  x + cum + (x / f) (M - f)
     auto enc = [&](uint32_t v, bool active) {
         const uint32_t sym = (v >> 7) & 0xFF;
-        const uint32_t t = s_tab[sym];
-        const uint32_t f = t & 0xFFFF, cf = t >> 16;
+        const uint4 t = s_tab[sym];
+        const uint32_t f = t.z & 0xFFFF, cf = t.z >> 16;
         const bool emit = active && (static_cast<uint64_t>(x) >= (static_cast<uint64_t>(f) << (32 - P)));
         const uint32_t m = __ballot_sync(kFull, emit);
         if (emit) {
@@ -386,8 +407,8 @@ __global__ void __launch_bounds__(kEncWarps * 32) xc_enc_chunks_kernel(
         }
         cur += __popc(m);
         if (active) {
-            const uint32_t q = x / f;
-            x = (q << P) + (x - q * f) + cf;
+            const uint32_t q = rcp_div(x, t.x, t.y & 0xFF, t.y >> 8);
+            x = x + cf + q * t.w;
         }
     };
 
@@ -399,11 +420,15 @@ __global__ void __launch_bounds__(kEncWarps * 32) xc_enc_chunks_kernel(
 #pragma unroll
         for (int j = 7; j >= 0; j--) enc(v[j], lane * 8 + j < rem);
     }
-    uint4 nxt = make_uint4(0, 0, 0, 0);
-    if (G > 0) nxt = reinterpret_cast<const uint4 *>(src + (G - 1) * 256 + lane * 8)[0];
+    // groups run backwards; the next two groups' values are in flight
+    auto grp = [&](int g) { return reinterpret_cast<const uint4 *>(src + g * 256 + lane * 8)[0]; };
+    uint4 n1 = make_uint4(0, 0, 0, 0), n2 = n1;
+    if (G > 0) n1 = grp(static_cast<int>(G) - 1);
+    if (G > 1) n2 = grp(static_cast<int>(G) - 2);
     for (int g = static_cast<int>(G) - 1; g >= 0; g--) {
-        const uint4 v = nxt;
-        if (g > 0) nxt = reinterpret_cast<const uint4 *>(src + (g - 1) * 256 + lane * 8)[0];
+        const uint4 v = n1;
+        n1 = n2;
+        if (g >= 2) n2 = grp(g - 2);
         enc(v.w >> 16, true);
         enc(v.w & 0xFFFF, true);
         enc(v.z >> 16, true);
@@ -429,7 +454,7 @@ __global__ void __launch_bounds__(kEncWarps * 32) xc_enc_chunks_tans_kernel(
     __shared__ uint32_t s_tab[256];
     __shared__ uint16_t s_sl[kXcMaxTable];
     const uint32_t M = 1u << prec;
-    s_tab[threadIdx.x] = enc_tab[threadIdx.x];
+    for (uint32_t i = threadIdx.x; i < 256; i += blockDim.x) s_tab[i] = enc_tab[i];
     for (uint32_t i = threadIdx.x; i < M; i += blockDim.x) s_sl[i] = slot_list[i];
     __syncthreads();
     const uint32_t lane = threadIdx.x & 31;
@@ -600,6 +625,7 @@ cudaError_t launch_xc_encode(const uint16_t *d_in, uint64_t n, int coder, int pr
     const uint64_t nc = (n + ce - 1) / ce;
     auto *counts = reinterpret_cast<unsigned long long *>(d_ws + kWsCounts);
     auto *tab = reinterpret_cast<uint32_t *>(d_ws + kWsTab);
+    auto *rcp = reinterpret_cast<const uint4 *>(d_ws + kWsRcp);
     auto *flags = reinterpret_cast<uint32_t *>(d_ws + kWsFlags);
     auto *aux = reinterpret_cast<uint32_t *>(d_ws + kWsAux);
     auto *pcounts = reinterpret_cast<unsigned long long *>(d_ws + kWsPairCounts);
@@ -631,14 +657,14 @@ cudaError_t launch_xc_encode(const uint16_t *d_in, uint64_t n, int coder, int pr
     const unsigned enc_blocks = static_cast<unsigned>((nc + kEncWarps - 1) / kEncWarps);
     if (coder == BS_CODER_RANS_PAIR) {
         xc_enc_chunks_pair_kernel<<<enc_blocks, kEncWarps * 32, 0, s>>>(d_in, n, ce, static_cast<uint32_t>(nc), prec,
-                                                                       tab, aux, slots, sb, recw, rece);
+                                                                       rcp, aux, slots, sb, recw, rece);
     } else if (coder == BS_CODER_TANS) {
         auto *scr = reinterpret_cast<uint32_t *>(d_ws + tans_scratch_off(nc, ce));
         xc_enc_chunks_tans_kernel<<<enc_blocks, kEncWarps * 32, 0, s>>>(d_in, n, ce, static_cast<uint32_t>(nc), prec,
                                                                        tab, slot_list, slots, sb, scr, recw);
     } else {
         xc_enc_chunks_kernel<<<enc_blocks, kEncWarps * 32, 0, s>>>(d_in, n, ce, static_cast<uint32_t>(nc), prec,
-                                                                  tab, slots, sb, recw);
+                                                                  rcp, slots, sb, recw);
     }
     xc_enc_scan_kernel<<<1, 1024, 0, s>>>(recw, rece, coder, static_cast<uint32_t>(nc), d_out, chunks_off, out_cap,
                                           reinterpret_cast<unsigned long long *>(d_out_len), flags);
