@@ -114,9 +114,13 @@ __global__ void __launch_bounds__(256) xc_enc_setup_kernel(const unsigned long l
     __shared__ uint32_t s_cum[256];
     __shared__ uint8_t s_spread[kXcMaxTable];
     __shared__ uint32_t s_occ[256];
+    __shared__ unsigned long long s_counts[256];
     const int tid = threadIdx.x;
     const int64_t M = 1ll << prec;
+    s_counts[tid] = counts[tid];   // one global load per thread instead of serial loads in thread 0
+    __syncthreads();
     if (tid == 0) {
+        const unsigned long long *counts = s_counts;
         int nnz = 0, first = -1;
         unsigned long long total = 0;
         for (int s = 0; s < 256; s++)
@@ -220,18 +224,36 @@ __device__ __forceinline__ uint32_t pair_a(uint32_t v, uint32_t e_lo) {
     return d <= 14 ? d : 15u;
 }
 
-// the 15-wide exponent window holding the most values (lowest base on ties)
-__global__ void xc_enc_window_kernel(const unsigned long long *counts, uint32_t *aux) {
-    if (threadIdx.x != 0) return;
-    unsigned long long best = 0, m = 0;
-    uint32_t bw = 0;
-    for (int k = 0; k < 15; k++) m += counts[k];
-    best = m;
-    for (uint32_t w = 1; w + 14 < 256; w++) {
-        m += counts[w + 14] - counts[w - 1];
-        if (m > best) { best = m; bw = w; }
+// the 15-wide exponent window holding the most values (lowest base on ties):
+// thread w sums window w, then a max reduction keeps the lowest w among equals
+__global__ void __launch_bounds__(256) xc_enc_window_kernel(const unsigned long long *counts, uint32_t *aux) {
+    __shared__ unsigned long long c[256];
+    __shared__ unsigned long long s_m[8];
+    __shared__ uint32_t s_w[8];
+    const uint32_t t = threadIdx.x, lane = t & 31;
+    c[t] = counts[t];
+    __syncthreads();
+    unsigned long long m = 0;
+    uint32_t w = 0xFFFFu;                         // not a window: loses every comparison
+    if (t + 14 < 256) {
+        for (int k = 0; k < 15; k++) m += c[t + k];
+        w = t;
     }
-    *aux = bw;
+    auto better = [](unsigned long long m1, uint32_t w1, unsigned long long m0, uint32_t w0) {
+        return m1 > m0 || (m1 == m0 && w1 < w0);
+    };
+    for (int off = 16; off; off >>= 1) {
+        const unsigned long long om = __shfl_down_sync(kFull, m, off);
+        const uint32_t ow = __shfl_down_sync(kFull, w, off);
+        if (better(om, ow, m, w)) { m = om; w = ow; }
+    }
+    if (lane == 0) { s_m[t >> 5] = m; s_w[t >> 5] = w; }
+    __syncthreads();
+    if (t == 0) {
+        for (int k = 1; k < 8; k++)
+            if (better(s_m[k], s_w[k], m, w)) { m = s_m[k]; w = s_w[k]; }
+        *aux = w;
+    }
 }
 
 // pairs (2k, 2k+1) of the tensor; an odd tail value pairs with b = 0
@@ -648,7 +670,7 @@ cudaError_t launch_xc_encode(const uint16_t *d_in, uint64_t n, int coder, int pr
     if (coder == BS_CODER_RANS_PAIR) {
         e = cudaMemsetAsync(pcounts, 0, 2048, s);
         if (e != cudaSuccess) return e;
-        xc_enc_window_kernel<<<1, 32, 0, s>>>(counts, aux);
+        xc_enc_window_kernel<<<1, 256, 0, s>>>(counts, aux);
         xc_enc_pair_hist_kernel<<<grid, 256, 0, s>>>(d_in, n, aux, pcounts);
         qcounts = pcounts;
     }
