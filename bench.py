@@ -225,6 +225,12 @@ def main():
     ap.add_argument("--chunk-elems", type=int, default=None)
     ap.add_argument("--coder", default="pair", choices=["rans", "tans", "pair"])
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-replicate", action="store_true",
+                    help="N>1: skip the separately reported NCCL materialisation of the full model on every GPU")
+    ap.add_argument("--stream-ctas", default="3",
+                    help="config 4: comma list of side-stream decode CTAs per SM to run (0 = uncapped)")
+    ap.add_argument("--stream-priority", default="1",
+                    help="config 4: comma list of 0/1: run the model on a high-priority stream (1) or not")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=8.0)
     ap.add_argument("--config", default="c2", choices=["c2", "small", "kv", "sweep", "stream", "mix", "legacy"],
@@ -332,7 +338,32 @@ def main():
     comp_bytes = sum(int(b.numel()) for b in blobs.values())
     del blobs
     torch.cuda.synchronize()
-    loader = DeviceLoader(image, device=local, owned=owned)
+    # N>1: outputs live in one flat buffer holding the whole model in name order,
+    # so the owners' spans can be broadcast into every rank's copy afterwards
+    replicate = world > 1 and not a.no_replicate
+    out_views, spans, flat = None, None, None
+    if replicate:
+        goff, pos = {}, 0
+        for name, shape, _ in tensors:
+            goff[name] = pos
+            pos += math.prod(shape)
+        flat = torch.empty(pos, dtype=torch.bfloat16, device=dev)
+        shapes = {name: shape for name, shape, _ in tensors}
+
+        def part_range(name, c0, cc):
+            n = math.prod(shapes[name])
+            lo, hi = (c0 * ce, min(n, (c0 + cc) * ce)) if cc else (0, n)
+            return goff[name] + lo, goff[name] + hi
+
+        out_views = {}
+        for name, c0, cc in owned:
+            lo, hi = part_range(name, c0, cc)
+            out_views[name] = flat[lo:hi] if cc else flat[lo:hi].view(shapes[name])
+        spans = []
+        for parts in owned_all:
+            rs = [part_range(*p) for p in parts]
+            spans.append((min(r[0] for r in rs), max(r[1] for r in rs)) if rs else (0, 0))
+    loader = DeviceLoader(image, device=local, owned=owned, out=out_views)
     # elements / compressed bytes this rank decodes per step
     dec_elems, algo_bytes = 0, 0
     for name, c0, cc in owned:
@@ -415,6 +446,38 @@ def main():
         if not torch.equal(ref.view(torch.int16), loader.out[name].reshape(-1).view(torch.int16)):
             bad.append(name)
     n_bad = int(sum_over_ranks(len(bad)))
+
+    # ---- replicated materialisation (reported separately, not in `value`) ---
+    rep = None
+    if replicate:
+        from bigsmall_b200.replicate import replicate_spans, span_checksums
+        own_sum = sum(int(originals[name].reshape(-1)[(c0 * ce if cc else 0):
+                                                       (min(originals[name].numel(), (c0 + cc) * ce) if cc
+                                                        else originals[name].numel())]
+                          .view(torch.int16).to(torch.int64).sum()) for name, c0, cc in owned)
+        for _ in range(2):
+            replicate_spans(flat, spans)
+        barrier()
+        rs, re_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        reps = 3
+        rs.record(stream)
+        for _ in range(reps):
+            replicate_spans(flat, spans)
+        re_.record(stream)
+        torch.cuda.synchronize()
+        rep_ms = max_over_ranks(rs.elapsed_time(re_) / reps)
+        cs = span_checksums(flat, spans)
+        allcs = [torch.zeros_like(cs) for _ in range(world)]
+        dist.all_gather(allcs, cs)
+        same = all(torch.equal(c, allcs[0]) for c in allcs)
+        own_ok = int(cs[rank]) == own_sum
+        rep_ok = int(sum_over_ranks(0 if (same and own_ok) else 1)) == 0
+        recv = 2 * (flat.numel() - (spans[rank][1] - spans[rank][0]))
+        rep = {"ms": round(rep_ms, 3), "bytes_received_per_gpu": recv,
+               "GBs_received_per_gpu": round(recv / rep_ms / 1e6, 1),
+               "collective": "NCCL broadcast of each owner's contiguous span (torch.distributed)",
+               "verified": "per-span 16-bit checksums equal on every rank and equal to the owners' originals"
+               if rep_ok else "MISMATCH"}
     total_elems = sum_over_ranks(dec_elems)
     total_comp = sum_over_ranks(sum(int(image.tensors[n]["compressed_bytes"]) for n in image.tensors))
     h2d = loader.h2d_bytes()
@@ -444,6 +507,7 @@ def main():
                 "path": "bigsmall_b200.loader.DeviceLoader.run_async (pinned H2D of compressed blobs "
                         f"in {n_groups} groups overlapped with decode) + status check"},
             "gpu_launches": 2 * a.steps,
+            "replicate": rep,
             "clocks": clk.summary(),
             "verified": f"bitwise equal on device for all {len(tensors)} tensors" if n_bad == 0 else f"MISMATCH in {n_bad} parts",
             "compression_ratio": round(total_comp / (2 * sum(math.prod(s) for _, s, _ in tensors)), 5)
@@ -727,44 +791,56 @@ def bench_stream(a, torch, dev, world, rank, dist, local):
 
     # warm-up runs cover every sequence length of the timed run: the first
     # occurrence of each KV-cache length pays one-time library costs
+    hp = torch.cuda.Stream(dev, priority=torch.cuda.Stream.priority_range()[1])
     ref = synthetic.resident_model(cfg, w, device=dev)
-    synthetic.greedy(ref, prompt, steps)
-    ids_r, lg_r, pre_r, dec_r = synthetic.greedy(ref, prompt, steps)
+    with torch.cuda.stream(hp):
+        synthetic.greedy(ref, prompt, steps)
+        ids_r, lg_r, pre_r, dec_r = synthetic.greedy(ref, prompt, steps)
     del ref
 
-    sm = BigSmallStreamingModel(StreamingLoader(image, device=dev), cfg)
-    synthetic.greedy(sm.model, prompt, steps)
-    ids_s, lg_s, pre_s, dec_s = synthetic.greedy(sm.model, prompt, steps)
-    sm.check()
-    same_ids = bool(torch.equal(ids_r, ids_s))
-    same_logits = bool(torch.equal(lg_r.view(torch.int16), lg_s.view(torch.int16)))
-    # standalone decode time of one layer (for the hidden-fraction accounting)
-    side = torch.cuda.current_stream(dev)
-    layer_ms = _timed(torch, lambda: sm._bundles[(1, 1)].decode(side), 10, 3, side)
-    layer_raw = sum(2 * sm._slots[0][k].numel() for k in sm._slots[0])
-    dec_work = layers * layer_ms
+    loader = StreamingLoader(image, device=dev)
+    for k, prio in [(int(v), int(p)) for v in a.stream_ctas.split(",") for p in a.stream_priority.split(",")]:
+        sm = BigSmallStreamingModel(loader, cfg, decode_ctas_per_sm=k or None)
+        # the model runs on a high-priority stream (as BigSmallStreamingModel.forward does) or on
+        # a default-priority one, the same priority as the side-stream decode
+        run_stream = hp if prio else torch.cuda.Stream(dev)
+        with torch.cuda.stream(run_stream):
+            synthetic.greedy(sm.model, prompt, steps)
+            ids_s, lg_s, pre_s, dec_s = synthetic.greedy(sm.model, prompt, steps)
+        sm.check()
+        same_ids = bool(torch.equal(ids_r, ids_s))
+        same_logits = bool(torch.equal(lg_r.view(torch.int16), lg_s.view(torch.int16)))
+        # standalone decode time of one layer with the same grid (hidden-fraction accounting)
+        side = torch.cuda.current_stream(dev)
+        layer_ms = _timed(torch, lambda: sm._bundles[(1, 1)].decode(side), 10, 3, side)
+        layer_raw = sum(2 * sm._slots[0][kk].numel() for kk in sm._slots[0])
+        dec_work = layers * layer_ms
 
-    def hidden(t_stream, t_res, n_passes):
-        work = dec_work * n_passes
-        return max(0.0, min(1.0, 1.0 - (t_stream - t_res) / work)) if work > 0 else None
+        def hidden(t_stream, t_res, n_passes):
+            work = dec_work * n_passes
+            return max(0.0, min(1.0, 1.0 - (t_stream - t_res) / work)) if work > 0 else None
 
-    res = {
-        "metric": "streaming inference ms/token (BASELINE config 4), batch 1", "unit": "ms/token",
-        "value": round(dec_s / steps, 3), "resident_ms_per_token": round(dec_r / steps, 3),
-        "prefill_ms": {"streaming": round(pre_s, 2), "resident": round(pre_r, 2)},
-        "layer_decode_ms": round(layer_ms, 4), "layer_decoded_GBs": round(layer_raw / layer_ms / 1e6, 1),
-        "hidden_fraction": {"prefill": hidden(pre_s, pre_r, 1), "decode": hidden(dec_s, dec_r, steps)},
-        "logits_bit_identical": same_logits, "tokens_identical": same_ids,
-        "hbm_resident_GB": {"streaming": round((comp_bytes + raw_bytes / layers * 0) / 1e9, 2),
-                            "compressed_model": round(comp_bytes / 1e9, 2), "full_model": round(raw_bytes / 1e9, 2)},
-        "ratio": round(comp_bytes / raw_bytes, 5), "higher_is_better": False, "n_gpus": 1,
-        "config": {"model": "Qwen2.5-14B-shaped random init (seed 0)", "layers": layers, "prompt": 512,
-                   "new_tokens": steps, "slots": 2, "chunk_elems": ce},
-        "setup_s": round(setup_s, 1)}
-    res["hbm_resident_GB"]["streaming"] = round((comp_bytes + sum(
-        2 * t.numel() for n, t in w.items() if ".layers." not in n) + 2 * layer_raw) / 1e9, 2)
-    print(json.dumps(res), flush=True)
-    sm.close()
+        res = {
+            "metric": "streaming inference ms/token (BASELINE config 4), batch 1", "unit": "ms/token",
+            "value": round(dec_s / steps, 3), "resident_ms_per_token": round(dec_r / steps, 3),
+            "prefill_ms": {"streaming": round(pre_s, 2), "resident": round(pre_r, 2)},
+            "layer_decode_ms": round(layer_ms, 4), "layer_decoded_GBs": round(layer_raw / layer_ms / 1e6, 1),
+            "hidden_fraction": {"prefill": hidden(pre_s, pre_r, 1), "decode": hidden(dec_s, dec_r, steps)},
+            "logits_bit_identical": same_logits, "tokens_identical": same_ids,
+            "hbm_resident_GB": {"compressed_model": round(comp_bytes / 1e9, 2), "full_model": round(raw_bytes / 1e9, 2)},
+            "ratio": round(comp_bytes / raw_bytes, 5), "higher_is_better": False, "n_gpus": 1,
+            "config": {"model": "Qwen2.5-14B-shaped random init (seed 0)", "layers": layers, "prompt": 512,
+                       "new_tokens": steps, "slots": 2, "chunk_elems": ce, "coder": a.coder,
+                       "decode_ctas_per_sm": k or "uncapped", "decode_max_ctas": sm.decode_max_ctas,
+                       "model_stream": "high priority" if prio else "default priority (same as the decode)",
+                       "resident_run": "high-priority stream"},
+            "setup_s": round(setup_s, 1)}
+        res["hbm_resident_GB"]["streaming"] = round((comp_bytes + sum(
+            2 * t.numel() for n, t in w.items() if ".layers." not in n) + 2 * layer_raw) / 1e9, 2)
+        print(json.dumps(res), flush=True)
+        sm.close()
+        del sm
+        torch.cuda.empty_cache()
 
 if __name__ == "__main__":
     main()

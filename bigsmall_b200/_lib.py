@@ -73,6 +73,7 @@ SIGNATURES = {
     "bs_plan_decode": (_I, [_P, _P]),
     "bs_plan_check": (_I, [_P, _P, ctypes.POINTER(_U32)]),
     "bs_plan_n_tensors": (_I, [_P]),
+    "bs_plan_set_max_ctas": (_I, [_P, _I]),
     "bs_plan_destroy": (_I, [_P]),
     "bs_xc_decode_noalloc": (_I, [ctypes.POINTER(XcTensor), _I, _P, ctypes.POINTER(_U32)]),
     "bs_par_plan_create": (_I, [_P, _U64, _U64, _P, _P, _I, ctypes.POINTER(_P)]),

@@ -80,6 +80,7 @@ struct bs_plan {
     XcItem *d_items = nullptr;
     int n_items = 0;
     uint32_t coders = 0;        // decode kernels to launch (bit per coder)
+    int max_ctas = 0;           // decode grid cap (0: one CTA per work item)
     uint32_t *d_tables = nullptr;
     // serial-stream formats (bf16_parallel_v1, bf16_se_single_kernel, bf16_se_tans)
     ParJob *d_jobs = nullptr;
@@ -153,6 +154,14 @@ const char *bs_status_string(int status) {
         case BS_E_PRECISION: return "precision mismatch";
         default: return "unknown status";
     }
+}
+
+int bs_plan_set_max_ctas(bs_plan *p, int max_ctas) {
+    if (!p) return fail(BS_E_INVALID_ARG, "plan is NULL");
+    if (max_ctas < 0) return fail(BS_E_INVALID_ARG, "max_ctas must be >= 0");
+    if (p->kind != kPlanXc) return fail(BS_E_INVALID_ARG, "max_ctas applies to bf16_exp_chunked_v1 plans");
+    p->max_ctas = max_ctas;
+    return BS_OK;
 }
 
 int bs_plan_n_tensors(const bs_plan *plan) { return plan ? plan->n_tensors : 0; }
@@ -272,7 +281,8 @@ int bs_plan_decode(bs_plan *p, void *stream) {
         if (p->n_internal == 0) return BS_OK;
         e = launch_xc_prepare(p->d_tens, p->n_internal, p->d_tables, p->d_errs, s);
         if (e == cudaSuccess)
-            e = launch_xc_decode(p->d_tens, p->d_items, p->n_items, p->d_tables, p->d_errs, p->coders, s);
+            e = launch_xc_decode(p->d_tens, p->d_items, p->n_items, p->d_tables, p->d_errs, p->coders,
+                                 p->max_ctas, s);
     } else if (p->kind == kPlanPar) {
         if (p->n_internal == 0) return BS_OK;
         e = cudaMemsetAsync(p->d_errs, 0, 4ull * p->n_internal, s);

@@ -163,7 +163,8 @@ constexpr uint32_t kXcAllCoders = 7u;   // BS_CODER_RANS | TANS | RANS_PAIR bits
 // Union of the tensors' coder masks (a zero mask counts as every coder).
 uint32_t xc_launch_mask(const XcTensorDev *h_tens, int n);
 cudaError_t launch_xc_decode(const XcTensorDev *d_tens, const XcItem *d_items, int n_items,
-                             const uint32_t *d_tables, uint32_t *d_errs, uint32_t coders, cudaStream_t s);
+                             const uint32_t *d_tables, uint32_t *d_errs, uint32_t coders, int max_ctas,
+                             cudaStream_t s);
 int xc_warps_per_cta();
 cudaError_t launch_xc_noalloc(const XcTensorDev *h_tens, const uint32_t *range_count, int n, cudaStream_t s,
                               uint32_t *h_status);

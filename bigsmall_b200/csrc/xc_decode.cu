@@ -616,71 +616,78 @@ __device__ __forceinline__ void decode_chunk_pair(uint32_t tab_s, uint8_t *ring_
     if (code && lane == 0) atomicOr(err, code);
 }
 
+// Both decode kernels walk the work list with a grid stride, so a plan can
+// cap its CTAs (bs_plan_set_max_ctas) and leave SM room to kernels on other
+// streams; uncapped, the grid is one CTA per item and the loop runs once.
 __global__ void __launch_bounds__(kThreads, kPairMinBlocks) xc_decode_pair_kernel(const XcTensorDev *__restrict__ tens,
-                                                                  const XcItem *__restrict__ items,
+                                                                  const XcItem *__restrict__ items, int n_items,
                                                                   const uint32_t *__restrict__ tables,
                                                                   uint32_t *errs) {
     extern __shared__ __align__(16) uint8_t smem[];
     uint8_t *s_ring = smem + kPairTableBytes;
-    const XcItem it = items[blockIdx.x];
-    const XcTensorDev &T = tens[it.tensor];
-    if (T.coder != 2) return;   // other coders: xc_decode_kernel; flagged tensors: skipped
-    const uint32_t P = T.prec;
-    const uint32_t M = 1u << P;
-    const uint4 *src = reinterpret_cast<const uint4 *>(tables + static_cast<uint64_t>(it.tensor) * kXcTableWords);
-    for (uint32_t i = threadIdx.x; i < M / 2; i += kThreads) reinterpret_cast<uint4 *>(smem)[i] = src[i];
-    __syncthreads();
     const uint32_t warp = threadIdx.x >> 5;
-    if (warp >= it.n_chunks) return;
-    const uint32_t c = it.first_chunk + warp;
-    const uint8_t *blob = T.blob;
-    const uint32_t *cs = reinterpret_cast<const uint32_t *>(blob + kXcTabOff);
-    const uint32_t a = cs[c], z = cs[c + 1];
-    const uint64_t e0 = static_cast<uint64_t>(c) * T.chunk_elems;
-    const uint64_t left = T.n - e0;
-    const uint32_t cn = left < T.chunk_elems ? static_cast<uint32_t>(left) : T.chunk_elems;
-    decode_chunk_pair(static_cast<uint32_t>(__cvta_generic_to_shared(smem)), s_ring + warp * kPairWarpRing,
-                      blob + T.chunks_off + 16ull * a, 16u * (z - a), blob + T.plane_off + e0,
-                      T.out + (e0 - static_cast<uint64_t>(T.chunk_begin) * T.chunk_elems), cn, P,
-                      &errs[it.tensor]);
+    for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
+        const XcItem it = items[item];
+        const XcTensorDev &T = tens[it.tensor];
+        if (T.coder != 2) continue;   // other coders: xc_decode_kernel; flagged tensors: skipped
+        const uint32_t P = T.prec;
+        const uint32_t M = 1u << P;
+        const uint4 *src = reinterpret_cast<const uint4 *>(tables + static_cast<uint64_t>(it.tensor) * kXcTableWords);
+        __syncthreads();   // the previous item's warps are done with the table
+        for (uint32_t i = threadIdx.x; i < M / 2; i += kThreads) reinterpret_cast<uint4 *>(smem)[i] = src[i];
+        __syncthreads();
+        if (warp >= it.n_chunks) continue;
+        const uint32_t c = it.first_chunk + warp;
+        const uint8_t *blob = T.blob;
+        const uint32_t *cs = reinterpret_cast<const uint32_t *>(blob + kXcTabOff);
+        const uint32_t a = cs[c], z = cs[c + 1];
+        const uint64_t e0 = static_cast<uint64_t>(c) * T.chunk_elems;
+        const uint64_t left = T.n - e0;
+        const uint32_t cn = left < T.chunk_elems ? static_cast<uint32_t>(left) : T.chunk_elems;
+        decode_chunk_pair(static_cast<uint32_t>(__cvta_generic_to_shared(smem)), s_ring + warp * kPairWarpRing,
+                          blob + T.chunks_off + 16ull * a, 16u * (z - a), blob + T.plane_off + e0,
+                          T.out + (e0 - static_cast<uint64_t>(T.chunk_begin) * T.chunk_elems), cn, P,
+                          &errs[it.tensor]);
+    }
 }
 
 __global__ void __launch_bounds__(kThreads) xc_decode_kernel(const XcTensorDev *__restrict__ tens,
-                                                             const XcItem *__restrict__ items,
+                                                             const XcItem *__restrict__ items, int n_items,
                                                              const uint32_t *__restrict__ tables,
                                                              uint32_t *errs) {
     extern __shared__ __align__(16) uint8_t smem[];
     uint32_t *s_tab = reinterpret_cast<uint32_t *>(smem);
     uint8_t *s_ring = smem + kXcMaxTable * 4;
-
-    const XcItem it = items[blockIdx.x];
-    const XcTensorDev &T = tens[it.tensor];
-    const uint32_t coder = T.coder;
-    if (coder > 1) return;   // the table build flagged this tensor
-    const uint32_t P = T.prec;
-    const uint32_t M = 1u << P;
-    const uint4 *src = reinterpret_cast<const uint4 *>(tables + static_cast<uint64_t>(it.tensor) * kXcTableWords);
-    for (uint32_t i = threadIdx.x; i < M / 4; i += kThreads) reinterpret_cast<uint4 *>(s_tab)[i] = src[i];
-    __syncthreads();
-
     const uint32_t warp = threadIdx.x >> 5;
-    if (warp >= it.n_chunks) return;
-    const uint32_t c = it.first_chunk + warp;
-    const uint8_t *blob = T.blob;
-    const uint32_t *cs = reinterpret_cast<const uint32_t *>(blob + kXcTabOff);
-    const uint32_t a = cs[c], z = cs[c + 1];
-    const uint8_t *rec = blob + T.chunks_off + 16ull * a;
-    const uint32_t rec_bytes = 16u * (z - a);
-    const uint64_t e0 = static_cast<uint64_t>(c) * T.chunk_elems;
-    const uint64_t left = T.n - e0;
-    const uint32_t cn = left < T.chunk_elems ? static_cast<uint32_t>(left) : T.chunk_elems;
-    uint8_t *ring = s_ring + warp * kWarpRing;
-    const uint8_t *plane = blob + T.plane_off + e0;
-    uint16_t *out = T.out + (e0 - static_cast<uint64_t>(T.chunk_begin) * T.chunk_elems);
-    if (coder == 0)
-        decode_chunk<0>(s_tab, ring, rec, rec_bytes, plane, out, cn, P, &errs[it.tensor]);
-    else
-        decode_chunk<1>(s_tab, ring, rec, rec_bytes, plane, out, cn, P, &errs[it.tensor]);
+    for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
+        const XcItem it = items[item];
+        const XcTensorDev &T = tens[it.tensor];
+        const uint32_t coder = T.coder;
+        if (coder > 1) continue;   // the table build flagged this tensor, or the pair kernel's
+        const uint32_t P = T.prec;
+        const uint32_t M = 1u << P;
+        const uint4 *src = reinterpret_cast<const uint4 *>(tables + static_cast<uint64_t>(it.tensor) * kXcTableWords);
+        __syncthreads();   // the previous item's warps are done with the table
+        for (uint32_t i = threadIdx.x; i < M / 4; i += kThreads) reinterpret_cast<uint4 *>(s_tab)[i] = src[i];
+        __syncthreads();
+        if (warp >= it.n_chunks) continue;
+        const uint32_t c = it.first_chunk + warp;
+        const uint8_t *blob = T.blob;
+        const uint32_t *cs = reinterpret_cast<const uint32_t *>(blob + kXcTabOff);
+        const uint32_t a = cs[c], z = cs[c + 1];
+        const uint8_t *rec = blob + T.chunks_off + 16ull * a;
+        const uint32_t rec_bytes = 16u * (z - a);
+        const uint64_t e0 = static_cast<uint64_t>(c) * T.chunk_elems;
+        const uint64_t left = T.n - e0;
+        const uint32_t cn = left < T.chunk_elems ? static_cast<uint32_t>(left) : T.chunk_elems;
+        uint8_t *ring = s_ring + warp * kWarpRing;
+        const uint8_t *plane = blob + T.plane_off + e0;
+        uint16_t *out = T.out + (e0 - static_cast<uint64_t>(T.chunk_begin) * T.chunk_elems);
+        if (coder == 0)
+            decode_chunk<0>(s_tab, ring, rec, rec_bytes, plane, out, cn, P, &errs[it.tensor]);
+        else
+            decode_chunk<1>(s_tab, ring, rec, rec_bytes, plane, out, cn, P, &errs[it.tensor]);
+    }
 }
 
 cudaError_t launch_xc_prepare(XcTensorDev *d_tens, int n_tensors, uint32_t *d_tables, uint32_t *d_errs,
@@ -715,14 +722,16 @@ uint32_t xc_launch_mask(const XcTensorDev *h_tens, int n) {
 // coder 2 has its own.  A CTA whose tensor uses the other family (possible
 // only with coder_mask 0) or was flagged by the prepare kernel returns at once.
 cudaError_t launch_xc_decode(const XcTensorDev *d_tens, const XcItem *d_items, int n_items,
-                             const uint32_t *d_tables, uint32_t *d_errs, uint32_t coders, cudaStream_t s) {
+                             const uint32_t *d_tables, uint32_t *d_errs, uint32_t coders, int max_ctas,
+                             cudaStream_t s) {
     if (n_items <= 0) return cudaSuccess;
+    const int grid = max_ctas > 0 && max_ctas < n_items ? max_ctas : n_items;
     cudaError_t e = cudaSuccess;
     if (coders & ((1u << BS_CODER_RANS) | (1u << BS_CODER_TANS))) {
         const size_t smem = kXcMaxTable * 4 + kWarps * kWarpRing;
         e = smem_opt_in(xc_decode_kernel, smem, g_attr_rans);
         if (e != cudaSuccess) return e;
-        xc_decode_kernel<<<n_items, kThreads, smem, s>>>(d_tens, d_items, d_tables, d_errs);
+        xc_decode_kernel<<<grid, kThreads, smem, s>>>(d_tens, d_items, n_items, d_tables, d_errs);
         e = cudaGetLastError();
         if (e != cudaSuccess) return e;
     }
@@ -730,7 +739,7 @@ cudaError_t launch_xc_decode(const XcTensorDev *d_tens, const XcItem *d_items, i
         const size_t psmem = kPairTableBytes + kWarps * kPairWarpRing;
         e = smem_opt_in(xc_decode_pair_kernel, psmem, g_attr_pair);
         if (e != cudaSuccess) return e;
-        xc_decode_pair_kernel<<<n_items, kThreads, psmem, s>>>(d_tens, d_items, d_tables, d_errs);
+        xc_decode_pair_kernel<<<grid, kThreads, psmem, s>>>(d_tens, d_items, n_items, d_tables, d_errs);
         e = cudaGetLastError();
     }
     return e;

@@ -123,7 +123,8 @@ class XcPlan(_Plan):
     BS_DEV_HEADER rather than being skipped.
     """
 
-    def __init__(self, entries: Iterable[tuple], device: Optional[int] = None, coders=None):
+    def __init__(self, entries: Iterable[tuple], device: Optional[int] = None, coders=None,
+                 max_ctas: Optional[int] = None):
         entries = list(entries)
         if coders is None or isinstance(coders, (str, int)):
             coders = [coders] * len(entries)
@@ -162,6 +163,13 @@ class XcPlan(_Plan):
         L = _lib.load()
         _lib.check(L.bs_xc_plan_create(arr, len(entries), dev, ctypes.byref(h)), "bs_xc_plan_create")
         super().__init__(h, dev, keep, len(entries))
+        if max_ctas:
+            self.set_max_ctas(max_ctas)
+
+    def set_max_ctas(self, max_ctas: int) -> None:
+        """Cap the decode grid at ``max_ctas`` CTAs (0: uncapped) so kernels on
+        other streams keep SM room while this plan decodes."""
+        _lib.check(_lib.load().bs_plan_set_max_ctas(self._h, int(max_ctas)), "bs_plan_set_max_ctas")
 
 
 class ParPlan(_Plan):

@@ -384,8 +384,10 @@ class ResidentContainer:
         m = self.image.tensors[self.resolve(name)]
         return torch.empty(m["shape"] or [], dtype=TORCH_DTYPES.get(m["dtype"], torch.uint8), device=self.device)
 
-    def bundle(self, outputs: dict) -> Bundle:
-        """outputs: {name: device tensor of the tensor's shape/dtype}."""
+    def bundle(self, outputs: dict, max_ctas: Optional[int] = None) -> Bundle:
+        """outputs: {name: device tensor of the tensor's shape/dtype}.
+        ``max_ctas`` caps the bf16_exp_chunked_v1 decode grid (see
+        :meth:`bigsmall_b200.gpu.XcPlan.set_max_ctas`)."""
         xc, coders, se, plans, copies = [], [], [], [], []
         for name, out in outputs.items():
             real = self.resolve(name)
@@ -406,7 +408,7 @@ class ResidentContainer:
         if se:
             plans.append(gpu.SePlan(se, device=self.device.index))
         if xc:
-            plans.insert(0, gpu.XcPlan(xc, device=self.device.index, coders=coders))
+            plans.insert(0, gpu.XcPlan(xc, device=self.device.index, coders=coders, max_ctas=max_ctas))
         return Bundle(plans, copies)
 
     def decode(self, names, stream=None) -> dict:

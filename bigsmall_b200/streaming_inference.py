@@ -11,6 +11,10 @@ Here:
   * the compressed container stays resident in HBM; non-layer tensors
     (embeddings, final norm, lm_head) are decoded once;
   * decoded layers live in ``slots`` (2) fixed device buffers allocated once;
+  * the side-stream decode runs on at most ``decode_ctas_per_sm`` CTAs per SM
+    (its kernels walk their work list), so the GEMMs of the running layer are
+    not queued behind a full-GPU decode grid, and ``forward``/``generate`` run
+    the model on a higher-priority stream than the decode;
   * global layer execution k uses slot ``k % slots``.  After layer i runs on the
     main stream, the decode of the layer that runs ``slots`` executions later
     is enqueued on a side stream into the slot just released, ordered by CUDA
@@ -73,7 +77,7 @@ def _materialize_meta_buffers(model, config, device) -> None:
 class BigSmallStreamingModel:
     def __init__(self, bs_path, hf_config, device: str = "cuda", dtype=None,
                  layer_template: str = "model.layers.{}", prefetch: int = 1, slots: int = 2,
-                 model_cls=None):
+                 model_cls=None, decode_ctas_per_sm: Optional[int] = 3, priority_compute: bool = True):
         from transformers import AutoConfig, AutoModelForCausalLM
         self.device = torch.device(device)
         if self.device.index is None:
@@ -114,13 +118,23 @@ class BigSmallStreamingModel:
                     raise ValueError(f"{n}: shape/dtype differs from layer 0")
         self._slots = [{k: self.loader.res.empty_like(self._local[0][k]) for k in sorted(keys0)}
                        for _ in range(self.n_slots)]
-        # one prebuilt decode bundle per (layer, slot)
+        # one prebuilt decode bundle per (layer, slot); the side-stream decode
+        # is capped at decode_ctas_per_sm CTAs per SM so that the layer running
+        # on the main stream keeps SM room (None: uncapped)
+        sms = torch.cuda.get_device_properties(self.device).multi_processor_count
+        self.decode_max_ctas = sms * decode_ctas_per_sm if decode_ctas_per_sm else 0
         self._bundles = {}
         for i in range(self.n_layers):
             for s in range(self.n_slots):
                 self._bundles[(i, s)] = self.loader.res.bundle(
-                    {self._local[i][k]: self._slots[s][k] for k in self._local[i]})
+                    {self._local[i][k]: self._slots[s][k] for k in self._local[i]},
+                    max_ctas=self.decode_max_ctas)
         self._side = torch.cuda.Stream(self.device)
+        # forward()/generate() run the model on a higher-priority stream than
+        # the side-stream decode, so the block scheduler places the running
+        # layer's CTAs first and the decode fills the gaps
+        hi = torch.cuda.Stream.priority_range()[1]
+        self.compute_stream = torch.cuda.Stream(self.device, priority=hi) if priority_compute else None
         self._decoded = [torch.cuda.Event() for _ in range(self.n_slots)]
         self._released = [torch.cuda.Event() for _ in range(self.n_slots)]
         self._k = 0                 # global layer-execution counter (selects the slot)
@@ -201,15 +215,25 @@ class BigSmallStreamingModel:
             hf_config_path = cand
         return cls(p, hf_config_path, device=device, dtype=dtype, layer_template=layer_template, prefetch=prefetch)
 
+    def _on_compute_stream(self, fn):
+        if self.compute_stream is None:
+            return fn()
+        caller = torch.cuda.current_stream(self.device)
+        self.compute_stream.wait_stream(caller)
+        with torch.cuda.stream(self.compute_stream):
+            out = fn()
+        caller.wait_stream(self.compute_stream)
+        return out
+
     def forward(self, *args, **kwargs):
         with torch.no_grad():
-            return self.model(*args, **kwargs)
+            return self._on_compute_stream(lambda: self.model(*args, **kwargs))
 
     def generate(self, input_ids, max_new_tokens: int = 20, **kwargs):
         kwargs.setdefault("do_sample", False)
         kwargs.setdefault("max_new_tokens", max_new_tokens)
         with torch.no_grad():
-            return self.model.generate(input_ids.to(self.device), **kwargs)
+            return self._on_compute_stream(lambda: self.model.generate(input_ids.to(self.device), **kwargs))
 
     def check(self) -> None:
         """Synchronise and raise if any layer decode reported a stream error."""

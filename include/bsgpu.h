@@ -100,6 +100,12 @@ int bs_plan_decode(bs_plan *plan, void *stream);
 int bs_plan_check(bs_plan *plan, void *stream, uint32_t *status_out);
 
 int bs_plan_n_tensors(const bs_plan *plan);
+/* Cap the decode grid of a bf16_exp_chunked_v1 plan at max_ctas CTAs (0: one
+ * CTA per work item, the default).  A capped plan leaves SM room to kernels on
+ * other streams, e.g. a layer decode overlapped with the previous layer's
+ * GEMMs; the CTAs walk the work list until it is done.  No reference
+ * counterpart. */
+int bs_plan_set_max_ctas(bs_plan *plan, int max_ctas);
 int bs_plan_destroy(bs_plan *plan);
 
 /* ---- allocation-free decode -------------------------------------------- */

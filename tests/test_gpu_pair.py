@@ -159,3 +159,28 @@ def test_coder_hint_selects_kernels_and_rejects_mismatch():
         assert ei.value.device_status[0] & 0x01, hint
     with pytest.raises(ValueError):
         gpu.XcPlan([(_dev(pair), torch.empty(n, dtype=torch.bfloat16, device="cuda"), 4096)], coders=["pair", "rans"])
+
+
+@pytest.mark.parametrize("max_ctas", [1, 3, 150])
+def test_capped_grid_walks_the_whole_work_list(max_ctas):
+    """A plan capped at a few CTAs (bs_plan_set_max_ctas) still decodes every
+    chunk of every tensor, for both decode kernels."""
+    from bigsmall_b200 import gpu
+    specs = [(300_001, 2, 65536), (40_000, 0, 256), (70_001, 2, 256), (123_457, 1, 4096)]
+    entries, outs, raws = [], [], []
+    for i, (n, coder, ce) in enumerate(specs):
+        raw = _wide(n, 40 + i)
+        entries.append((_dev(O.xc_encode(raw, coder, 12, ce)), torch.empty(n, dtype=torch.bfloat16, device="cuda"), ce))
+        outs.append(entries[-1][1])
+        raws.append(raw)
+    with gpu.XcPlan(entries, max_ctas=max_ctas) as plan:
+        for _ in range(2):
+            for o in outs:
+                o.fill_(0)
+            plan.run()
+            for raw, o in zip(raws, outs):
+                assert o.cpu().view(torch.uint8).numpy().tobytes() == raw
+        plan.set_max_ctas(0)
+        plan.run()
+        for raw, o in zip(raws, outs):
+            assert o.cpu().view(torch.uint8).numpy().tobytes() == raw
