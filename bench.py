@@ -475,7 +475,7 @@ def main():
         recv = 2 * (flat.numel() - (spans[rank][1] - spans[rank][0]))
         rep = {"ms": round(rep_ms, 3), "bytes_received_per_gpu": recv,
                "GBs_received_per_gpu": round(recv / rep_ms / 1e6, 1),
-               "collective": "NCCL broadcast of each owner's contiguous span (torch.distributed)",
+               "collective": "NCCL point-to-point batch: every owner span to every rank (torch.distributed.batch_isend_irecv)",
                "verified": "per-span 16-bit checksums equal on every rank and equal to the owners' originals"
                if rep_ok else "MISMATCH"}
     total_elems = sum_over_ranks(dec_elems)

@@ -2,11 +2,12 @@
 
 Decode needs no communication: each rank decodes its own contiguous span of
 the container's values (tensors in name order).  When every GPU must hold the
-whole model, each rank's span is broadcast from its owner over NCCL (NVLink /
-NVSwitch on one box) into the same offsets of every rank's flat buffer.  The
-spans differ in length by up to one chunk, so this is a sequence of
-per-owner broadcasts rather than an equal-split all-gather; each broadcast
-already drives every link.  Reported separately from the decode throughput.
+whole model, every rank sends its span to every other rank and receives
+theirs into the same offsets of its flat buffer: one batch of point-to-point
+transfers over NCCL (NVLink / NVSwitch on one box), all in flight together so
+every GPU's links carry traffic in both directions.  The spans differ in
+length by up to one chunk, which an equal-split all-gather would not allow.
+Reported separately from the decode throughput.
 """
 from __future__ import annotations
 
@@ -24,10 +25,21 @@ def replicate_spans(flat: torch.Tensor, spans: Sequence[tuple], group=None) -> N
         raise ValueError(f"need one span per rank ({world}), got {len(spans)}")
     b = flat.view(torch.uint8)          # bytes: every backend carries uint8
     es = flat.element_size()
-    for r, (lo, hi) in enumerate(spans):
+    me = dist.get_rank(group)
+    glob = (lambda r: dist.get_global_rank(group, r)) if group is not None else (lambda r: r)
+    lo, hi = spans[me]
+    ops = []
+    for r in range(world):
+        if r == me:
+            continue
         if hi > lo:
-            dist.broadcast(b[lo * es:hi * es], src=dist.get_global_rank(group, r) if group is not None else r,
-                           group=group)
+            ops.append(dist.P2POp(dist.isend, b[lo * es:hi * es], glob(r), group))
+        rlo, rhi = spans[r]
+        if rhi > rlo:
+            ops.append(dist.P2POp(dist.irecv, b[rlo * es:rhi * es], glob(r), group))
+    if ops:
+        for w in dist.batch_isend_irecv(ops):
+            w.wait()
 
 
 def span_checksums(flat: torch.Tensor, spans: Sequence[tuple]) -> torch.Tensor:
