@@ -216,6 +216,35 @@ def cpu_baseline(torch, seconds: float = 8.0, threads=None, device="cuda:0"):
 
 
 # ---------------------------------------------------------------------------
+# reference arm: the reference's own CPU decoder on the box's host cores
+# ---------------------------------------------------------------------------
+def reference_arm(a, torch, world, rank):
+    """--impl reference: rank 0 alone times the reference's fastest CPU decoder
+    (its C port in oracle/) on all host threads; other ranks exit without work.
+    Needs no GPU (the sample is generated on the GPU when one is present)."""
+    if rank != 0:
+        return
+    from bigsmall_b200 import gpu
+    ce = a.chunk_elems or gpu.DEFAULT_CHUNK_ELEMS
+    config = {"workload": "llama3-8b-shaped bf16 container (BASELINE config 2), full-container decode",
+              "codec": "bf16_exp_chunked_v1", "coder": a.coder, "chunk_elems": ce, "prec": gpu.DEFAULT_PREC,
+              "partition": "contiguous chunk-span ownership, no collective", "ranks": world,
+              "l2": "inputs (~10.6 GB compressed) far larger than the 126 MB L2; no flush"}
+    device = "cuda:0" if torch.cuda.is_available() else "cpu"
+    res = cpu_baseline(torch, seconds=a.cpu_seconds, device=device)
+    line = {"metric": METRIC, "value": round(res["value"], 4), "unit": "GB/s", "n_gpus": world,
+            "steps": a.steps, "warmup": a.warmup, "ms_per_step": None, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "u16", "data": "synthetic",
+            "config": config, "impl": "reference",
+            "cpu_baseline": {"value": round(res["value"], 4), "unit": "GB/s", "cores": res["cores"],
+                             "kind": res["kind"], "sample": res["sample"]},
+            "e2e": {"value": round(res["value"], 4), "unit": "GB/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0},
+            "note": "reference is Python/Numba; timed through its C port in oracle/ on host cores"}
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -233,9 +262,11 @@ def main():
                     help="config 4: comma list of 0/1: run the model on a high-priority stream (1) or not")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=8.0)
-    ap.add_argument("--config", default="c2", choices=["c2", "small", "kv", "sweep", "stream", "mix", "legacy"],
+    ap.add_argument("--config", default="c2", choices=["c2", "small", "medium", "kv", "sweep", "stream", "mix",
+                                                      "legacy"],
                     help="c2: the benchmark workload; small: one 2^27-value tensor of the same "
-                         "distribution (compressed ~170 MB, above L2) for ncu captures; kv: BASELINE "
+                         "distribution (compressed ~170 MB, above L2) for ncu captures; medium: one "
+                         "2^30-value tensor (fills every SM; ~3.5 GB on the device) for ncu captures; kv: BASELINE "
                          "config 5 (KV cache encode+decode); sweep: config 3 (coders x chunk size); "
                          "stream: config 4; mix: HBM calibration of the decode's read:write mix; "
                          "legacy: the reference's serial formats (bf16_se_single_kernel, bf16_se_tans) "
@@ -247,6 +278,8 @@ def main():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
+    if a.impl == "reference":
+        return reference_arm(a, torch, world, rank)
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     dist = None
@@ -265,25 +298,6 @@ def main():
               "partition": "contiguous chunk-span ownership, no collective", "ranks": world,
               "l2": "inputs (~10.6 GB compressed) far larger than the 126 MB L2; no flush"}
 
-    if a.impl == "reference":
-        if rank != 0:
-            if dist: dist.destroy_process_group()
-            return
-        res = cpu_baseline(torch, seconds=a.cpu_seconds)
-        # steps of the bounded sample, as the timed unit
-        line = {"metric": METRIC, "value": round(res["value"], 4), "unit": "GB/s", "n_gpus": world,
-                "steps": a.steps, "warmup": a.warmup, "ms_per_step": None, "higher_is_better": True,
-                "scaling": "strong", "vs_baseline": None, "dtype": "u16", "data": "synthetic",
-                "config": config, "impl": "reference",
-                "cpu_baseline": {"value": round(res["value"], 4), "unit": "GB/s", "cores": res["cores"],
-                                 "kind": res["kind"], "sample": res["sample"]},
-                "e2e": {"value": round(res["value"], 4), "unit": "GB/s", "h2d_bytes_per_step": 0,
-                        "d2h_bytes_per_step": 0},
-                "note": "reference is Python/Numba; timed through its C port in oracle/ on host cores"}
-        print(json.dumps(line), flush=True)
-        if dist: dist.destroy_process_group()
-        return
-
     if a.config == "kv":
         return bench_kv(a, torch, dev, world, rank, dist, local)
     if a.config == "sweep":
@@ -297,6 +311,9 @@ def main():
     if a.config == "small":
         tensors = [("model.layers.0.mlp.small_proj.weight", (1 << 15, 4096), "linear")]
         config["workload"] = "one 2^27-value bf16 tensor, config-2 distribution (profiling case)"
+    elif a.config == "medium":
+        tensors = [("model.layers.0.mlp.medium_proj.weight", (1 << 18, 4096), "linear")]
+        config["workload"] = "one 2^30-value bf16 tensor, config-2 distribution (profiling case, fills every SM)"
     else:
         tensors = llama3_8b_tensors()
     owned_all, load = partition(tensors, world, ce)
