@@ -227,7 +227,7 @@ def reference_arm(a, torch, world, rank):
     from bigsmall_b200 import gpu
     ce = a.chunk_elems or gpu.DEFAULT_CHUNK_ELEMS
     config = {"workload": "llama3-8b-shaped bf16 container (BASELINE config 2), full-container decode",
-              "codec": "bf16_exp_chunked_v1", "coder": a.coder, "chunk_elems": ce, "prec": gpu.DEFAULT_PREC,
+              "codec": "bf16_exp_chunked_v1", "coder": a.coder, "chunk_elems": ce, "prec": a.prec,
               "partition": "contiguous chunk-span ownership, no collective", "ranks": world,
               "l2": "inputs (~10.6 GB compressed) far larger than the 126 MB L2; no flush"}
     device = "cuda:0" if torch.cuda.is_available() else "cpu"
@@ -253,6 +253,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--chunk-elems", type=int, default=None)
     ap.add_argument("--coder", default="pair", choices=["rans", "tans", "pair"])
+    ap.add_argument("--prec", type=int, default=None, help="log2 of the coder's table size (default: the library's)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-replicate", action="store_true",
                     help="N>1: skip the separately reported NCCL materialisation of the full model on every GPU")
@@ -273,6 +274,9 @@ def main():
                          "on the config-1 tensor and on a batch of config-2 k/v tensors")
     a = ap.parse_args()
     a.warmup = max(3, a.warmup)
+    if a.prec is None:
+        from bigsmall_b200 import gpu as _gpu
+        a.prec = _gpu.DEFAULT_PREC
 
     import torch
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -294,7 +298,7 @@ def main():
 
     ce = a.chunk_elems or gpu.DEFAULT_CHUNK_ELEMS
     config = {"workload": "llama3-8b-shaped bf16 container (BASELINE config 2), full-container decode",
-              "codec": "bf16_exp_chunked_v1", "coder": a.coder, "chunk_elems": ce, "prec": gpu.DEFAULT_PREC,
+              "codec": "bf16_exp_chunked_v1", "coder": a.coder, "chunk_elems": ce, "prec": a.prec,
               "partition": "contiguous chunk-span ownership, no collective", "ranks": world,
               "l2": "inputs (~10.6 GB compressed) far larger than the 126 MB L2; no flush"}
 
@@ -325,7 +329,7 @@ def main():
     g = torch.Generator(device=dev).manual_seed(0)
     originals, blobs = {}, {}
     max_n = max(math.prod(s) for n, s, _ in tensors if n in owned_names)
-    enc = gpu.XcEncoder(max_n, ce, a.coder, gpu.DEFAULT_PREC, device=local)
+    enc = gpu.XcEncoder(max_n, ce, a.coder, a.prec, device=local)
     for name, shape, kind in tensors:
         x = gen_tensor(torch, g, shape, kind, dev)
         if name in owned_names:
@@ -348,7 +352,7 @@ def main():
         host[offs[name]:offs[name] + b.numel()].copy_(b)
         metas.append({"name": name, "shape": list(shape), "dtype": "BF16", "codec": "bf16_exp_chunked_v1",
                       "special": None, "compressed_bytes": int(b.numel()), "offset": offs[name], "md5": "",
-                      "extra": gpu.xc_extras(ce, a.coder, gpu.DEFAULT_PREC)})
+                      "extra": gpu.xc_extras(ce, a.coder, a.prec)})
     header = {"format": "bf16", "mode": "balanced", "model_type": "llm", "base_model": None,
               "tensor_count": len(metas), "tensors": metas}
     image = ContainerImage(header, host, pin=True)
@@ -577,7 +581,7 @@ def bench_kv(a, torch, dev, world, rank, dist, local):
             del x
     ce = a.chunk_elems or gpu.DEFAULT_CHUNK_ELEMS
     n = kv[0].numel()
-    enc = gpu.XcEncoder(n, ce, a.coder, gpu.DEFAULT_PREC, device=local)
+    enc = gpu.XcEncoder(n, ce, a.coder, a.prec, device=local)
     bound = gpu.encode_bound(n, ce)
     outs = [torch.empty(bound, dtype=torch.uint8, device=dev) for _ in kv]
     lens = torch.zeros(len(kv), 2, dtype=torch.int64, device=dev)
@@ -792,11 +796,11 @@ def bench_stream(a, torch, dev, world, rank, dist, local):
     t0 = time.time()
     w = synthetic.random_weights(cfg, seed=0, device=dev)
     ce = a.chunk_elems or gpu.DEFAULT_CHUNK_ELEMS
-    enc = gpu.XcEncoder(max(t.numel() for t in w.values()), ce, a.coder, gpu.DEFAULT_PREC, device=local)
+    enc = gpu.XcEncoder(max(t.numel() for t in w.values()), ce, a.coder, a.prec, device=local)
     wr = ContainerWriter()
     for n, t in w.items():
         wr.add(n, t.shape, "BF16", "bf16_exp_chunked_v1", enc.encode(t.reshape(-1)).cpu().numpy().tobytes(), "",
-               gpu.xc_extras(ce, a.coder, gpu.DEFAULT_PREC))
+               gpu.xc_extras(ce, a.coder, a.prec))
     del enc
     image = ContainerImage.from_bytes(wr.to_bytes())
     del wr
