@@ -254,6 +254,7 @@ def main():
     ap.add_argument("--chunk-elems", type=int, default=None)
     ap.add_argument("--coder", default="pair", choices=["rans", "tans", "pair"])
     ap.add_argument("--prec", type=int, default=None, help="log2 of the coder's table size (default: the library's)")
+    ap.add_argument("--max-ctas", type=int, default=0, help="cap the decode grid (0: one CTA per work item)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-replicate", action="store_true",
                     help="N>1: skip the separately reported NCCL materialisation of the full model on every GPU")
@@ -441,7 +442,7 @@ def main():
         _, d, nb = loader.layout[name]
         entries.append((loader.dev_data[d:d + nb], loader.out[name].reshape(-1).view(torch.int16), ce,
                         math.prod(m["shape"]), c0, cc))
-    plan = gpu.XcPlan(entries, device=local, coders=a.coder)
+    plan = gpu.XcPlan(entries, device=local, coders=a.coder, max_ctas=a.max_ctas)
     for _ in range(a.warmup):
         plan.decode(stream)
     plan.check(stream)

@@ -626,16 +626,21 @@ __global__ void __launch_bounds__(kThreads, kPairMinBlocks) xc_decode_pair_kerne
     extern __shared__ __align__(16) uint8_t smem[];
     uint8_t *s_ring = smem + kPairTableBytes;
     const uint32_t warp = threadIdx.x >> 5;
+    uint32_t staged = 0xFFFFFFFFu;   // tensor whose table is in shared memory
     for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
         const XcItem it = items[item];
         const XcTensorDev &T = tens[it.tensor];
         if (T.coder != 2) continue;   // other coders: xc_decode_kernel; flagged tensors: skipped
         const uint32_t P = T.prec;
         const uint32_t M = 1u << P;
-        const uint4 *src = reinterpret_cast<const uint4 *>(tables + static_cast<uint64_t>(it.tensor) * kXcTableWords);
-        __syncthreads();   // the previous item's warps are done with the table
-        for (uint32_t i = threadIdx.x; i < M / 2; i += kThreads) reinterpret_cast<uint4 *>(smem)[i] = src[i];
-        __syncthreads();
+        if (it.tensor != staged) {    // a capped grid often walks several items of one tensor
+            const uint4 *src =
+                reinterpret_cast<const uint4 *>(tables + static_cast<uint64_t>(it.tensor) * kXcTableWords);
+            __syncthreads();   // the previous item's warps are done with the table
+            for (uint32_t i = threadIdx.x; i < M / 2; i += kThreads) reinterpret_cast<uint4 *>(smem)[i] = src[i];
+            __syncthreads();
+            staged = it.tensor;
+        }
         if (warp >= it.n_chunks) continue;
         const uint32_t c = it.first_chunk + warp;
         const uint8_t *blob = T.blob;
@@ -659,6 +664,7 @@ __global__ void __launch_bounds__(kThreads) xc_decode_kernel(const XcTensorDev *
     uint32_t *s_tab = reinterpret_cast<uint32_t *>(smem);
     uint8_t *s_ring = smem + kXcMaxTable * 4;
     const uint32_t warp = threadIdx.x >> 5;
+    uint32_t staged = 0xFFFFFFFFu;   // tensor whose table is in shared memory
     for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
         const XcItem it = items[item];
         const XcTensorDev &T = tens[it.tensor];
@@ -666,10 +672,14 @@ __global__ void __launch_bounds__(kThreads) xc_decode_kernel(const XcTensorDev *
         if (coder > 1) continue;   // the table build flagged this tensor, or the pair kernel's
         const uint32_t P = T.prec;
         const uint32_t M = 1u << P;
-        const uint4 *src = reinterpret_cast<const uint4 *>(tables + static_cast<uint64_t>(it.tensor) * kXcTableWords);
-        __syncthreads();   // the previous item's warps are done with the table
-        for (uint32_t i = threadIdx.x; i < M / 4; i += kThreads) reinterpret_cast<uint4 *>(s_tab)[i] = src[i];
-        __syncthreads();
+        if (it.tensor != staged) {    // a capped grid often walks several items of one tensor
+            const uint4 *src =
+                reinterpret_cast<const uint4 *>(tables + static_cast<uint64_t>(it.tensor) * kXcTableWords);
+            __syncthreads();   // the previous item's warps are done with the table
+            for (uint32_t i = threadIdx.x; i < M / 4; i += kThreads) reinterpret_cast<uint4 *>(s_tab)[i] = src[i];
+            __syncthreads();
+            staged = it.tensor;
+        }
         if (warp >= it.n_chunks) continue;
         const uint32_t c = it.first_chunk + warp;
         const uint8_t *blob = T.blob;
