@@ -45,9 +45,13 @@ for _name in se_legacy.CODECS:
     register_codec(_name, se_legacy.encode, se_legacy.decoder_for(_name))
 
 
-def install_into(reference_registry) -> None:
-    """Register this package's codecs in a reference codec_registry module."""
+def install_into(reference_registry, legacy: bool = False) -> None:
+    """Register this package's codecs in a reference codec_registry module.
+    The legacy serial formats are registered (device decode, the reference's
+    encoder kept) only with ``legacy``."""
     for name, (enc, dec) in _REGISTRY.items():
+        if name in se_legacy.CODECS and not legacy:
+            continue
         if (name == bf16_parallel.CODEC or name in se_legacy.CODECS) and reference_registry.get_codec(name) is not None:
             enc = reference_registry.get_codec(name)[0]   # keep the reference encoder
         reference_registry.register_codec(name, enc, dec)

@@ -24,13 +24,20 @@ from . import decoder as _dec
 from .kernels import ac_cuda as _ac_cuda
 
 DEVICE_CODECS = ("bf16_exp_chunked_v1", "bf16_parallel_v1")
+# the reference's serial formats; their device decode is bit-exact but one
+# serial stream per tensor, slower than the reference's CPU decoder per tensor
+LEGACY_CODECS = ("bf16_se_single_kernel", "bf16_se_tans")
 
 
-def install(bigsmall_pkg) -> dict:
+def install(bigsmall_pkg, legacy_on_device: bool = False) -> dict:
     """Wire the device engine into an imported reference package.  Returns the
-    original callables so :func:`uninstall` can restore them."""
+    original callables so :func:`uninstall` can restore them.  With
+    ``legacy_on_device`` the legacy serial formats decode on the device too
+    (no CPU work; useful when host cores are busy); otherwise they keep the
+    reference's CPU decoders."""
     name = bigsmall_pkg.__name__
     saved = {}
+    device_codecs = DEVICE_CODECS + (LEGACY_CODECS if legacy_on_device else ())
     # 1. backend slot
     kern = sys.modules.get(f"{name}.kernels") or getattr(bigsmall_pkg, "kernels", None)
     sys.modules[f"{name}.kernels.ac_cuda"] = _ac_cuda
@@ -46,7 +53,7 @@ def install(bigsmall_pkg) -> dict:
     saved["_decode_blob"] = orig
 
     def _decode_blob(t, blob):
-        if t.get("codec") in DEVICE_CODECS:
+        if t.get("codec") in device_codecs:
             return _dec._decode_blob(t, blob)
         return orig(t, blob)
 
@@ -60,7 +67,7 @@ def install(bigsmall_pkg) -> dict:
     # 3. registry
     reg = sys.modules.get(f"{name}.codec_registry") or getattr(bigsmall_pkg, "codec_registry", None)
     if reg is not None:
-        _reg.install_into(reg)
+        _reg.install_into(reg, legacy=legacy_on_device)
     return saved
 
 

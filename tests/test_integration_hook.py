@@ -67,3 +67,31 @@ def test_install_and_uninstall(monkeypatch):
         for n in [m for m in sys.modules if m.startswith("fakebs")]:
             del sys.modules[n]
     assert "fakebs.kernels.ac_cuda" not in sys.modules
+
+
+@pytest.mark.parametrize("legacy_on_device", [False, True])
+def test_legacy_formats_stay_on_the_reference_cpu_unless_asked(monkeypatch, legacy_on_device):
+    from bigsmall_b200 import integration
+    from bigsmall_b200 import decoder as gdec
+    pkg = _fake_reference()
+    pkg.codec_registry.register_codec("bf16_se_single_kernel", "ref-sk-enc", "ref-sk-dec")
+    orig = pkg.decoder._decode_blob
+
+    def ref_decode(t, blob):
+        if t["codec"] == "bf16_se_single_kernel":
+            return b"cpu"
+        return orig(t, blob)
+
+    pkg.decoder._decode_blob = ref_decode
+    monkeypatch.setattr(gdec, "_decode_blob", lambda t, b: b"device")
+    saved = integration.install(pkg, legacy_on_device=legacy_on_device)
+    try:
+        got = pkg.decoder._decode_blob({"codec": "bf16_se_single_kernel"}, b"x")
+        assert got == (b"device" if legacy_on_device else b"cpu")
+        enc, dec = pkg.codec_registry.get_codec("bf16_se_single_kernel")
+        assert enc == "ref-sk-enc"
+        assert (dec != "ref-sk-dec") == legacy_on_device
+    finally:
+        integration.uninstall(pkg, saved)
+        for n in [m for m in sys.modules if m.startswith("fakebs")]:
+            del sys.modules[n]
