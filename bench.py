@@ -448,14 +448,17 @@ def main():
     plan.check(stream)
     barrier()
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    # per step, events around the decode kernels alone (after the table build)
+    kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(a.steps)]
     with ClockSampler(local) as clk:
         s.record(stream)
-        for _ in range(a.steps):
-            plan.decode(stream)
+        for k0, k1 in kev:
+            plan.decode_timed(k0, k1, stream)
         e.record(stream)
         torch.cuda.synchronize()
     plan.check(stream)
     local_ms = s.elapsed_time(e) / a.steps
+    kernel_ms = sum(k0.elapsed_time(k1) for k0, k1 in kev) / a.steps
     barrier()
     ms = max_over_ranks(local_ms)
 
@@ -506,7 +509,7 @@ def main():
     if rank == 0:
         peak, peak_kind = measured_peak()
         value = 2 * total_elems / (ms * 1e-3) / 1e9
-        achieved = algo_bytes / (local_ms * 1e-3) / 1e9
+        achieved = algo_bytes / (kernel_ms * 1e-3) / 1e9
         prof = profile_traffic(a.coder) if a.config == "c2" else None
         traffic = None
         if prof and prof.get("chunk_elems") == ce and world == 1:
@@ -519,8 +522,10 @@ def main():
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_source": f"hbm_gbs of {peak_kind}",
                          "traffic": traffic,
-                         "kernel": f"{'xc_decode_pair_kernel' if a.coder == 'pair' else 'xc_decode_kernel'} "
-                                   "(+ xc_prepare_kernel: one plan launch pair per step, timed together)",
+                         "kernel": f"{'xc_decode_pair_kernel' if a.coder == 'pair' else 'xc_decode_kernel'}",
+                         "kernel_ms": round(kernel_ms, 4),
+                         "timing": "CUDA events recorded on the launching stream around the decode kernel of "
+                                   "every timed step (the per-step table build, xc_prepare_kernel, is outside)",
                          "algorithmic_bytes_per_step": algo_bytes},
             "e2e": None if e2e_ms is None else {
                 "value": round(2 * total_elems / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",

@@ -71,6 +71,7 @@ SIGNATURES = {
     "bs_status_string": (ctypes.c_char_p, [_I]),
     "bs_xc_plan_create": (_I, [ctypes.POINTER(XcTensor), _I, _I, ctypes.POINTER(_P)]),
     "bs_plan_decode": (_I, [_P, _P]),
+    "bs_plan_decode_timed": (_I, [_P, _P, _P, _P]),
     "bs_plan_check": (_I, [_P, _P, ctypes.POINTER(_U32)]),
     "bs_plan_n_tensors": (_I, [_P]),
     "bs_plan_set_max_ctas": (_I, [_P, _I]),

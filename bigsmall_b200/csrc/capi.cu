@@ -272,33 +272,50 @@ int bs_xc_plan_create(const bs_xc_tensor *tensors, int n_tensors, int device, bs
     return BS_OK;
 }
 
-int bs_plan_decode(bs_plan *p, void *stream) {
+// The decode step of a plan; `ev_start` / `ev_stop` (cudaEvent_t, optional)
+// are recorded on the stream right before and after the decode kernels, after
+// the table build, so a caller can time the decode kernels alone.
+static int plan_decode(bs_plan *p, void *stream, void *ev_start, void *ev_stop) {
     if (!p) return fail(BS_E_INVALID_ARG, "plan is NULL");
     DeviceGuard guard(p->device);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     cudaError_t e = cudaSuccess;
+    auto mark = [&](void *ev) {
+        if (ev && e == cudaSuccess) e = cudaEventRecord(static_cast<cudaEvent_t>(ev), s);
+    };
     if (p->kind == kPlanXc) {
-        if (p->n_internal == 0) return BS_OK;
+        if (p->n_internal == 0) { mark(ev_start); mark(ev_stop); return e == cudaSuccess ? BS_OK : cuda_fail(e, "event"); }
         e = launch_xc_prepare(p->d_tens, p->n_internal, p->d_tables, p->d_errs, s);
+        mark(ev_start);
         if (e == cudaSuccess)
             e = launch_xc_decode(p->d_tens, p->d_items, p->n_items, p->d_tables, p->d_errs, p->coders,
                                  p->max_ctas, s);
+        mark(ev_stop);
     } else if (p->kind == kPlanPar) {
-        if (p->n_internal == 0) return BS_OK;
-        e = cudaMemsetAsync(p->d_errs, 0, 4ull * p->n_internal, s);
-        if (e == cudaSuccess)
-            e = launch_par_jobs(p->d_jobs, p->n_jobs, p->d_tabs, p->d_syms, p->d_se_sym, p->d_mant, p->d_errs, s);
-        if (e == cudaSuccess)
-            e = launch_par_merge(p->d_streams, p->n_streams_total, p->d_buckets, p->d_se_sym, p->d_mant,
-                                 p->d_errs, s);
-        if (e == cudaSuccess)
-            e = launch_seg_merge(p->d_ss, p->n_ss, p->d_seg_stream, p->n_segs, p->d_hist, p->d_buckets,
-                                 p->d_se_sym, p->d_mant, p->d_errs, s);
+        mark(ev_start);
+        if (p->n_internal > 0) {
+            if (e == cudaSuccess) e = cudaMemsetAsync(p->d_errs, 0, 4ull * p->n_internal, s);
+            if (e == cudaSuccess)
+                e = launch_par_jobs(p->d_jobs, p->n_jobs, p->d_tabs, p->d_syms, p->d_se_sym, p->d_mant, p->d_errs, s);
+            if (e == cudaSuccess)
+                e = launch_par_merge(p->d_streams, p->n_streams_total, p->d_buckets, p->d_se_sym, p->d_mant,
+                                     p->d_errs, s);
+            if (e == cudaSuccess)
+                e = launch_seg_merge(p->d_ss, p->n_ss, p->d_seg_stream, p->n_segs, p->d_hist, p->d_buckets,
+                                     p->d_se_sym, p->d_mant, p->d_errs, s);
+        }
+        mark(ev_stop);
     } else {
         return fail(BS_E_INVALID_ARG, "unknown plan kind");
     }
     if (e != cudaSuccess) return cuda_fail(e, "decode launch");
     return BS_OK;
+}
+
+int bs_plan_decode(bs_plan *p, void *stream) { return plan_decode(p, stream, nullptr, nullptr); }
+
+int bs_plan_decode_timed(bs_plan *p, void *stream, void *ev_start, void *ev_stop) {
+    return plan_decode(p, stream, ev_start, ev_stop);
 }
 
 int bs_plan_check(bs_plan *p, void *stream, uint32_t *status_out) {

@@ -60,6 +60,19 @@ class _Plan:
         L = _lib.load()
         _lib.check(L.bs_plan_decode(self._h, _stream_ptr(stream, self.device)), "bs_plan_decode")
 
+    def decode_timed(self, start: torch.cuda.Event, stop: torch.cuda.Event,
+                     stream: Optional[torch.cuda.Stream] = None) -> None:
+        """``decode`` with ``start`` / ``stop`` (timing events) recorded right
+        before and after the decode kernels, so ``start.elapsed_time(stop)``
+        is the decode kernels' time alone (without the per-launch table build)."""
+        s = stream if stream is not None else torch.cuda.current_stream(self.device)
+        for ev in (start, stop):
+            if not ev.cuda_event:          # torch creates the event on first record
+                ev.record(s)
+        L = _lib.load()
+        _lib.check(L.bs_plan_decode_timed(self._h, _stream_ptr(s, self.device), ctypes.c_void_p(start.cuda_event),
+                                          ctypes.c_void_p(stop.cuda_event)), "bs_plan_decode_timed")
+
     def check(self, stream: Optional[torch.cuda.Stream] = None) -> list[int]:
         """Synchronise `stream` and raise BsCorruptError if any tensor failed."""
         L = _lib.load()

@@ -93,6 +93,11 @@ int bs_xc_plan_create(const bs_xc_tensor *tensors, int n_tensors, int device,
  * Asynchronous; stream-ordered; launches a table-build kernel and the decode
  * kernel.  The plan may be decoded any number of times. */
 int bs_plan_decode(bs_plan *plan, void *stream);
+/* bs_plan_decode that also records two cudaEvent_t (may be NULL) on the
+ * stream right before and right after the decode kernels (after the
+ * per-launch table build), so the caller can time the decode kernels alone
+ * with cudaEventElapsedTime.  No reference counterpart. */
+int bs_plan_decode_timed(bs_plan *plan, void *stream, void *ev_start, void *ev_stop);
 
 /* Synchronise `stream`, read the per-tensor device status words into
  * `status_out` (may be NULL; else n_tensors entries) and return BS_OK or

@@ -184,3 +184,19 @@ def test_capped_grid_walks_the_whole_work_list(max_ctas):
         plan.run()
         for raw, o in zip(raws, outs):
             assert o.cpu().view(torch.uint8).numpy().tobytes() == raw
+
+
+def test_decode_timed_records_events_around_the_decode_kernels():
+    from bigsmall_b200 import gpu
+    n = 1_000_003
+    raw = _normal(n, 77)
+    out = torch.empty(n, dtype=torch.bfloat16, device="cuda")
+    with gpu.XcPlan([(_dev(O.xc_encode(raw, 2, 12, 65536)), out, 65536)], coders="pair") as p:
+        k0, k1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s0.record()
+        p.decode_timed(k0, k1)
+        s1.record()
+        p.check()
+        assert 0 < k0.elapsed_time(k1) <= s0.elapsed_time(s1)
+    assert out.cpu().view(torch.uint8).numpy().tobytes() == raw
