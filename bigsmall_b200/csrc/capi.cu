@@ -318,6 +318,23 @@ int bs_plan_decode_timed(bs_plan *p, void *stream, void *ev_start, void *ev_stop
     return plan_decode(p, stream, ev_start, ev_stop);
 }
 
+int bs_plan_decode_after(bs_plan *p, void *stream, void *wait_event, void *done_event) {
+    if (!p) return fail(BS_E_INVALID_ARG, "plan is NULL");
+    DeviceGuard guard(p->device);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (wait_event) {
+        const cudaError_t e = cudaStreamWaitEvent(s, static_cast<cudaEvent_t>(wait_event), 0);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaStreamWaitEvent");
+    }
+    const int rc = plan_decode(p, stream, nullptr, nullptr);
+    if (rc) return rc;
+    if (done_event) {
+        const cudaError_t e = cudaEventRecord(static_cast<cudaEvent_t>(done_event), s);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaEventRecord");
+    }
+    return BS_OK;
+}
+
 int bs_plan_check(bs_plan *p, void *stream, uint32_t *status_out) {
     if (!p) return fail(BS_E_INVALID_ARG, "plan is NULL");
     DeviceGuard guard(p->device);

@@ -73,6 +73,16 @@ class _Plan:
         _lib.check(L.bs_plan_decode_timed(self._h, _stream_ptr(s, self.device), ctypes.c_void_p(start.cuda_event),
                                           ctypes.c_void_p(stop.cuda_event)), "bs_plan_decode_timed")
 
+    def decode_after(self, stream: torch.cuda.Stream, wait: Optional[torch.cuda.Event] = None,
+                     done: Optional[torch.cuda.Event] = None) -> None:
+        """``stream`` waits for ``wait``, decodes, then records ``done``: one
+        library call (events must have been recorded once, which creates them)."""
+        L = _lib.load()
+        _lib.check(L.bs_plan_decode_after(self._h, _stream_ptr(stream, self.device),
+                                          ctypes.c_void_p(wait.cuda_event) if wait is not None else None,
+                                          ctypes.c_void_p(done.cuda_event) if done is not None else None),
+                   "bs_plan_decode_after")
+
     def check(self, stream: Optional[torch.cuda.Stream] = None) -> list[int]:
         """Synchronise `stream` and raise BsCorruptError if any tensor failed."""
         L = _lib.load()

@@ -310,6 +310,18 @@ class Bundle:
         self.plans = plans
         self.copies = copies
 
+    def decode_after(self, stream: torch.cuda.Stream, wait=None, done=None) -> None:
+        """``stream`` waits for event ``wait``, decodes, records ``done``; a
+        bundle of one plan and no copies does this in one library call."""
+        if len(self.plans) == 1 and not self.copies:
+            self.plans[0].decode_after(stream, wait, done)
+            return
+        if wait is not None:
+            stream.wait_event(wait)
+        self.decode(stream)
+        if done is not None:
+            done.record(stream)
+
     def decode(self, stream: Optional[torch.cuda.Stream] = None) -> None:
         for pl in self.plans:
             pl.decode(stream)

@@ -137,6 +137,8 @@ class BigSmallStreamingModel:
         self.compute_stream = torch.cuda.Stream(self.device, priority=hi) if priority_compute else None
         self._decoded = [torch.cuda.Event() for _ in range(self.n_slots)]
         self._released = [torch.cuda.Event() for _ in range(self.n_slots)]
+        for ev in self._decoded + self._released:   # create the CUDA events now
+            ev.record(torch.cuda.current_stream(self.device))
         self._k = 0                 # global layer-execution counter (selects the slot)
         self._expect = 0            # layer expected to run next
         self._primed = False
@@ -191,9 +193,9 @@ class BigSmallStreamingModel:
             out = original(*args, **kwargs)
             outer._released[slot].record(main)
             nxt = (layer_idx + outer.n_slots) % outer.n_layers
-            outer._side.wait_event(outer._released[slot])
-            outer._bundles[(nxt, slot)].decode(outer._side)
-            outer._decoded[slot].record(outer._side)
+            # side stream: wait for "slot released", decode layer nxt into it,
+            # record "slot decoded" -- one library call for an all-xc bundle
+            outer._bundles[(nxt, slot)].decode_after(outer._side, outer._released[slot], outer._decoded[slot])
             outer._k += 1
             outer._expect = (layer_idx + 1) % outer.n_layers
             return out

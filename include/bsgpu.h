@@ -98,6 +98,11 @@ int bs_plan_decode(bs_plan *plan, void *stream);
  * per-launch table build), so the caller can time the decode kernels alone
  * with cudaEventElapsedTime.  No reference counterpart. */
 int bs_plan_decode_timed(bs_plan *plan, void *stream, void *ev_start, void *ev_stop);
+/* One call for an event-chained decode on a side stream: the stream waits for
+ * `wait_event` (cudaEvent_t, may be NULL), the plan decodes, then `done_event`
+ * (may be NULL) is recorded.  Used by the streaming model's per-layer prefetch
+ * to keep host work per layer to one call.  No reference counterpart. */
+int bs_plan_decode_after(bs_plan *plan, void *stream, void *wait_event, void *done_event);
 
 /* Synchronise `stream`, read the per-tensor device status words into
  * `status_out` (may be NULL; else n_tensors entries) and return BS_OK or
