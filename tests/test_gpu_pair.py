@@ -200,3 +200,21 @@ def test_decode_timed_records_events_around_the_decode_kernels():
         p.check()
         assert 0 < k0.elapsed_time(k1) <= s0.elapsed_time(s1)
     assert out.cpu().view(torch.uint8).numpy().tobytes() == raw
+
+
+@pytest.mark.parametrize("coder,name", [(0, "rans"), (1, "tans"), (2, "pair")])
+@pytest.mark.parametrize("prec", [8, 10, 12])
+def test_special_distributions_decode_and_device_encoder(coder, name, prec):
+    """All-zero, NaN/Inf, subnormal, top-exponent (window base 241) and
+    two-cluster tensors: device decode of oracle blobs and device encode,
+    both bit-exact, at the format's small and default precisions."""
+    from bigsmall_b200 import gpu
+    from tests.test_oracle_xc import _special
+    for kind in ("zeros", "nan_inf", "subnormal", "top_exponents", "two_clusters"):
+        for n in (1, 300, 70_001):
+            raw = _special(kind, n)
+            blob = O.xc_encode(raw, coder, prec, 4096)
+            assert _decode(blob, n, 4096) == raw, (kind, name, prec, n)
+            x = torch.from_numpy(np.frombuffer(raw, dtype=np.int16).copy()).view(torch.bfloat16).cuda()
+            d = gpu.encode_xc(x, coder=name, prec=prec, chunk_elems=4096).cpu().numpy().tobytes()
+            assert d == blob, (kind, name, prec, n)

@@ -136,3 +136,30 @@ def test_xc_pair_coder_bad_escape_count_detected():
     struct.pack_into("<I", bad, 28, 300)                  # window base out of range
     with pytest.raises(O.OracleError):
         O.xc_decode(bytes(bad), 20000)
+
+
+def _special(kind: str, n: int) -> bytes:
+    rng = np.random.default_rng(n)
+    if kind == "zeros":
+        w = np.zeros(n, np.uint16)
+    elif kind == "nan_inf":
+        w = rng.choice(np.array([0x7F80, 0xFF80, 0x7FC0, 0xFFFF, 0x7F81], np.uint16), n)
+    elif kind == "subnormal":
+        w = (rng.integers(0, 0x80, n) | (rng.integers(0, 2, n) << 15)).astype(np.uint16)
+    elif kind == "top_exponents":      # exponents 240..255: window base at its maximum (241)
+        e = rng.integers(240, 256, n)
+        w = ((rng.integers(0, 2, n) << 15) | (e << 7) | rng.integers(0, 128, n)).astype(np.uint16)
+    else:                              # two far-apart exponent clusters: many escapes
+        e = np.where(rng.random(n) < 0.5, rng.integers(1, 8, n), rng.integers(200, 230, n))
+        w = ((e << 7) | rng.integers(0, 128, n)).astype(np.uint16)
+    return w.tobytes()
+
+
+@pytest.mark.parametrize("kind", ["zeros", "nan_inf", "subnormal", "top_exponents", "two_clusters"])
+@pytest.mark.parametrize("coder", [0, 1, 2])
+@pytest.mark.parametrize("prec", [8, 10, 12])
+def test_xc_special_value_distributions(kind, coder, prec):
+    for n in (1, 300, 70_001):
+        raw = _special(kind, n)
+        blob = O.xc_encode(raw, coder, prec, 4096)
+        assert O.xc_decode(blob, n) == raw, (kind, coder, prec, n)
