@@ -76,3 +76,10 @@ def test_bench_partition_covers_container_once(world):
             assert c0 == pos
             pos = c0 + (cc or nc)
         assert pos == nc
+
+
+def test_top_level_names_follow_the_reference():
+    import bigsmall_b200 as b
+    for name in ("decompress", "load", "verify", "info", "StreamingLoader", "BigSmallStreamingModel",
+                 "CompressedKVCache", "BigSmallVersionError"):
+        assert callable(getattr(b, name)), name
