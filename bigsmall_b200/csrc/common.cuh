@@ -82,7 +82,7 @@ __host__ __device__ inline uint32_t rcp_div(uint32_t n, uint32_t m, uint32_t sh1
     return (t + ((n - t) >> sh1)) >> sh2;
 }
 
-// A work item: up to kXcWarps consecutive chunks of one tensor, one CTA.
+// A work item: up to 16 consecutive chunks of one tensor (xc_warps_per_cta), one CTA.
 struct XcItem {
     uint32_t tensor;
     uint32_t first_chunk;

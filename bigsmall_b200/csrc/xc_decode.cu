@@ -20,7 +20,7 @@
 //   xc_prepare_kernel  one CTA per tensor: validates the blob header against the
 //                      plan descriptor, builds the 2^P-entry decode table into
 //                      the plan's workspace and checks the chunk offset table.
-//   xc_decode_kernel   one CTA per work item (<= 8 chunks of one tensor): copies
+//   xc_decode_kernel   one CTA per work item (<= 16 chunks of one tensor): copies
 //                      the table into shared memory, then each warp decodes one
 //                      chunk.  Compressed words are staged per warp in a 2 KiB
 //                      shared-memory ring (plus a 1 KiB mirror of its head)
@@ -35,8 +35,14 @@
 
 namespace bsg {
 
-constexpr int kWarps = 8;                   // warps (= chunks) per CTA
+// A work item is up to kWarps chunks of one tensor; the pair kernel runs one
+// warp per chunk (16 warps share one staged 32 KiB table); the rANS/tANS
+// kernel runs two CTAs of kRansWarps warps per item, one per half.
+constexpr int kWarps = 16;                  // chunks per work item = warps per pair-kernel CTA
 constexpr int kThreads = kWarps * 32;
+constexpr int kRansWarps = 8;               // warps per rANS/tANS CTA
+constexpr int kRansThreads = kRansWarps * 32;
+constexpr int kRansMinBlocks = 5;           // 5 x 8 warps per SM: registers capped at 48
 constexpr uint32_t kRingBytes = 2048;       // per-warp staging ring
 constexpr uint32_t kFill = 512;             // bytes per refill: 32 lanes x 16 B
 
@@ -447,7 +453,7 @@ constexpr uint32_t kPairRingBytes = 2048;                // per-warp staging rin
 constexpr uint32_t kPairMirror = kFill;                 // 8 pair-steps consume <= 512 B
 constexpr uint32_t kPairWarpRing = kPairRingBytes + kPairMirror;
 constexpr uint32_t kPairTableBytes = 8 * kXcMaxTable;
-constexpr int kPairMinBlocks = 4;                        // CTAs per SM the registers must allow
+constexpr int kPairMinBlocks = 2;                        // CTAs (of kThreads) per SM the registers must allow
 
 __device__ __forceinline__ uint2 lds_u64(uint32_t a) {
     uint2 v;
@@ -656,7 +662,7 @@ __global__ void __launch_bounds__(kThreads, kPairMinBlocks) xc_decode_pair_kerne
     }
 }
 
-__global__ void __launch_bounds__(kThreads) xc_decode_kernel(const XcTensorDev *__restrict__ tens,
+__global__ void __launch_bounds__(kRansThreads, kRansMinBlocks) xc_decode_kernel(const XcTensorDev *__restrict__ tens,
                                                              const XcItem *__restrict__ items, int n_items,
                                                              const uint32_t *__restrict__ tables,
                                                              uint32_t *errs) {
@@ -665,8 +671,9 @@ __global__ void __launch_bounds__(kThreads) xc_decode_kernel(const XcTensorDev *
     uint8_t *s_ring = smem + kXcMaxTable * 4;
     const uint32_t warp = threadIdx.x >> 5;
     uint32_t staged = 0xFFFFFFFFu;   // tensor whose table is in shared memory
-    for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
-        const XcItem it = items[item];
+    for (int half = blockIdx.x; half < 2 * n_items; half += gridDim.x) {
+        const XcItem it = items[half >> 1];
+        const uint32_t k = (half & 1) * kRansWarps + warp;   // this warp's chunk within the item
         const XcTensorDev &T = tens[it.tensor];
         const uint32_t coder = T.coder;
         if (coder > 1) continue;   // the table build flagged this tensor, or the pair kernel's
@@ -676,12 +683,12 @@ __global__ void __launch_bounds__(kThreads) xc_decode_kernel(const XcTensorDev *
             const uint4 *src =
                 reinterpret_cast<const uint4 *>(tables + static_cast<uint64_t>(it.tensor) * kXcTableWords);
             __syncthreads();   // the previous item's warps are done with the table
-            for (uint32_t i = threadIdx.x; i < M / 4; i += kThreads) reinterpret_cast<uint4 *>(s_tab)[i] = src[i];
+            for (uint32_t i = threadIdx.x; i < M / 4; i += kRansThreads) reinterpret_cast<uint4 *>(s_tab)[i] = src[i];
             __syncthreads();
             staged = it.tensor;
         }
-        if (warp >= it.n_chunks) continue;
-        const uint32_t c = it.first_chunk + warp;
+        if (k >= it.n_chunks) continue;
+        const uint32_t c = it.first_chunk + k;
         const uint8_t *blob = T.blob;
         const uint32_t *cs = reinterpret_cast<const uint32_t *>(blob + kXcTabOff);
         const uint32_t a = cs[c], z = cs[c + 1];
@@ -738,10 +745,12 @@ cudaError_t launch_xc_decode(const XcTensorDev *d_tens, const XcItem *d_items, i
     const int grid = max_ctas > 0 && max_ctas < n_items ? max_ctas : n_items;
     cudaError_t e = cudaSuccess;
     if (coders & ((1u << BS_CODER_RANS) | (1u << BS_CODER_TANS))) {
-        const size_t smem = kXcMaxTable * 4 + kWarps * kWarpRing;
+        const size_t smem = kXcMaxTable * 4 + kRansWarps * kWarpRing;
         e = smem_opt_in(xc_decode_kernel, smem, g_attr_rans);
         if (e != cudaSuccess) return e;
-        xc_decode_kernel<<<grid, kThreads, smem, s>>>(d_tens, d_items, n_items, d_tables, d_errs);
+        // two CTAs per item (one per half of its chunks); a cap counts pair-kernel-sized CTAs
+        const int rgrid = 2 * grid;
+        xc_decode_kernel<<<rgrid, kRansThreads, smem, s>>>(d_tens, d_items, n_items, d_tables, d_errs);
         e = cudaGetLastError();
         if (e != cudaSuccess) return e;
     }
@@ -787,26 +796,27 @@ __global__ void xc_noalloc_stage_kernel(const NoallocArgs a, XcTensorDev *tens) 
     if (t < a.n) tens[t] = a.tens[t];
 }
 
-__global__ void __launch_bounds__(kThreads) xc_decode_noalloc_kernel(const NoallocArgs a,
+__global__ void __launch_bounds__(kRansThreads, kRansMinBlocks) xc_decode_noalloc_kernel(const NoallocArgs a,
                                                                      const XcTensorDev *__restrict__ tens,
                                                                      const uint32_t *__restrict__ tables,
                                                                      uint32_t *errs) {
     extern __shared__ __align__(16) uint8_t smem[];
     uint32_t *s_tab = reinterpret_cast<uint32_t *>(smem);
     uint8_t *s_ring = smem + kXcMaxTable * 4;
+    const uint32_t unit = blockIdx.x >> 1;   // two CTAs (halves) per kWarps-chunk unit
     int ti = 0;
-    while (ti + 1 < a.n && blockIdx.x >= a.cta_prefix[ti + 1]) ti++;
+    while (ti + 1 < a.n && unit >= a.cta_prefix[ti + 1]) ti++;
     const XcTensorDev &T = tens[ti];
     const uint32_t coder = T.coder;
     if (coder > 1) return;   // xc_prepare_kernel flagged this tensor
     const uint32_t P = T.prec;
     const uint32_t M = 1u << P;
     const uint4 *src = reinterpret_cast<const uint4 *>(tables + static_cast<uint64_t>(ti) * kXcTableWords);
-    for (uint32_t i = threadIdx.x; i < M / 4; i += kThreads) reinterpret_cast<uint4 *>(s_tab)[i] = src[i];
+    for (uint32_t i = threadIdx.x; i < M / 4; i += kRansThreads) reinterpret_cast<uint4 *>(s_tab)[i] = src[i];
     __syncthreads();
     const uint32_t warp = threadIdx.x >> 5;
     const uint32_t c0 = a.tens[ti].chunk_begin;
-    const uint32_t c = c0 + (blockIdx.x - a.cta_prefix[ti]) * kWarps + warp;
+    const uint32_t c = c0 + (unit - a.cta_prefix[ti]) * kWarps + (blockIdx.x & 1) * kRansWarps + warp;
     if (c >= c0 + a.range_count[ti]) return;
     const uint8_t *blob = T.blob;
     const uint32_t *cs = reinterpret_cast<const uint32_t *>(blob + kXcTabOff);
@@ -901,8 +911,8 @@ cudaError_t launch_xc_noalloc(const XcTensorDev *h_tens, const uint32_t *range_c
     if (e == cudaSuccess) e = launch_xc_prepare(d_tens, n, d_tables, d_errs, s);
     const uint32_t coders = xc_launch_mask(h_tens, n);
     if (e == cudaSuccess && a.cta_prefix[n] > 0 && (coders & ((1u << BS_CODER_RANS) | (1u << BS_CODER_TANS)))) {
-        const size_t smem = kXcMaxTable * 4 + kWarps * kWarpRing;   // below the 48 KiB default
-        xc_decode_noalloc_kernel<<<a.cta_prefix[n], kThreads, smem, s>>>(a, d_tens, d_tables, d_errs);
+        const size_t smem = kXcMaxTable * 4 + kRansWarps * kWarpRing;   // below the 48 KiB default
+        xc_decode_noalloc_kernel<<<2 * a.cta_prefix[n], kRansThreads, smem, s>>>(a, d_tens, d_tables, d_errs);
         e = cudaGetLastError();
     }
     if (e == cudaSuccess && a.cta_prefix[n] > 0 && (coders & (1u << BS_CODER_RANS_PAIR))) {
