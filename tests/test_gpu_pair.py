@@ -60,7 +60,7 @@ def test_decode_golden_inputs(manifest):
 def test_decode_ragged_sizes(n):
     for make in (_normal, _wide, _uniform):
         raw = make(n, n)
-        for ce in (256, 65536):
+        for ce in (256, 32768, 65536):
             blob = O.xc_encode(raw, 2, 12, ce)
             assert _decode(blob, n, ce) == raw, (make.__name__, n, ce)
 
@@ -73,7 +73,7 @@ def test_device_encoder_matches_oracle_bytes(manifest):
     cases += [_uniform(70_001, 4)]
     for raw in cases:
         x = torch.from_numpy(np.frombuffer(raw, dtype=np.int16).copy()).view(torch.bfloat16).cuda()
-        for ce in (256, 65536):
+        for ce in (256, 32768, 65536):
             for prec in (11, 12):
                 d = gpu.encode_xc(x, coder="pair", prec=prec, chunk_elems=ce).cpu().numpy().tobytes()
                 assert d == O.xc_encode(raw, 2, prec, ce), (len(raw) // 2, ce, prec)
