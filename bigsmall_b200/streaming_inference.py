@@ -77,7 +77,7 @@ def _materialize_meta_buffers(model, config, device) -> None:
 class BigSmallStreamingModel:
     def __init__(self, bs_path, hf_config, device: str = "cuda", dtype=None,
                  layer_template: str = "model.layers.{}", prefetch: int = 1, slots: int = 2,
-                 model_cls=None, decode_ctas_per_sm: Optional[int] = 3, priority_compute: bool = True):
+                 model_cls=None, decode_ctas_per_sm: Optional[int] = 1, priority_compute: bool = True):
         from transformers import AutoConfig, AutoModelForCausalLM
         self.device = torch.device(device)
         if self.device.index is None:
@@ -119,8 +119,9 @@ class BigSmallStreamingModel:
         self._slots = [{k: self.loader.res.empty_like(self._local[0][k]) for k in sorted(keys0)}
                        for _ in range(self.n_slots)]
         # one prebuilt decode bundle per (layer, slot); the side-stream decode
-        # is capped at decode_ctas_per_sm CTAs per SM so that the layer running
-        # on the main stream keeps SM room (None: uncapped)
+        # is capped at decode_ctas_per_sm CTAs per SM (a decode CTA is 16 warps,
+        # half an SM's resident decode warps) so that the layer running on the
+        # main stream keeps SM room (None: uncapped)
         sms = torch.cuda.get_device_properties(self.device).multi_processor_count
         self.decode_max_ctas = sms * decode_ctas_per_sm if decode_ctas_per_sm else 0
         self._bundles = {}
