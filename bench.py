@@ -258,7 +258,7 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-replicate", action="store_true",
                     help="N>1: skip the separately reported NCCL materialisation of the full model on every GPU")
-    ap.add_argument("--stream-ctas", default="1",
+    ap.add_argument("--stream-ctas", default="0",
                     help="config 4: comma list of side-stream decode CTAs per SM to run (0 = uncapped)")
     ap.add_argument("--stream-priority", default="1",
                     help="config 4: comma list of 0/1: run the model on a high-priority stream (1) or not")

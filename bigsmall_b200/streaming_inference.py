@@ -11,10 +11,10 @@ Here:
   * the compressed container stays resident in HBM; non-layer tensors
     (embeddings, final norm, lm_head) are decoded once;
   * decoded layers live in ``slots`` (2) fixed device buffers allocated once;
-  * the side-stream decode runs on at most ``decode_ctas_per_sm`` CTAs per SM
-    (its kernels walk their work list), so the GEMMs of the running layer are
-    not queued behind a full-GPU decode grid, and ``forward``/``generate`` run
-    the model on a higher-priority stream than the decode;
+  * ``forward``/``generate`` run the model on a higher-priority stream than
+    the side-stream decode, so the block scheduler places the running layer's
+    CTAs first; the decode can also be capped at ``decode_ctas_per_sm`` CTAs
+    per SM (its kernels then walk their work list);
   * global layer execution k uses slot ``k % slots``.  After layer i runs on the
     main stream, the decode of the layer that runs ``slots`` executions later
     is enqueued on a side stream into the slot just released, ordered by CUDA
@@ -77,7 +77,7 @@ def _materialize_meta_buffers(model, config, device) -> None:
 class BigSmallStreamingModel:
     def __init__(self, bs_path, hf_config, device: str = "cuda", dtype=None,
                  layer_template: str = "model.layers.{}", prefetch: int = 1, slots: int = 2,
-                 model_cls=None, decode_ctas_per_sm: Optional[int] = 1, priority_compute: bool = True):
+                 model_cls=None, decode_ctas_per_sm: Optional[int] = None, priority_compute: bool = True):
         from transformers import AutoConfig, AutoModelForCausalLM
         self.device = torch.device(device)
         if self.device.index is None:
@@ -119,9 +119,9 @@ class BigSmallStreamingModel:
         self._slots = [{k: self.loader.res.empty_like(self._local[0][k]) for k in sorted(keys0)}
                        for _ in range(self.n_slots)]
         # one prebuilt decode bundle per (layer, slot); the side-stream decode
-        # is capped at decode_ctas_per_sm CTAs per SM (a decode CTA is 16 warps,
-        # half an SM's resident decode warps) so that the layer running on the
-        # main stream keeps SM room (None: uncapped)
+        # can be capped at decode_ctas_per_sm CTAs per SM (a decode CTA is 16
+        # warps, half an SM's resident decode warps) to leave the running layer
+        # SM room; uncapped measured best with 16-warp CTAs (None: uncapped)
         sms = torch.cuda.get_device_properties(self.device).multi_processor_count
         self.decode_max_ctas = sms * decode_ctas_per_sm if decode_ctas_per_sm else 0
         self._bundles = {}
