@@ -14,7 +14,6 @@ reference does for names it does not know; there is no CPU decoder here.
 from __future__ import annotations
 
 import hashlib
-from pathlib import Path
 from typing import Optional
 
 import numpy as np
