@@ -1,0 +1,65 @@
+"""Property tests of the bf16_exp_chunked_v1 format on the CPU oracle (the
+reference's property-test style, bigsmall tests/test_property_based.py:80-202,
+applied to this project's format): any bf16 tensor, any coder, precision and
+chunk size round-trips exactly, and the coded size stays within a small
+margin of the exponent entropy (the reference's ratio gates,
+tests/test_rans.py:52-62, restated for this format)."""
+from __future__ import annotations
+
+import math
+
+import numpy as np
+import pytest
+
+hyp = pytest.importorskip("hypothesis")
+from hypothesis import given, settings, strategies as st  # noqa: E402
+
+from oracle import oracle as O  # noqa: E402
+
+
+@st.composite
+def bf16_tensors(draw):
+    n = draw(st.integers(min_value=1, max_value=5000))
+    kind = draw(st.sampled_from(["normal", "uniform_words", "few_values", "wide"]))
+    seed = draw(st.integers(min_value=0, max_value=2 ** 31 - 1))
+    rng = np.random.default_rng(seed)
+    if kind == "normal":
+        w = (rng.standard_normal(n).astype(np.float32) * draw(st.sampled_from([1e-3, 0.02, 1.0, 300.0])))
+        words = (w.view(np.uint32) >> 16).astype(np.uint16)
+    elif kind == "uniform_words":
+        words = rng.integers(0, 1 << 16, n, dtype=np.uint16)
+    elif kind == "few_values":
+        words = rng.choice(rng.integers(0, 1 << 16, draw(st.integers(1, 4)), dtype=np.uint16), n)
+    else:
+        w = (rng.standard_normal(n) * np.exp(rng.standard_normal(n) * 4)).astype(np.float32)
+        words = (w.view(np.uint32) >> 16).astype(np.uint16)
+    return words.tobytes()
+
+
+@settings(max_examples=150, deadline=None)
+@given(raw=bf16_tensors(), coder=st.sampled_from([0, 1, 2]), prec=st.integers(8, 12),
+       chunk=st.sampled_from([256, 512, 4096, 32768]))
+def test_any_tensor_round_trips(raw, coder, prec, chunk):
+    blob = O.xc_encode(raw, coder, prec, chunk)
+    assert len(blob) % 16 == 0
+    assert O.xc_decode(blob, len(raw) // 2) == raw
+
+
+@pytest.mark.parametrize("coder", [0, 1, 2])
+def test_coded_size_close_to_exponent_entropy(coder):
+    """1M config-1-like values: the exponent stream costs at most 3 % more
+    than its empirical entropy (plus record headers and the raw plane)."""
+    n = 1 << 20
+    rng = np.random.default_rng(0)
+    x = rng.standard_normal(n).astype(np.float32) * 0.02
+    x[rng.permutation(n)[: n // 1000]] *= 30
+    words = (x.view(np.uint32) >> 16).astype(np.uint16)
+    e = (words >> 7) & 0xFF
+    p = np.bincount(e, minlength=256) / n
+    h = -sum(q * math.log2(q) for q in p if q > 0)          # bits per value
+    ce = 32768
+    blob = O.xc_encode(words.tobytes(), coder, 12, ce)
+    n_chunks = n // ce
+    framing = 576 + 4 * (n_chunks + 1) + n_chunks * (144 if coder == 2 else 128) + 16 * n_chunks
+    coded_bits = (len(blob) - n - framing) * 8
+    assert coded_bits <= 1.03 * h * n, (coder, coded_bits / n, h)
