@@ -244,10 +244,15 @@ __global__ void __launch_bounds__(256) xc_prepare_kernel(XcTensorDev *tens, uint
     // chunk offset table: monotone, >= 128 B per record, inside [chunks_off, total)
     const uint32_t *cs = reinterpret_cast<const uint32_t *>(b + kXcTabOff);
     const uint64_t lim16 = (s_total - s_chunks_off) >> 4;
+    // independent iterations: unrolled so a big tensor's table (16k+ chunks)
+    // keeps several loads in flight per thread
+    uint32_t bad = 0;
+#pragma unroll 8
     for (uint32_t c = tid; c < T.n_chunks; c += blockDim.x) {
-        uint32_t a = cs[c], z = cs[c + 1];
-        if (z < a + 8 || z > lim16) atomicOr(&s_err, BS_DEV_CHUNK_TABLE);
+        const uint32_t a = cs[c], z = cs[c + 1];
+        bad |= (z < a + 8 || z > lim16) ? 1u : 0u;
     }
+    if (bad) atomicOr(&s_err, BS_DEV_CHUNK_TABLE);
     __syncthreads();
     if (tid == 0) {
         errs[t] = s_err;
