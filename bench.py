@@ -255,6 +255,7 @@ def main():
     ap.add_argument("--coder", default="pair", choices=["rans", "tans", "pair"])
     ap.add_argument("--prec", type=int, default=None, help="log2 of the coder's table size (default: the library's)")
     ap.add_argument("--max-ctas", type=int, default=0, help="cap the decode grid (0: one CTA per work item)")
+    ap.add_argument("--group-mb", type=int, default=256, help="e2e: compressed bytes per host-to-device copy group")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-replicate", action="store_true",
                     help="N>1: skip the separately reported NCCL materialisation of the full model on every GPU")
@@ -385,7 +386,7 @@ def main():
         for parts in owned_all:
             rs = [part_range(*p) for p in parts]
             spans.append((min(r[0] for r in rs), max(r[1] for r in rs)) if rs else (0, 0))
-    loader = DeviceLoader(image, device=local, owned=owned, out=out_views)
+    loader = DeviceLoader(image, device=local, owned=owned, out=out_views, group_bytes=a.group_mb << 20)
     # elements / compressed bytes this rank decodes per step
     dec_elems, algo_bytes = 0, 0
     for name, c0, cc in owned:
