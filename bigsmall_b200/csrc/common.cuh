@@ -52,7 +52,7 @@ struct XcTensorDev {
     uint32_t coder;
     uint32_t prec;
     uint32_t coder_mask;      // from the caller: coders the blob may use (0: any)
-    uint32_t pad_;
+    uint32_t rec_lim16;       // end of the chunk-record area in 16-byte units from chunks_off
 };
 
 // Exact unsigned division by an invariant divisor (Granlund & Montgomery,

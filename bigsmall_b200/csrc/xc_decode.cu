@@ -97,9 +97,13 @@ __global__ void __launch_bounds__(256) xc_prepare_kernel(XcTensorDev *tens, uint
     __shared__ uint32_t s_next[256];
     __shared__ uint8_t s_spread[kXcMaxTable];
     const uint8_t *b = T.blob;
+    // the frequency table is loaded by every thread up front, its latency
+    // overlapping the header checks (the check below guarantees it is in bounds)
+    const bool hdr_in = T.blob_bytes >= kXcTabOff && !(reinterpret_cast<uintptr_t>(b) & 15);
+    const uint32_t f = hdr_in ? reinterpret_cast<const uint16_t *>(b + kXcFreqOff)[tid] : 0u;
     if (tid == 0) {
         uint32_t err = 0;
-        if (T.blob_bytes < kXcTabOff || (reinterpret_cast<uintptr_t>(b) & 15)) {
+        if (!hdr_in) {
             err = BS_DEV_HEADER;
         } else {
             const uint32_t *h32 = reinterpret_cast<const uint32_t *>(b);
@@ -136,8 +140,6 @@ __global__ void __launch_bounds__(256) xc_prepare_kernel(XcTensorDev *tens, uint
     }
     const uint32_t P = s_prec, M = 1u << P, coder = s_coder;
     // frequencies and their exclusive prefix sum
-    const uint16_t *fr = reinterpret_cast<const uint16_t *>(b + kXcFreqOff);
-    uint32_t f = fr[tid];
     s_freq[tid] = f;
     __syncthreads();
     if (tid < 32) {
@@ -241,27 +243,27 @@ __global__ void __launch_bounds__(256) xc_prepare_kernel(XcTensorDev *tens, uint
             }
         }
     }
-    // chunk offset table: monotone, >= 128 B per record, inside [chunks_off, total)
-    const uint32_t *cs = reinterpret_cast<const uint32_t *>(b + kXcTabOff);
-    const uint64_t lim16 = (s_total - s_chunks_off) >> 4;
-    // independent iterations: unrolled so a big tensor's table (16k+ chunks)
-    // keeps several loads in flight per thread
-    uint32_t bad = 0;
-#pragma unroll 8
-    for (uint32_t c = tid; c < T.n_chunks; c += blockDim.x) {
-        const uint32_t a = cs[c], z = cs[c + 1];
-        bad |= (z < a + 8 || z > lim16) ? 1u : 0u;
-    }
-    if (bad) atomicOr(&s_err, BS_DEV_CHUNK_TABLE);
-    __syncthreads();
+    // The chunk offset table is checked where it is read: each decoding warp
+    // checks its own chunk's two entries (checked_rec_bytes), so a plan that
+    // decodes part of a tensor reads only its part of the table.
     if (tid == 0) {
-        errs[t] = s_err;
-        T.coder = s_err ? 0xFFFFFFFFu : coder;
+        const uint64_t lim16 = (s_total - s_chunks_off) >> 4;
+        errs[t] = 0;
+        T.coder = coder;
         T.prec = P;
         T.chunks_off = s_chunks_off;
         T.plane_off = s_plane_off;
         T.aux = s_aux;
+        T.rec_lim16 = lim16 > 0xFFFFFFFFull ? 0xFFFFFFFFu : static_cast<uint32_t>(lim16);
     }
+}
+
+// Record bytes of a chunk whose offset table entries are [a, z) (16-byte
+// units from chunks_off), or 0 when the entries are not monotone with at least
+// 128 bytes (the lane states) per record ending inside the record area.  The
+// decode routines read nothing of a record whose size is 0.
+__device__ __forceinline__ uint32_t checked_rec_bytes(uint32_t a, uint32_t z, uint32_t lim16) {
+    return (z >= a && z - a >= 8 && z <= lim16) ? 16u * (z - a) : 0u;
 }
 
 // --------------------------------------------------------------------------
@@ -338,6 +340,10 @@ __device__ __forceinline__ void decode_chunk(const uint32_t *__restrict__ s_tab,
     const uint32_t lt = lanemask_lt();
     const uint32_t smask = (1u << P) - 1;
 
+    if (rec_bytes == 0) {   // bad chunk offset table entry
+        if (lane == 0) atomicOr(err, BS_DEV_CHUNK_TABLE);
+        return;
+    }
     const uint32_t ring_s = static_cast<uint32_t>(__cvta_generic_to_shared(ring_buf));
     const uint32_t tab_s = static_cast<uint32_t>(__cvta_generic_to_shared(s_tab));
     const uint32_t init = reinterpret_cast<const uint32_t *>(rec)[lane];
@@ -527,6 +533,10 @@ __device__ __forceinline__ void decode_chunk_pair(uint32_t tab_s, uint8_t *ring_
     const uint32_t lt = lanemask_lt();
     const uint32_t smask = (1u << P) - 1;
     const uint32_t ring_s = static_cast<uint32_t>(__cvta_generic_to_shared(ring_buf));
+    if (rec_bytes == 0) {   // bad chunk offset table entry
+        if (lane == 0) atomicOr(err, BS_DEV_CHUNK_TABLE);
+        return;
+    }
     const uint32_t *rec32 = reinterpret_cast<const uint32_t *>(rec);
     uint32_t x = rec32[lane];
     const uint32_t n_words = rec32[32], n_esc = rec32[33];
@@ -644,6 +654,17 @@ __global__ void __launch_bounds__(kThreads, kPairMinBlocks) xc_decode_pair_kerne
         if (T.coder != 2) continue;   // other coders: xc_decode_kernel; flagged tensors: skipped
         const uint32_t P = T.prec;
         const uint32_t M = 1u << P;
+        // this warp's chunk offsets, loaded before the table staging so the
+        // two loads' latency hides behind it
+        const bool mine = warp < it.n_chunks;
+        const uint32_t c = it.first_chunk + warp;
+        const uint8_t *blob = T.blob;
+        const uint32_t *cs = reinterpret_cast<const uint32_t *>(blob + kXcTabOff);
+        uint32_t a = 0, z = 0;
+        if (mine) {
+            a = cs[c];
+            z = cs[c + 1];
+        }
         if (it.tensor != staged) {    // a capped grid often walks several items of one tensor
             const uint4 *src =
                 reinterpret_cast<const uint4 *>(tables + static_cast<uint64_t>(it.tensor) * kXcTableWords);
@@ -652,16 +673,12 @@ __global__ void __launch_bounds__(kThreads, kPairMinBlocks) xc_decode_pair_kerne
             __syncthreads();
             staged = it.tensor;
         }
-        if (warp >= it.n_chunks) continue;
-        const uint32_t c = it.first_chunk + warp;
-        const uint8_t *blob = T.blob;
-        const uint32_t *cs = reinterpret_cast<const uint32_t *>(blob + kXcTabOff);
-        const uint32_t a = cs[c], z = cs[c + 1];
+        if (!mine) continue;
         const uint64_t e0 = static_cast<uint64_t>(c) * T.chunk_elems;
         const uint64_t left = T.n - e0;
         const uint32_t cn = left < T.chunk_elems ? static_cast<uint32_t>(left) : T.chunk_elems;
         decode_chunk_pair(static_cast<uint32_t>(__cvta_generic_to_shared(smem)), s_ring + warp * kPairWarpRing,
-                          blob + T.chunks_off + 16ull * a, 16u * (z - a), blob + T.plane_off + e0,
+                          blob + T.chunks_off + 16ull * a, checked_rec_bytes(a, z, T.rec_lim16), blob + T.plane_off + e0,
                           T.out + (e0 - static_cast<uint64_t>(T.chunk_begin) * T.chunk_elems), cn, P,
                           &errs[it.tensor]);
     }
@@ -684,6 +701,15 @@ __global__ void __launch_bounds__(kRansThreads, kRansMinBlocks) xc_decode_kernel
         if (coder > 1) continue;   // the table build flagged this tensor, or the pair kernel's
         const uint32_t P = T.prec;
         const uint32_t M = 1u << P;
+        const bool mine = k < it.n_chunks;   // chunk offsets loaded before the table staging
+        const uint32_t c = it.first_chunk + k;
+        const uint8_t *blob = T.blob;
+        const uint32_t *cs = reinterpret_cast<const uint32_t *>(blob + kXcTabOff);
+        uint32_t a = 0, z = 0;
+        if (mine) {
+            a = cs[c];
+            z = cs[c + 1];
+        }
         if (it.tensor != staged) {    // a capped grid often walks several items of one tensor
             const uint4 *src =
                 reinterpret_cast<const uint4 *>(tables + static_cast<uint64_t>(it.tensor) * kXcTableWords);
@@ -692,13 +718,9 @@ __global__ void __launch_bounds__(kRansThreads, kRansMinBlocks) xc_decode_kernel
             __syncthreads();
             staged = it.tensor;
         }
-        if (k >= it.n_chunks) continue;
-        const uint32_t c = it.first_chunk + k;
-        const uint8_t *blob = T.blob;
-        const uint32_t *cs = reinterpret_cast<const uint32_t *>(blob + kXcTabOff);
-        const uint32_t a = cs[c], z = cs[c + 1];
+        if (!mine) continue;
         const uint8_t *rec = blob + T.chunks_off + 16ull * a;
-        const uint32_t rec_bytes = 16u * (z - a);
+        const uint32_t rec_bytes = checked_rec_bytes(a, z, T.rec_lim16);
         const uint64_t e0 = static_cast<uint64_t>(c) * T.chunk_elems;
         const uint64_t left = T.n - e0;
         const uint32_t cn = left < T.chunk_elems ? static_cast<uint32_t>(left) : T.chunk_elems;
@@ -827,7 +849,7 @@ __global__ void __launch_bounds__(kRansThreads, kRansMinBlocks) xc_decode_noallo
     const uint32_t *cs = reinterpret_cast<const uint32_t *>(blob + kXcTabOff);
     const uint32_t ca = cs[c], cz = cs[c + 1];
     const uint8_t *rec = blob + T.chunks_off + 16ull * ca;
-    const uint32_t rec_bytes = 16u * (cz - ca);
+    const uint32_t rec_bytes = checked_rec_bytes(ca, cz, T.rec_lim16);
     const uint64_t e0 = static_cast<uint64_t>(c) * T.chunk_elems;
     const uint64_t left = T.n - e0;
     const uint32_t cn = left < T.chunk_elems ? static_cast<uint32_t>(left) : T.chunk_elems;
@@ -866,7 +888,7 @@ __global__ void __launch_bounds__(kThreads, kPairMinBlocks) xc_decode_noalloc_pa
     const uint64_t left = T.n - e0;
     const uint32_t cn = left < T.chunk_elems ? static_cast<uint32_t>(left) : T.chunk_elems;
     decode_chunk_pair(static_cast<uint32_t>(__cvta_generic_to_shared(smem)), s_ring + warp * kPairWarpRing,
-                      blob + T.chunks_off + 16ull * ca, 16u * (cz - ca), blob + T.plane_off + e0,
+                      blob + T.chunks_off + 16ull * ca, checked_rec_bytes(ca, cz, T.rec_lim16), blob + T.plane_off + e0,
                       T.out + (e0 - static_cast<uint64_t>(T.chunk_begin) * T.chunk_elems), cn, P, &errs[ti]);
 }
 
