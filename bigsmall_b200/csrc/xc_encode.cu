@@ -114,48 +114,87 @@ __global__ void __launch_bounds__(256) xc_enc_setup_kernel(const unsigned long l
     __shared__ uint32_t s_cum[256];
     __shared__ uint8_t s_spread[kXcMaxTable];
     __shared__ uint32_t s_occ[256];
-    __shared__ unsigned long long s_counts[256];
+    __shared__ unsigned long long s_red64[8];
+    __shared__ uint32_t s_red[8];
     const int tid = threadIdx.x;
+    const uint32_t lane = tid & 31, warp = tid >> 5;
     const int64_t M = 1ll << prec;
-    s_counts[tid] = counts[tid];   // one global load per thread instead of serial loads in thread 0
-    __syncthreads();
-    if (tid == 0) {
-        const unsigned long long *counts = s_counts;
-        int nnz = 0, first = -1;
-        unsigned long long total = 0;
-        for (int s = 0; s < 256; s++)
-            if (counts[s]) { nnz++; total += counts[s]; if (first < 0) first = s; }
-        for (int s = 0; s < 256; s++) f[s] = 0;
-        if (nnz <= 1) {
-            int s = first < 0 ? 0 : first;
-            f[s] = M - 1;
-            f[(s + 1) & 255] = 1;
-        } else {
-            int64_t sum = 0;
-            for (int s = 0; s < 256; s++) {
-                unsigned long long cs = counts[s];
-                // cs < 2^51 for any tensor that fits in memory, so cs*M fits in 64 bits
-                int64_t v = cs ? static_cast<int64_t>((cs * static_cast<unsigned long long>(M)) / total) : 0;
-                if (cs && v == 0) v = 1;
-                f[s] = v;
-                sum += v;
-            }
-            int64_t diff = M - sum;
+    // One symbol per thread; the sequential steps of the rule (the remainder
+    // and excess go to the most frequent symbol, lowest index on ties) become
+    // block reductions over (freq << 8 | 255 - symbol).
+    auto block_max = [&](uint32_t k) -> uint32_t {
+        k = __reduce_max_sync(0xFFFFFFFFu, k);
+        __syncthreads();   // the previous reduction's readers are done
+        if (lane == 0) s_red[warp] = k;
+        __syncthreads();
+        uint32_t r = s_red[0];
+#pragma unroll
+        for (int w = 1; w < 8; w++) r = max(r, s_red[w]);
+        return r;
+    };
+    auto block_add = [&](uint32_t k) -> uint32_t {
+        k = __reduce_add_sync(0xFFFFFFFFu, k);
+        __syncthreads();
+        if (lane == 0) s_red[warp] = k;
+        __syncthreads();
+        uint32_t r = 0;
+#pragma unroll
+        for (int w = 0; w < 8; w++) r += s_red[w];
+        return r;
+    };
+    const unsigned long long c = counts[tid];
+    unsigned long long tot = c;
+#pragma unroll
+    for (int d = 16; d > 0; d >>= 1) tot += __shfl_xor_sync(0xFFFFFFFFu, tot, d);
+    if (lane == 0) s_red64[warp] = tot;
+    const int nnz = __syncthreads_count(c != 0);
+    unsigned long long total = 0;
+#pragma unroll
+    for (int w = 0; w < 8; w++) total += s_red64[w];
+    int64_t v;
+    if (nnz <= 1) {
+        // the present symbol (0 if none) gets M-1, its successor a phantom 1
+        const uint32_t first = 255u - (block_max(c ? 255u - tid : 0u) & 255u);
+        const uint32_t s = nnz ? first : 0u;
+        v = tid == static_cast<int>(s) ? M - 1 : (tid == static_cast<int>((s + 1) & 255) ? 1 : 0);
+        f[tid] = v;
+    } else {
+        // c < 2^51 for any tensor that fits in memory, so c*M fits in 64 bits
+        v = c ? static_cast<int64_t>((c * static_cast<unsigned long long>(M)) / total) : 0;
+        if (c && v == 0) v = 1;
+        f[tid] = v;
+        int64_t diff = M - static_cast<int64_t>(block_add(static_cast<uint32_t>(v)));
+        while (diff != 0) {   // uniform: every thread sees the same diff
+            const uint32_t best = 255u - (block_max((static_cast<uint32_t>(f[tid]) << 8) | (255u - tid)) & 255u);
             if (diff > 0) {
-                int best = 0;
-                for (int s = 1; s < 256; s++) if (f[s] > f[best]) best = s;
-                f[best] += diff;
-            }
-            while (diff < 0) {
-                int best = 0;
-                for (int s = 1; s < 256; s++) if (f[s] > f[best]) best = s;
-                int64_t take = f[best] - 1 < -diff ? f[best] - 1 : -diff;
-                f[best] -= take;
+                if (tid == static_cast<int>(best)) f[tid] += diff;
+                diff = 0;
+            } else {
+                const int64_t fb = f[best];
+                const int64_t take = fb - 1 < -diff ? fb - 1 : -diff;
+                __syncthreads();   // everyone has read f[best]
+                if (tid == static_cast<int>(best)) f[tid] -= take;
                 diff += take;
             }
+            __syncthreads();
         }
-        uint32_t cum = 0;
-        for (int s = 0; s < 256; s++) { s_cum[s] = cum; cum += static_cast<uint32_t>(f[s]); }
+    }
+    __syncthreads();
+    {
+        // exclusive prefix sum of the frequencies
+        const uint32_t fv = static_cast<uint32_t>(f[tid]);
+        uint32_t incl = fv;
+#pragma unroll
+        for (int d = 1; d < 32; d <<= 1) {
+            const uint32_t o = __shfl_up_sync(0xFFFFFFFFu, incl, d);
+            if (lane >= static_cast<uint32_t>(d)) incl += o;
+        }
+        __syncthreads();
+        if (lane == 31) s_red[warp] = incl;
+        __syncthreads();
+        uint32_t base = 0;
+        for (uint32_t w = 0; w < warp; w++) base += s_red[w];
+        s_cum[tid] = base + incl - fv;
     }
     __syncthreads();
     // header

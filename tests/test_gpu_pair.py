@@ -205,12 +205,12 @@ def test_decode_timed_records_events_around_the_decode_kernels():
 @pytest.mark.parametrize("coder,name", [(0, "rans"), (1, "tans"), (2, "pair")])
 @pytest.mark.parametrize("prec", [8, 10, 12])
 def test_special_distributions_decode_and_device_encoder(coder, name, prec):
-    """All-zero, NaN/Inf, subnormal, top-exponent (window base 241) and
-    two-cluster tensors: device decode of oracle blobs and device encode,
+    """All-zero, NaN/Inf, subnormal, top-exponent (window base 241),
+    two-cluster and many-rare-exponent tensors: device decode of oracle blobs and device encode,
     both bit-exact, at the format's small and default precisions."""
     from bigsmall_b200 import gpu
     from tests.test_oracle_xc import _special
-    for kind in ("zeros", "nan_inf", "subnormal", "top_exponents", "two_clusters"):
+    for kind in ("zeros", "nan_inf", "subnormal", "top_exponents", "two_clusters", "many_rare"):
         for n in (1, 300, 70_001):
             raw = _special(kind, n)
             blob = O.xc_encode(raw, coder, prec, 4096)

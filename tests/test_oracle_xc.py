@@ -149,13 +149,20 @@ def _special(kind: str, n: int) -> bytes:
     elif kind == "top_exponents":      # exponents 240..255: window base at its maximum (241)
         e = rng.integers(240, 256, n)
         w = ((rng.integers(0, 2, n) << 15) | (e << 7) | rng.integers(0, 128, n)).astype(np.uint16)
+    elif kind == "many_rare":          # every exponent present, two dominant ones: at low precision
+        # the rare symbols' floor of 1 overshoots M and the excess is taken
+        # from more than one symbol
+        e = np.where(rng.random(n) < 0.5, 120, 121)
+        k = min(n, 512)
+        e[:k] = np.arange(k) % 256
+        w = ((e << 7) | rng.integers(0, 128, n)).astype(np.uint16)
     else:                              # two far-apart exponent clusters: many escapes
         e = np.where(rng.random(n) < 0.5, rng.integers(1, 8, n), rng.integers(200, 230, n))
         w = ((e << 7) | rng.integers(0, 128, n)).astype(np.uint16)
     return w.tobytes()
 
 
-@pytest.mark.parametrize("kind", ["zeros", "nan_inf", "subnormal", "top_exponents", "two_clusters"])
+@pytest.mark.parametrize("kind", ["zeros", "nan_inf", "subnormal", "top_exponents", "two_clusters", "many_rare"])
 @pytest.mark.parametrize("coder", [0, 1, 2])
 @pytest.mark.parametrize("prec", [8, 10, 12])
 def test_xc_special_value_distributions(kind, coder, prec):
