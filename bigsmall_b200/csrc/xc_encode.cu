@@ -326,7 +326,7 @@ __global__ void __launch_bounds__(256) xc_enc_pair_hist_kernel(const uint16_t *_
     if (t) atomicAdd(&pcounts[threadIdx.x], static_cast<unsigned long long>(t));
 }
 
-// 3c. per-chunk reverse rANS over exponent pairs, then the escape list ------
+// 3c. per-chunk reverse rANS over exponent pairs, with the escape list -------
 __global__ void __launch_bounds__(kEncWarps * 32) xc_enc_chunks_pair_kernel(
     const uint16_t *__restrict__ in, uint64_t n, uint32_t ce, uint32_t nc, int prec,
     const uint4 *__restrict__ rcp_tab, const uint32_t *aux, uint8_t *__restrict__ slots, uint64_t slot_b,
@@ -349,19 +349,38 @@ __global__ void __launch_bounds__(kEncWarps * 32) xc_enc_chunks_pair_kernel(
     asm("mov.u32 %0, %%lanemask_lt;" : "=r"(lt));
     uint32_t x = kRansL, cur = 0;
     const uint32_t G = cn >> 8, rem = cn & 255;
+    // Escapes are written during the backward pass, downwards from eend: a
+    // pair-step's escapes (lanes in order, first value then second) go just
+    // below those of the later steps, so the list ends up in forward order in
+    // [eend - n_esc, eend).  At most one renorm word per lane and pair-step
+    // keeps the words (<= ce bytes, downwards from the slot end) above eend.
+    uint8_t *eend = slot + kXcPairRecHdr + ce;
+    uint32_t ecur = 0;
+    const uint32_t thr_shift = 32 - P;
 
     // x <- (x / f) << P | (x mod f) + cum  ==  x + cum + (x / f) (M - f)
-    auto enc = [&](uint32_t sym, bool active) {
-        const uint4 t = s_tab[sym];
+    auto enc = [&](uint32_t v0, uint32_t v1, bool act, bool has_b) {
+        const uint32_t a = act ? pair_a(v0, e_lo) : 0u;
+        const uint32_t b = has_b ? pair_a(v1, e_lo) : 0u;
+        const bool ea = act && a == 15, eb = has_b && b == 15;
+        const uint32_t ba = __ballot_sync(kFull, ea), bb = __ballot_sync(kFull, eb);
+        if (ba | bb) {
+            const int64_t k = static_cast<int64_t>(ecur) + __popc(ba) + __popc(bb);
+            const int64_t pa = static_cast<int64_t>(__popc(ba & lt) + __popc(bb & lt)) - k;
+            if (ea) eend[pa] = static_cast<uint8_t>((v0 >> 7) & 0xFF);
+            if (eb) eend[pa + (ea ? 1 : 0)] = static_cast<uint8_t>((v1 >> 7) & 0xFF);
+            ecur = static_cast<uint32_t>(k);
+        }
+        const uint4 t = s_tab[a * 16 + b];
         const uint32_t f = t.z & 0xFFFF, cf = t.z >> 16;
-        const bool emit = active && (static_cast<uint64_t>(x) >= (static_cast<uint64_t>(f) << (32 - P)));
+        const bool emit = act && x >= (f << thr_shift);   // f < 2^P: the threshold fits 32 bits
         const uint32_t m = __ballot_sync(kFull, emit);
         if (emit) {
             wend[-1 - static_cast<int64_t>(cur + __popc(m & gt))] = static_cast<uint16_t>(x & 0xFFFF);
             x >>= 16;
         }
         cur += __popc(m);
-        if (active) {
+        if (act) {
             const uint32_t q = rcp_div(x, t.x, t.y & 0xFF, t.y >> 8);
             x = x + cf + q * t.w;
         }
@@ -370,10 +389,8 @@ __global__ void __launch_bounds__(kEncWarps * 32) xc_enc_chunks_pair_kernel(
         const uint32_t eb = G * 256 + lane * 8;
         for (int jj = 3; jj >= 0; jj--) {
             const uint32_t e = lane * 8 + 2 * jj;
-            const bool act = e < rem;
-            const uint32_t a = act ? pair_a(src[eb + 2 * jj], e_lo) : 0u;
-            const uint32_t b = e + 1 < rem ? pair_a(src[eb + 2 * jj + 1], e_lo) : 0u;
-            enc(a * 16 + b, act);
+            const bool act = e < rem, has_b = e + 1 < rem;
+            enc(act ? src[eb + 2 * jj] : 0u, has_b ? src[eb + 2 * jj + 1] : 0u, act, has_b);
         }
     }
     // groups run backwards; the next two groups' values are in flight
@@ -385,51 +402,15 @@ __global__ void __launch_bounds__(kEncWarps * 32) xc_enc_chunks_pair_kernel(
         const uint4 v = n1;
         n1 = n2;
         if (g >= 2) n2 = grp(g - 2);
-        enc(pair_a(v.w & 0xFFFF, e_lo) * 16 + pair_a(v.w >> 16, e_lo), true);
-        enc(pair_a(v.z & 0xFFFF, e_lo) * 16 + pair_a(v.z >> 16, e_lo), true);
-        enc(pair_a(v.y & 0xFFFF, e_lo) * 16 + pair_a(v.y >> 16, e_lo), true);
-        enc(pair_a(v.x & 0xFFFF, e_lo) * 16 + pair_a(v.x >> 16, e_lo), true);
+        enc(v.w & 0xFFFF, v.w >> 16, true, true);
+        enc(v.z & 0xFFFF, v.z >> 16, true, true);
+        enc(v.y & 0xFFFF, v.y >> 16, true, true);
+        enc(v.x & 0xFFFF, v.x >> 16, true, true);
     }
     reinterpret_cast<uint32_t *>(slot)[lane] = x;
-    // escape list, forward: per pair-step, lanes in order, first value then second
-    uint8_t *esc = slot + kXcPairRecHdr;
-    uint32_t epos = 0;
-    auto esc_step = [&](uint32_t w, bool act, bool has_b) {
-        const uint32_t v0 = w & 0xFFFF, v1 = w >> 16;
-        const bool ea = act && pair_a(v0, e_lo) == 15;
-        const bool eb = has_b && pair_a(v1, e_lo) == 15;
-        const uint32_t ba = __ballot_sync(kFull, ea), bb = __ballot_sync(kFull, eb);
-        if (ba | bb) {
-            const uint32_t pa = epos + __popc(ba & lt) + __popc(bb & lt);
-            if (ea) esc[pa] = static_cast<uint8_t>((v0 >> 7) & 0xFF);
-            if (eb) esc[pa + (ea ? 1u : 0u)] = static_cast<uint8_t>((v1 >> 7) & 0xFF);
-            epos += __popc(ba) + __popc(bb);
-        }
-    };
-    n1 = G > 0 ? grp(0) : make_uint4(0, 0, 0, 0);
-    n2 = G > 1 ? grp(1) : make_uint4(0, 0, 0, 0);
-    for (uint32_t g = 0; g < G; g++) {
-        const uint4 v = n1;
-        n1 = n2;
-        if (g + 2 < G) n2 = grp(static_cast<int>(g) + 2);
-        esc_step(v.x, true, true);
-        esc_step(v.y, true, true);
-        esc_step(v.z, true, true);
-        esc_step(v.w, true, true);
-    }
-    if (rem) {
-        const uint32_t eb0 = G * 256 + lane * 8;
-        for (uint32_t jj = 0; jj < 4; jj++) {
-            const uint32_t e = lane * 8 + 2 * jj;
-            const bool act = e < rem, has_b = e + 1 < rem;
-            const uint32_t w = (act ? static_cast<uint32_t>(src[eb0 + 2 * jj]) : 0u) |
-                               (has_b ? static_cast<uint32_t>(src[eb0 + 2 * jj + 1]) << 16 : 0u);
-            esc_step(w, act, has_b);
-        }
-    }
     if (lane == 0) {
         rec_words[c] = cur;
-        rec_esc[c] = epos;
+        rec_esc[c] = ecur;
     }
 }
 
@@ -460,7 +441,7 @@ __global__ void __launch_bounds__(kEncWarps * 32) xc_enc_chunks_kernel(
         const uint32_t sym = (v >> 7) & 0xFF;
         const uint4 t = s_tab[sym];
         const uint32_t f = t.z & 0xFFFF, cf = t.z >> 16;
-        const bool emit = active && (static_cast<uint64_t>(x) >= (static_cast<uint64_t>(f) << (32 - P)));
+        const bool emit = active && x >= (f << (32 - P));   // f < 2^P: the threshold fits 32 bits
         const uint32_t m = __ballot_sync(kFull, emit);
         if (emit) {
             wend[-1 - static_cast<int64_t>(cur + __popc(m & gt))] = static_cast<uint16_t>(x & 0xFFFF);
@@ -644,11 +625,21 @@ __global__ void __launch_bounds__(1024) xc_enc_scan_kernel(const uint32_t *__res
 }
 
 // 5. compaction -----------------------------------------------------------------
+// Four bytes from any address: one aligned load, or two and a funnel shift.
+// Only the aligned words holding the four bytes are read.
+__device__ __forceinline__ uint32_t ld_u32_any(const uint8_t *p) {
+    const uintptr_t a = reinterpret_cast<uintptr_t>(p);
+    const uint32_t *base = reinterpret_cast<const uint32_t *>(a & ~static_cast<uintptr_t>(3));
+    const uint32_t k = static_cast<uint32_t>(a & 3);
+    if (k == 0) return base[0];
+    return __funnelshift_r(base[0], base[1], 8 * k);
+}
+
 __global__ void __launch_bounds__(256) xc_enc_compact_kernel(const uint8_t *__restrict__ slots, uint64_t slot_b,
                                                              const uint32_t *__restrict__ rec_words,
                                                              const uint32_t *__restrict__ rec_esc,
                                                              uint8_t *out, uint64_t chunks_off,
-                                                             const uint32_t *flags, int coder) {
+                                                             const uint32_t *flags, int coder, uint32_t ce) {
     if (*flags) return;
     const uint32_t c = blockIdx.x;
     const uint32_t W = rec_words[c];
@@ -657,27 +648,46 @@ __global__ void __launch_bounds__(256) xc_enc_compact_kernel(const uint8_t *__re
     const uint8_t *slot = slots + static_cast<uint64_t>(c) * slot_b;
     if (threadIdx.x < 32)
         reinterpret_cast<uint32_t *>(dst)[threadIdx.x] = reinterpret_cast<const uint32_t *>(slot)[threadIdx.x];
-    if (coder == BS_CODER_RANS_PAIR) {
-        // [states][n_words][n_esc][0][0][words][escapes] zero-padded to 16 B
-        const uint32_t E = rec_esc[c];
+    // pair records: [states][n_words][n_esc][0][0][words][escapes]; rANS and
+    // tANS records: [states][words]; zero-padded to 16 bytes.  rANS and pair
+    // words sit at the end of the slot (written backwards), tANS words right
+    // after the lane states; pair escapes end at hdr + ce (written backwards).
+    const bool pair = coder == BS_CODER_RANS_PAIR;
+    const uint32_t hdr = pair ? kXcPairRecHdr : 128u;
+    const uint32_t E = pair ? rec_esc[c] : 0u;
+    if (pair && threadIdx.x == 0) {
         uint32_t *d32 = reinterpret_cast<uint32_t *>(dst);
-        if (threadIdx.x == 0) { d32[32] = W; d32[33] = E; d32[34] = 0; d32[35] = 0; }
-        const uint16_t *ws = reinterpret_cast<const uint16_t *>(slot + slot_b) - W;
-        uint16_t *wd = reinterpret_cast<uint16_t *>(dst + kXcPairRecHdr);
-        for (uint32_t i = threadIdx.x; i < W; i += blockDim.x) wd[i] = ws[i];
-        const uint8_t *es = slot + kXcPairRecHdr;
-        uint8_t *ed = dst + kXcPairRecHdr + 2ull * W;
-        const uint32_t tail = ((kXcPairRecHdr + 2u * W + E + 15u) & ~15u) - kXcPairRecHdr - 2u * W;
-        for (uint32_t i = threadIdx.x; i < tail; i += blockDim.x) ed[i] = i < E ? es[i] : 0;
-        return;
+        d32[32] = W; d32[33] = E; d32[34] = 0; d32[35] = 0;
     }
-    // rANS records hold their words at the end of the slot (written backwards),
-    // tANS records right after the lane states (written forwards)
-    const uint16_t *ws = coder == BS_CODER_TANS ? reinterpret_cast<const uint16_t *>(slot + 128)
-                                                : reinterpret_cast<const uint16_t *>(slot + slot_b) - W;
-    uint16_t *wd = reinterpret_cast<uint16_t *>(dst + 128);
-    const uint32_t padded = ((128u + 2u * W + 15u) & ~15u) - 128u;   // bytes incl. zero pad
-    for (uint32_t i = threadIdx.x; i < padded / 2; i += blockDim.x) wd[i] = i < W ? ws[i] : 0;
+    const uint8_t *ws = coder == BS_CODER_TANS ? slot + 128 : slot + slot_b - 2ull * W;
+    const uint8_t *es = slot + hdr + ce - E;
+    // body = words, escapes, zero pad: 16 bytes per thread and pass, each
+    // 32-bit piece funnel-shifted from aligned loads of the source region it
+    // lies in (words start 2-byte aligned, escapes anywhere)
+    const uint32_t wb = 2u * W, eb = wb + E;
+    const uint32_t body = ((hdr + eb + 15u) & ~15u) - hdr;
+    uint4 *bd = reinterpret_cast<uint4 *>(dst + hdr);
+    for (uint32_t v = threadIdx.x; v < body / 16; v += blockDim.x) {
+        uint32_t o[4];
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            const uint32_t jb = 16 * v + 4 * k;
+            if (jb + 4 <= wb) {
+                o[k] = ld_u32_any(ws + jb);
+            } else if (jb >= wb && jb + 4 <= eb) {
+                o[k] = ld_u32_any(es + (jb - wb));
+            } else {   // a piece across a region edge, or the pad
+                uint32_t w = 0;
+                for (uint32_t q = 0; q < 4; q++) {
+                    const uint32_t b = jb + q;
+                    const uint32_t byte = b < wb ? ws[b] : (b < eb ? es[b - wb] : 0u);
+                    w |= byte << (8 * q);
+                }
+                o[k] = w;
+            }
+        }
+        bd[v] = make_uint4(o[0], o[1], o[2], o[3]);
+    }
 }
 
 cudaError_t launch_xc_encode(const uint16_t *d_in, uint64_t n, int coder, int prec, uint32_t ce,
@@ -730,7 +740,7 @@ cudaError_t launch_xc_encode(const uint16_t *d_in, uint64_t n, int coder, int pr
     xc_enc_scan_kernel<<<1, 1024, 0, s>>>(recw, rece, coder, static_cast<uint32_t>(nc), d_out, chunks_off, out_cap,
                                           reinterpret_cast<unsigned long long *>(d_out_len), flags);
     xc_enc_compact_kernel<<<static_cast<unsigned>(nc), 256, 0, s>>>(slots, sb, recw, rece, d_out, chunks_off,
-                                                                    flags, coder);
+                                                                    flags, coder, ce);
     (void)ws_bytes;
     return cudaGetLastError();
 }
