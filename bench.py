@@ -68,42 +68,6 @@ def gen_tensor(torch, g, shape, kind, device):
     return (torch.randn(shape, generator=g, device=device) * (1.0 / math.sqrt(fan_in))).to(torch.bfloat16)
 
 
-def partition(tensors, world, chunk_elems):
-    """Ownership: cut the container's chunk sequence (tensors in name order)
-    into `world` contiguous spans of equal element count.  Each rank owns a few
-    whole tensors plus at most two chunk ranges of the tensors at its span
-    ends; loads differ by at most one chunk."""
-    spans = []          # (name, n, n_chunks)
-    for name, shape, _ in tensors:
-        n = math.prod(shape)
-        spans.append((name, n, -(-n // chunk_elems)))
-    total = sum(n for _, n, _ in spans)
-    owned = [[] for _ in range(world)]
-    load = [0] * world
-    r, acc = 0, 0
-    for name, n, nc in spans:
-        c = 0
-        while c < nc:
-            target = total * (r + 1) / world
-            # chunks of this tensor that still fit into rank r's span
-            take = nc - c
-            if r < world - 1:
-                room = target - acc
-                fit = max(1, int(round(room / chunk_elems))) if room > 0 else 0
-                take = min(take, fit) if fit else 0
-            if take == 0:
-                r += 1
-                continue
-            e = min(n, (c + take) * chunk_elems) - c * chunk_elems
-            owned[r].append((name, c, take) if (c, take) != (0, nc) else (name, 0, 0))
-            load[r] += e
-            acc += e
-            c += take
-            if r < world - 1 and acc >= target - chunk_elems / 2:
-                r += 1
-    return owned, load
-
-
 # ---------------------------------------------------------------------------
 # clocks (NVML polled during the timed region)
 # ---------------------------------------------------------------------------
@@ -297,6 +261,7 @@ def main():
     from bigsmall_b200 import gpu
     from bigsmall_b200.container import ContainerWriter
     from bigsmall_b200.loader import ContainerImage, DeviceLoader
+    from bigsmall_b200.sharding import partition
 
     ce = a.chunk_elems or gpu.DEFAULT_CHUNK_ELEMS
     config = {"workload": "llama3-8b-shaped bf16 container (BASELINE config 2), full-container decode",

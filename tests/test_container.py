@@ -59,10 +59,11 @@ def test_v1_files_read():
 
 
 @pytest.mark.parametrize("world", [1, 2, 3, 4, 8])
-def test_bench_partition_covers_container_once(world):
+def test_partition_covers_container_once(world):
     import bench
+    from bigsmall_b200.sharding import partition
     tensors = bench.llama3_8b_tensors()
-    owned, load = bench.partition(tensors, world, 65536)
+    owned, load = partition(tensors, world, 65536)
     assert max(load) - min(load) <= 65536
     seen = {}
     for r in owned:
@@ -83,3 +84,28 @@ def test_top_level_names_follow_the_reference():
     for name in ("decompress", "load", "verify", "info", "StreamingLoader", "BigSmallStreamingModel",
                  "CompressedKVCache", "BigSmallVersionError"):
         assert callable(getattr(b, name)), name
+
+
+def test_owned_for_header_mixed_chunk_sizes():
+    """Per-tensor chunk sizes from the header; every chunk has one owner and
+    rank loads differ by at most the largest chunk."""
+    from bigsmall_b200.sharding import owned_for, partition_chunks
+    sizes = [(f"t{i}", n, ce) for i, (n, ce) in
+             enumerate([(5_000_000, 32768), (123_457, 65536), (40_000_000, 32768), (4096, 256), (9_999_999, 65536)])]
+    hdr = {"tensors": [{"name": nm, "shape": [n], "codec": "bf16_exp_chunked_v1", "extra": {"chunk_elems": ce}}
+                       for nm, n, ce in sizes] + [{"name": "raw", "shape": [7], "codec": "raw", "extra": {}}]}
+    for world in (1, 2, 3, 5, 8):
+        owned = [owned_for(hdr, r, world) for r in range(world)]
+        _, load = partition_chunks(sizes, world)
+        assert max(load) - min(load) <= 65536
+        for nm, n, ce in sizes:
+            nc = -(-n // ce)
+            parts = sorted((c0, cc or nc) for r in owned for name, c0, cc in r if name == nm)
+            pos = 0
+            for c0, cc in parts:
+                assert c0 == pos
+                pos += cc
+            assert pos == nc
+        assert all(name != "raw" for r in owned for name, _, _ in r)
+    with pytest.raises(ValueError):
+        owned_for(hdr, 2, 2)
