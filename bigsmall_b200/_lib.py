@@ -73,6 +73,7 @@ SIGNATURES = {
     "bs_plan_decode": (_I, [_P, _P]),
     "bs_plan_decode_timed": (_I, [_P, _P, _P, _P]),
     "bs_plan_decode_after": (_I, [_P, _P, _P, _P]),
+    "bs_plan_decode_handoff": (_I, [_P, _P, _P, _P, _P, _P]),
     "bs_plan_check": (_I, [_P, _P, ctypes.POINTER(_U32)]),
     "bs_plan_n_tensors": (_I, [_P]),
     "bs_plan_set_max_ctas": (_I, [_P, _I]),

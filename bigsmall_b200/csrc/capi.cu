@@ -335,6 +335,23 @@ int bs_plan_decode_after(bs_plan *p, void *stream, void *wait_event, void *done_
     return BS_OK;
 }
 
+int bs_plan_decode_handoff(bs_plan *p, void *main_stream, void *side_stream, void *release_event,
+                           void *done_event, void *next_event) {
+    if (!p) return fail(BS_E_INVALID_ARG, "plan is NULL");
+    if (!release_event || !done_event) return fail(BS_E_INVALID_ARG, "hand-off needs release and done events");
+    DeviceGuard guard(p->device);
+    cudaStream_t m = static_cast<cudaStream_t>(main_stream);
+    cudaError_t e = cudaEventRecord(static_cast<cudaEvent_t>(release_event), m);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaEventRecord(release)");
+    const int rc = bs_plan_decode_after(p, side_stream, release_event, done_event);
+    if (rc) return rc;
+    if (next_event) {
+        e = cudaStreamWaitEvent(m, static_cast<cudaEvent_t>(next_event), 0);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaStreamWaitEvent(next)");
+    }
+    return BS_OK;
+}
+
 int bs_plan_check(bs_plan *p, void *stream, uint32_t *status_out) {
     if (!p) return fail(BS_E_INVALID_ARG, "plan is NULL");
     DeviceGuard guard(p->device);

@@ -88,6 +88,27 @@ class _Plan:
                                           ctypes.c_void_p(done.cuda_event) if done is not None else None),
                    "bs_plan_decode_after")
 
+    def handoff_call(self, side: torch.cuda.Stream, release: torch.cuda.Event, done: torch.cuda.Event,
+                     next_ev: Optional[torch.cuda.Event] = None):
+        """A prepared ``f(main_stream)`` for a two-stream prefetch: records
+        ``release`` on ``main_stream``, makes ``side`` wait for it, decodes on
+        ``side``, records ``done`` there, then makes ``main_stream`` wait for
+        ``next_ev`` -- one library call per use, its arguments resolved once
+        (events must have been recorded once, which creates them)."""
+        for ev in (release, done, next_ev):
+            if ev is not None and not ev.cuda_event:
+                raise ValueError("hand-off events must have been recorded once")
+        fn = _lib.load().bs_plan_decode_handoff
+        h = self._h
+        args = (ctypes.c_void_p(side.cuda_stream), ctypes.c_void_p(release.cuda_event),
+                ctypes.c_void_p(done.cuda_event), ctypes.c_void_p(next_ev.cuda_event) if next_ev is not None else None)
+
+        def call(main: torch.cuda.Stream) -> None:
+            rc = fn(h, main.cuda_stream, *args)
+            if rc:
+                _lib.check(rc, "bs_plan_decode_handoff")
+        return call
+
     def check(self, stream: Optional[torch.cuda.Stream] = None) -> list[int]:
         """Synchronise `stream` and raise BsCorruptError if any tensor failed."""
         L = _lib.load()

@@ -322,6 +322,21 @@ class Bundle:
         if done is not None:
             done.record(stream)
 
+    def handoff_call(self, side: torch.cuda.Stream, release, done, next_ev=None):
+        """A prepared ``f(main_stream)``: ``release`` recorded on the main
+        stream, ``side`` waits for it, decodes, records ``done``, and the main
+        stream waits for ``next_ev``; one library call for a bundle of one plan
+        and no copies."""
+        if len(self.plans) == 1 and not self.copies:
+            return self.plans[0].handoff_call(side, release, done, next_ev)
+
+        def call(main: torch.cuda.Stream) -> None:
+            release.record(main)
+            self.decode_after(side, release, done)
+            if next_ev is not None:
+                main.wait_event(next_ev)
+        return call
+
     def decode(self, stream: Optional[torch.cuda.Stream] = None) -> None:
         for pl in self.plans:
             pl.decode(stream)

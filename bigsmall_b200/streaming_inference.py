@@ -150,6 +150,14 @@ class BigSmallStreamingModel:
         self._bound = [-1] * self.n_layers
         for i in range(self.n_layers):
             self._bind(i, i % self.n_slots)
+        # per (layer, slot): the whole hand-off after the running layer as one
+        # prepared library call -- "slot released" on the model stream, the
+        # side stream decodes the layer into it, and the model stream waits for
+        # the slot of the layer that runs next
+        self._handoff = {(i, s): self._bundles[(i, s)].handoff_call(
+                             self._side, self._released[s], self._decoded[s],
+                             self._decoded[(s + 1) % self.n_slots])
+                         for i in range(self.n_layers) for s in range(self.n_slots)}
 
     # ------------------------------------------------------------------
     def _bind(self, layer: int, slot: int) -> None:
@@ -182,21 +190,20 @@ class BigSmallStreamingModel:
                 if outer._bound[layer_idx] != slot:
                     outer._bind(layer_idx, slot)
                 return original(*args, **kwargs)
+            slot = outer._k % outer.n_slots
             if not outer._primed or outer._expect != layer_idx:
                 # first call, or out of the expected order: drain the side
                 # stream and restart the pipeline at this layer
                 outer._side.synchronize()
                 outer._prime(first_layer=layer_idx)
-            slot = outer._k % outer.n_slots
-            main.wait_event(outer._decoded[slot])
+                main.wait_event(outer._decoded[slot])
+            # (in order, the previous layer's hand-off made the model stream
+            # wait for this layer's slot)
             if outer._bound[layer_idx] != slot:
                 outer._bind(layer_idx, slot)
             out = original(*args, **kwargs)
-            outer._released[slot].record(main)
             nxt = (layer_idx + outer.n_slots) % outer.n_layers
-            # side stream: wait for "slot released", decode layer nxt into it,
-            # record "slot decoded" -- one library call for an all-xc bundle
-            outer._bundles[(nxt, slot)].decode_after(outer._side, outer._released[slot], outer._decoded[slot])
+            outer._handoff[(nxt, slot)](main)
             outer._k += 1
             outer._expect = (layer_idx + 1) % outer.n_layers
             return out

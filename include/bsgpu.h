@@ -103,6 +103,15 @@ int bs_plan_decode_timed(bs_plan *plan, void *stream, void *ev_start, void *ev_s
  * (may be NULL) is recorded.  Used by the streaming model's per-layer prefetch
  * to keep host work per layer to one call.  No reference counterpart. */
 int bs_plan_decode_after(bs_plan *plan, void *stream, void *wait_event, void *done_event);
+/* The whole per-layer hand-off of a two-stream prefetch in one call:
+ * `release_event` is recorded on `main_stream` (the running layer is done with
+ * the slot), `side_stream` waits for it, the plan decodes on `side_stream`,
+ * `done_event` is recorded there, and finally `main_stream` waits for
+ * `next_event` (the slot of the layer that runs next; may be NULL).  Replaces
+ * the reference's prefetch-thread hand-off, bigsmall/streaming_inference.py:
+ * 272-348 (decode the next layer while this one runs, swap it in after). */
+int bs_plan_decode_handoff(bs_plan *plan, void *main_stream, void *side_stream, void *release_event,
+                           void *done_event, void *next_event);
 
 /* Synchronise `stream`, read the per-tensor device status words into
  * `status_out` (may be NULL; else n_tensors entries) and return BS_OK or

@@ -218,3 +218,30 @@ def test_special_distributions_decode_and_device_encoder(coder, name, prec):
             x = torch.from_numpy(np.frombuffer(raw, dtype=np.int16).copy()).view(torch.bfloat16).cuda()
             d = gpu.encode_xc(x, coder=name, prec=prec, chunk_elems=4096).cpu().numpy().tobytes()
             assert d == blob, (kind, name, prec, n)
+
+
+def test_handoff_call_chains_both_streams():
+    """bs_plan_decode_handoff (the streaming prefetch's per-layer call): the
+    side-stream decode follows the main stream's release point, and main-stream
+    work enqueued after the call sees the decoded tensor."""
+    from bigsmall_b200 import gpu
+    n = 1_000_003
+    raw = _normal(n, 21)
+    blob = _dev(O.xc_encode(raw, 2, 12, 4096))
+    out = torch.empty(n, dtype=torch.bfloat16, device="cuda")
+    main, side = torch.cuda.current_stream(), torch.cuda.Stream()
+    rel, done = torch.cuda.Event(), torch.cuda.Event()
+    with pytest.raises(ValueError):
+        with gpu.XcPlan([(blob, out.view(torch.int16), 4096)], coders="pair") as p:
+            p.handoff_call(side, rel, done, done)          # events not created yet
+    for ev in (rel, done):
+        ev.record(main)
+    with gpu.XcPlan([(blob, out.view(torch.int16), 4096)], coders="pair") as p:
+        call = p.handoff_call(side, rel, done, done)
+        for _ in range(3):
+            out.fill_(0)          # main-stream work the decode must follow
+            call(main)
+            got = out.clone()     # main-stream work after the hand-off's wait
+            torch.cuda.synchronize()
+            assert got.cpu().view(torch.uint8).numpy().tobytes() == raw
+        p.check()
