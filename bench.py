@@ -227,6 +227,7 @@ def main():
                     help="config 4: comma list of side-stream decode CTAs per SM to run (0 = uncapped)")
     ap.add_argument("--stream-priority", default="1",
                     help="config 4: comma list of 0/1: run the model on a high-priority stream (1) or not")
+    ap.add_argument("--kv-layers", type=int, default=32, help="config kv: layers of K and V (32 = config 5)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=8.0)
     ap.add_argument("--config", default="c2", choices=["c2", "small", "medium", "kv", "sweep", "stream", "mix",
@@ -541,7 +542,7 @@ def bench_kv(a, torch, dev, world, rank, dist, local):
     """32 layers x {K, V} of [16, 8, 8192, 128] bf16, N(0,1) x per-channel scale
     log-normal(0,1) [1,8,1,128], seed 0; this rank encodes and decodes its batch slice."""
     from bigsmall_b200 import gpu
-    B, H, T, D, L = 16, 8, 8192, 128, 32
+    B, H, T, D, L = 16, 8, 8192, 128, a.kv_layers
     b0, b1 = rank * B // world, (rank + 1) * B // world
     g = torch.Generator(device=dev).manual_seed(0)
     kv = []
@@ -594,8 +595,10 @@ def bench_kv(a, torch, dev, world, rank, dist, local):
             "ratio": round(comp_all / raw_all, 5), "n_gpus": world, "steps": a.steps, "warmup": a.warmup,
             "decode_ms_per_step": round(dec_ms_max, 3), "encode_ms_per_step": round(enc_ms_max, 3),
             "higher_is_better": True, "scaling": "strong", "dtype": "u16", "data": "synthetic",
-            "config": {"workload": "32 layers x {K,V} [16,8,8192,128] bf16, N(0,1) x log-normal per-channel "
-                                   "scale, seed 0; batch sharded across ranks", "chunk_elems": ce, "coder": a.coder},
+            "config": {"workload": f"{L} layers x {{K,V}} [16,8,8192,128] bf16, N(0,1) x log-normal per-channel "
+                                   "scale, seed 0; batch sharded across ranks"
+                                   + ("" if L == 32 else " (reduced case; config 5 is 32 layers)"),
+                       "chunk_elems": ce, "coder": a.coder},
             "verified": "bitwise equal" if bad == 0 else f"MISMATCH on {int(bad)} ranks"}), flush=True)
     plan.close()
     if dist:

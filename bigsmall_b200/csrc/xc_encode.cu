@@ -260,7 +260,7 @@ __global__ void __launch_bounds__(256) xc_enc_setup_kernel(const unsigned long l
 // 2b. pair coder: exponent window and pair-symbol histogram ------------------
 __device__ __forceinline__ uint32_t pair_a(uint32_t v, uint32_t e_lo) {
     const uint32_t d = ((v >> 7) & 0xFF) - e_lo;   // wraps to a large value below e_lo
-    return d <= 14 ? d : 15u;
+    return min(d, 15u);
 }
 
 // the 15-wide exponent window holding the most values (lowest base on ties):
@@ -359,30 +359,30 @@ __global__ void __launch_bounds__(kEncWarps * 32) xc_enc_chunks_pair_kernel(
     const uint32_t thr_shift = 32 - P;
 
     // x <- (x / f) << P | (x mod f) + cum  ==  x + cum + (x / f) (M - f)
-    auto enc = [&](uint32_t v0, uint32_t v1, bool act, bool has_b) {
-        const uint32_t a = act ? pair_a(v0, e_lo) : 0u;
-        const uint32_t b = has_b ? pair_a(v1, e_lo) : 0u;
-        const bool ea = act && a == 15, eb = has_b && b == 15;
+    uint16_t *wtop = wend - 1;   // the next word goes to wtop[-cur - (emitting lanes below)]
+    // one pair-step: w holds the lane's two values (first in the low half)
+    auto enc = [&](uint32_t w, bool act, bool has_b) {
+        // window index: exponent - e_lo, 15 (escape) outside the window
+        const uint32_t da = ((w >> 7) & 0xFF) - e_lo, db = ((w >> 23) & 0xFF) - e_lo;
+        const bool ea = act && da > 14, eb = has_b && db > 14;
+        const uint32_t a = act ? min(da, 15u) : 0u, b = has_b ? min(db, 15u) : 0u;
         const uint32_t ba = __ballot_sync(kFull, ea), bb = __ballot_sync(kFull, eb);
         if (ba | bb) {
             const int64_t k = static_cast<int64_t>(ecur) + __popc(ba) + __popc(bb);
             const int64_t pa = static_cast<int64_t>(__popc(ba & lt) + __popc(bb & lt)) - k;
-            if (ea) eend[pa] = static_cast<uint8_t>((v0 >> 7) & 0xFF);
-            if (eb) eend[pa + (ea ? 1 : 0)] = static_cast<uint8_t>((v1 >> 7) & 0xFF);
+            if (ea) eend[pa] = static_cast<uint8_t>((w >> 7) & 0xFF);
+            if (eb) eend[pa + (ea ? 1 : 0)] = static_cast<uint8_t>((w >> 23) & 0xFF);
             ecur = static_cast<uint32_t>(k);
         }
         const uint4 t = s_tab[a * 16 + b];
-        const uint32_t f = t.z & 0xFFFF, cf = t.z >> 16;
-        const bool emit = act && x >= (f << thr_shift);   // f < 2^P: the threshold fits 32 bits
+        const bool emit = act && x >= ((t.z & 0xFFFF) << thr_shift);   // f < 2^P: fits 32 bits
         const uint32_t m = __ballot_sync(kFull, emit);
-        if (emit) {
-            wend[-1 - static_cast<int64_t>(cur + __popc(m & gt))] = static_cast<uint16_t>(x & 0xFFFF);
-            x >>= 16;
-        }
+        if (emit) wtop[-static_cast<int32_t>(cur + __popc(m & gt))] = static_cast<uint16_t>(x);
+        x = emit ? x >> 16 : x;
         cur += __popc(m);
         if (act) {
             const uint32_t q = rcp_div(x, t.x, t.y & 0xFF, t.y >> 8);
-            x = x + cf + q * t.w;
+            x = x + (t.z >> 16) + q * t.w;
         }
     };
     if (rem) {
@@ -390,7 +390,8 @@ __global__ void __launch_bounds__(kEncWarps * 32) xc_enc_chunks_pair_kernel(
         for (int jj = 3; jj >= 0; jj--) {
             const uint32_t e = lane * 8 + 2 * jj;
             const bool act = e < rem, has_b = e + 1 < rem;
-            enc(act ? src[eb + 2 * jj] : 0u, has_b ? src[eb + 2 * jj + 1] : 0u, act, has_b);
+            enc((act ? static_cast<uint32_t>(src[eb + 2 * jj]) : 0u) |
+                    (has_b ? static_cast<uint32_t>(src[eb + 2 * jj + 1]) << 16 : 0u), act, has_b);
         }
     }
     // groups run backwards; the next two groups' values are in flight
@@ -402,10 +403,10 @@ __global__ void __launch_bounds__(kEncWarps * 32) xc_enc_chunks_pair_kernel(
         const uint4 v = n1;
         n1 = n2;
         if (g >= 2) n2 = grp(g - 2);
-        enc(v.w & 0xFFFF, v.w >> 16, true, true);
-        enc(v.z & 0xFFFF, v.z >> 16, true, true);
-        enc(v.y & 0xFFFF, v.y >> 16, true, true);
-        enc(v.x & 0xFFFF, v.x >> 16, true, true);
+        enc(v.w, true, true);
+        enc(v.z, true, true);
+        enc(v.y, true, true);
+        enc(v.x, true, true);
     }
     reinterpret_cast<uint32_t *>(slot)[lane] = x;
     if (lane == 0) {
