@@ -6,19 +6,23 @@
 // leaves HBM:
 //   1. xc_enc_hist_kernel    exponent histogram (per-warp shared-memory bins)
 //                            and the sign|mantissa byte plane, one pass.
+//      (pair coder: xc_enc_window_kernel picks the 15-exponent window, then
+//      xc_enc_pair_hist_kernel counts the pair symbols)
 //   2. xc_enc_setup_kernel   deterministic frequency quantisation (the same
-//                            rule as the CPU reference encoder), blob header,
-//                            per-symbol encode table.
+//                            rule as the CPU reference encoder, one symbol per
+//                            thread), blob header, per-symbol encode table.
 //   3. xc_enc_chunks_kernel  one warp per chunk: the 32 interleaved rANS states
 //                            run backwards over the chunk; renorm words are
 //                            written from the end of a per-chunk scratch slot
 //                            downwards so they land in decode order.
+//      xc_enc_chunks_pair_kernel  the same over exponent pairs; the escape list
+//                            is written in the same backward pass, downwards.
 //      xc_enc_chunks_tans_kernel  the tANS coder: a backward pass per lane, then
 //                            a forward replay of the decoder's refills.
 //   4. xc_enc_scan_kernel    exclusive scan of record sizes -> chunk table and
 //                            blob length.
 //   5. xc_enc_compact_kernel copy every record from its scratch slot into the
-//                            blob.
+//                            blob, 16 bytes per thread and pass.
 // Output bytes equal the CPU reference encoder's for the same input.
 #include <cstdint>
 
