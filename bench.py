@@ -237,8 +237,8 @@ def main():
                          "2^30-value tensor (fills every SM; ~3.5 GB on the device) for ncu captures; kv: BASELINE "
                          "config 5 (KV cache encode+decode); sweep: config 3 (coders x chunk size); "
                          "stream: config 4; mix: HBM calibration of the decode's read:write mix; "
-                         "legacy: the reference's serial formats (bf16_se_single_kernel, bf16_se_tans) "
-                         "on the config-1 tensor and on a batch of config-2 k/v tensors")
+                         "legacy: the reference's serial-stream formats (bf16_se_single_kernel, bf16_se_tans, "
+                         "bf16_parallel_v1) on the config-1 tensor and on a batch of config-2 k/v tensors")
     a = ap.parse_args()
     a.warmup = max(3, a.warmup)
     if a.prec is None:
@@ -703,10 +703,12 @@ def legacy_cpu_leg(kind: str, raws: list, threads: int):
 
 
 def bench_legacy(a, torch, dev, world, rank, dist, local):
-    """bf16_se_single_kernel / bf16_se_tans decoded on the device.  Case 1:
-    the BASELINE config-1 tensor (16.8M values; one serial (sign,exp) stream).
-    Case 2: 16 tensors of the config-2 k/v shape (1024x4096) in one plan, all
-    streams concurrent.  One JSON line per (codec, case)."""
+    """bf16_se_single_kernel / bf16_se_tans and the reference's GPU-oriented
+    bf16_parallel_v1 (N = 128 slices, its default) decoded on the device by
+    serial-stream plans.  Case 1: the BASELINE config-1 tensor (16.8M values;
+    one serial (sign,exp) stream, or 128 for bf16_parallel_v1).  Case 2: 16
+    tensors of the config-2 k/v shape (1024x4096) in one plan, all streams
+    concurrent.  One JSON line per (codec, case)."""
     import numpy as np
     from bigsmall_b200 import gpu
     if rank != 0:
@@ -722,7 +724,10 @@ def bench_legacy(a, torch, dev, world, rank, dist, local):
     kv = [gen_tensor(torch, gd, (1024, 4096), "linear", dev).view(torch.int16).cpu().numpy().tobytes()
           for _ in range(16)]
     stream = torch.cuda.current_stream(dev)
-    for kind, codec in (("sk", "bf16_se_single_kernel"), ("tans", "bf16_se_tans")):
+    # kernels per decode: the serial streams, then the legacy formats' segmented
+    # un-sort (histogram, scan, scatter) or bf16_parallel_v1's slice merge
+    launches = {"sk": 4, "tans": 4, "par": 2}
+    for kind, codec in (("sk", "bf16_se_single_kernel"), ("tans", "bf16_se_tans"), ("par", "bf16_parallel_v1")):
         for case, raws in (("config-1 tensor 4096x4096", [c1]), ("16 x config-2 k/v 1024x4096, one plan", kv)):
             blobs, cpu_s = legacy_cpu_leg(kind, raws, 1 if len(raws) == 1 else threads)
             entries, outs = [], []
@@ -743,7 +748,7 @@ def bench_legacy(a, torch, dev, world, rank, dist, local):
                                                "cores": 1 if len(raws) == 1 else threads, "kind": "port",
                                                "sample": "the same blobs, reference decoder restated in C"},
                               "ratio": round(sum(len(b) for b in blobs) / nbytes, 5),
-                              "gpu_launches_per_decode": 2, "verified": ok}), flush=True)
+                              "gpu_launches_per_decode": launches[kind], "verified": ok}), flush=True)
             plan.close()
 
 

@@ -35,6 +35,7 @@ CODER_TANS = 1
 CODER_RANS_PAIR = 2
 SE_SINGLE_KERNEL = 1
 SE_TANS = 2
+SE_PARALLEL = 3   # bf16_parallel_v1 blobs in a serial-format batch
 
 
 class XcTensor(ctypes.Structure):

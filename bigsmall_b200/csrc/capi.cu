@@ -904,6 +904,7 @@ int parse_serial(int codec, SerialLayout &L, const SerialBlob &B) {
     switch (codec) {
         case BS_SE_SINGLE_KERNEL: return parse_sk(L, B);
         case BS_SE_TANS: return parse_setans(L, B);
+        case BS_SE_PARALLEL: return parse_par1(L, B);
         default: return fail(BS_E_INVALID_ARG, "unknown legacy codec " + std::to_string(codec));
     }
 }
@@ -1010,7 +1011,7 @@ int bs_par_plan_create(const uint8_t *h, uint64_t len, uint64_t n_weights, const
 
 int bs_se_parse(int codec, const uint8_t *h, uint64_t len, uint64_t n_weights, uint32_t *n_jobs_out) {
     if (n_jobs_out) *n_jobs_out = 0;
-    if (codec != BS_SE_SINGLE_KERNEL && codec != BS_SE_TANS)
+    if (codec != BS_SE_SINGLE_KERNEL && codec != BS_SE_TANS && codec != BS_SE_PARALLEL)
         return fail(BS_E_INVALID_ARG, "unknown legacy codec " + std::to_string(codec));
     if (n_weights == 0 || len == 0) return BS_OK;
     if (!h) return fail(BS_E_INVALID_ARG, "host blob is NULL");
@@ -1034,9 +1035,9 @@ int bs_se_plan_create_many(const bs_se_blob *blobs, int n_blobs, int device, bs_
     for (int i = 0; i < n_blobs; i++) {
         const bs_se_blob &b = blobs[i];
         const std::string who = "blob " + std::to_string(i) + ": ";
-        if (b.codec != BS_SE_SINGLE_KERNEL && b.codec != BS_SE_TANS)
+        if (b.codec != BS_SE_SINGLE_KERNEL && b.codec != BS_SE_TANS && b.codec != BS_SE_PARALLEL)
             return fail(BS_E_INVALID_ARG, who + "unknown legacy codec " + std::to_string(b.codec));
-        // single_kernel.py:603-613 / bf16_tans.py:121-125: nothing to decode
+        // single_kernel.py:603-613 / bf16_tans.py:121-125 / bf16_parallel.py:268-269: nothing to decode
         if (b.n_weights == 0 || b.blob_bytes == 0) continue;
         if (!b.h_blob) return fail(BS_E_INVALID_ARG, who + "host blob is NULL");
         if (!b.d_blob || !b.d_out || !on_device(b.d_blob, device) || !on_device(b.d_out, device))

@@ -245,11 +245,13 @@ class ParPlan(_Plan):
 
 
 SE_CODECS = {"bf16_se_single_kernel": _lib.SE_SINGLE_KERNEL, "bf16_se_tans": _lib.SE_TANS}
+# every format decoded by serial streams, batchable in one SePlan
+SERIAL_CODECS = {**SE_CODECS, "bf16_parallel_v1": _lib.SE_PARALLEL}
 
 
 class SePlan(_Plan):
-    """Decode plan for blobs of the legacy serial formats (bf16_se_single_kernel,
-    bf16_se_tans).
+    """Decode plan for blobs of the serial-stream formats: the legacy
+    bf16_se_single_kernel / bf16_se_tans and the reference's bf16_parallel_v1.
 
     ``entries``: iterable of ``(codec, host_blob, d_blob, out, n_weights)``;
     the framing is parsed from ``host_blob`` (bytes identical to ``d_blob``,
@@ -262,8 +264,8 @@ class SePlan(_Plan):
         arr = (_lib.SeBlob * max(1, len(entries)))()
         keep, dev = [], device
         for i, (codec, host_blob, d_blob, out, n_weights) in enumerate(entries):
-            if codec not in SE_CODECS:
-                raise ValueError(f"not a legacy serial codec: {codec!r}")
+            if codec not in SERIAL_CODECS:
+                raise ValueError(f"not a serial-stream codec: {codec!r}")
             _as_cuda(out, "out")
             if out.element_size() != 2:
                 raise TypeError("out must be a 16-bit tensor (bfloat16)")
@@ -278,7 +280,7 @@ class SePlan(_Plan):
             if d != dev or (d_blob is not None and d_blob.numel() and _dev_index(d_blob) != dev):
                 raise ValueError("all tensors of a plan must live on one device")
             cbuf = ctypes.create_string_buffer(hb, len(hb)) if hb else None
-            arr[i].codec = SE_CODECS[codec]
+            arr[i].codec = SERIAL_CODECS[codec]
             arr[i].h_blob = ctypes.cast(cbuf, ctypes.c_void_p) if cbuf is not None else None
             arr[i].blob_bytes = len(hb)
             arr[i].n_weights = int(n_weights)
@@ -414,6 +416,6 @@ def sync(device=None) -> None:
 
 
 __all__: Sequence[str] = [
-    "DEFAULT_CHUNK_ELEMS", "DEFAULT_PREC", "DEFAULT_CODER", "SePlan", "decode_se_into", "SE_CODECS", "XcPlan", "ParPlan", "XcEncoder", "decode_xc_into",
+    "DEFAULT_CHUNK_ELEMS", "DEFAULT_PREC", "DEFAULT_CODER", "SePlan", "decode_se_into", "SE_CODECS", "SERIAL_CODECS", "XcPlan", "ParPlan", "XcEncoder", "decode_xc_into",
     "decode_par_into", "encode_xc", "encode_bound", "encode_workspace", "xc_extras", "aligned_view",
 ]

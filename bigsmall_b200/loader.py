@@ -208,11 +208,7 @@ class DeviceLoader:
                     out = self.out[p.name].reshape(-1).view(torch.int16)
                     xc_entries.append((blob, out, ce, _ct.n_elements(m["shape"]), p.chunk_begin, p.chunk_count))
                     xc_coders.append((m.get("extra") or {}).get("coder"))
-                elif m["codec"] == "bf16_parallel_v1":
-                    n = _ct.n_elements(m["shape"])
-                    out = self.out[p.name].reshape(-1).view(torch.int16)
-                    g.plans.append(gpu.ParPlan(bytes(self.image.blob_host(p.name)), blob, out, n))
-                elif m["codec"] in gpu.SE_CODECS:
+                elif m["codec"] in gpu.SERIAL_CODECS:
                     n = _ct.n_elements(m["shape"])
                     out = self.out[p.name].reshape(-1).view(torch.int16)
                     se_entries.append((m["codec"], bytes(self.image.blob_host(p.name)), blob, out, n))
@@ -221,7 +217,7 @@ class DeviceLoader:
                     if dst.numel() != nb:
                         raise ValueError(f"raw tensor {p.name}: {nb} bytes for {dst.numel()}")
                     g.copies.append((dst, blob))
-            if se_entries:   # legacy serial tensors of the group: one plan, streams concurrent
+            if se_entries:   # serial-stream tensors of the group: one plan, all streams concurrent
                 g.plans.append(gpu.SePlan(se_entries, device=self.device.index))
             if xc_entries:
                 g.plans.insert(0, gpu.XcPlan(xc_entries, device=self.device.index, coders=xc_coders))
@@ -424,10 +420,7 @@ class ResidentContainer:
             if m["codec"] == "bf16_exp_chunked_v1":
                 xc.append((blob, flat.view(torch.int16), int((m.get("extra") or {})["chunk_elems"])))
                 coders.append((m.get("extra") or {}).get("coder"))
-            elif m["codec"] == "bf16_parallel_v1":
-                plans.append(gpu.ParPlan(bytes(self.image.blob_host(real)), blob, flat.view(torch.int16),
-                                         _ct.n_elements(m["shape"])))
-            elif m["codec"] in gpu.SE_CODECS:
+            elif m["codec"] in gpu.SERIAL_CODECS:
                 se.append((m["codec"], bytes(self.image.blob_host(real)), blob, flat.view(torch.int16),
                            _ct.n_elements(m["shape"])))
             else:   # raw

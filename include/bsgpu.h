@@ -168,6 +168,10 @@ int bs_par_plan_create(const uint8_t *h_blob, uint64_t blob_bytes,
  *           bigsmall/codecs/bf16_tans.py:121-167 + numba_rans.py:168-217. */
 #define BS_SE_SINGLE_KERNEL 1
 #define BS_SE_TANS          2
+/* bf16_parallel_v1 blobs in a bs_se_plan_create_many batch: their N slice
+ * streams join the batch's concurrent streams (one bs_par_plan_create per
+ * tensor runs its tensors one after another). */
+#define BS_SE_PARALLEL      3
 int bs_se_plan_create(int codec, const uint8_t *h_blob, uint64_t blob_bytes,
                       uint64_t n_weights, const void *d_blob, void *d_out,
                       int device, bs_plan **out_plan);
@@ -175,7 +179,7 @@ int bs_se_plan_create(int codec, const uint8_t *h_blob, uint64_t blob_bytes,
  * so a batch decodes in the time of its longest (sign,exp) stream; one status
  * word per blob.  `h_blob` holds the same bytes as `d_blob`. */
 typedef struct bs_se_blob {
-    int            codec;        /* BS_SE_SINGLE_KERNEL or BS_SE_TANS */
+    int            codec;        /* BS_SE_SINGLE_KERNEL, BS_SE_TANS or BS_SE_PARALLEL */
     const uint8_t *h_blob;
     uint64_t       blob_bytes;
     uint64_t       n_weights;

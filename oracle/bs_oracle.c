@@ -1417,3 +1417,8 @@ int bso_xc_decode_many(const uint8_t *const *blobs, const int64_t *lens, const i
                        uint16_t *const *outs, int count, int threads) {
     return run_pool(bso_xc_decode, blobs, lens, n_weights, outs, count, threads);
 }
+
+int bso_par_decode_many(const uint8_t *const *blobs, const int64_t *lens, const int64_t *n_weights,
+                        uint16_t *const *outs, int count, int threads) {
+    return run_pool(bso_par_decode, blobs, lens, n_weights, outs, count, threads);
+}

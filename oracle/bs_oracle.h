@@ -86,6 +86,9 @@ int bso_tans_decode_many(const uint8_t *const *blobs, const int64_t *lens,
 int bso_xc_decode_many(const uint8_t *const *blobs, const int64_t *lens,
                        const int64_t *n_weights, uint16_t *const *outs,
                        int count, int threads);
+int bso_par_decode_many(const uint8_t *const *blobs, const int64_t *lens,
+                        const int64_t *n_weights, uint16_t *const *outs,
+                        int count, int threads);
 
 #ifdef __cplusplus
 }

@@ -70,6 +70,7 @@ def lib():
         "bso_xc_decode": (I32, [P, I64, I64, P]),
         "bso_xc_quantise": (I32, [P, I32, P]),
         "bso_xc_decode_many": (I32, [P, P, P, P, I32, I32]),
+        "bso_par_decode_many": (I32, [P, P, P, P, I32, I32]),
     }
     for name, (res, args) in sigs.items():
         fn = getattr(L, name)
@@ -189,7 +190,7 @@ def xc_quantise(counts, prec: int = 12) -> np.ndarray:
 
 
 def decode_many(kind: str, blobs, n_weights, threads: int) -> list[np.ndarray]:
-    """Decode many blobs on `threads` host threads (kind 'sk', 'tans' or 'xc')."""
+    """Decode many blobs on `threads` host threads (kind 'sk', 'tans', 'xc' or 'par')."""
     arrs = [_blob(b) for b in blobs]
     outs = [np.empty(max(int(n), 1), dtype=np.uint16) for n in n_weights]
     cnt = len(arrs)

@@ -64,3 +64,30 @@ def test_errors_mirror_reference():
     with pytest.raises(BsCorruptError):
         _gpu_par(blob[:100], 8192)
     assert _gpu_par(b"", 0) == b""
+
+
+def test_batched_serial_plan_mixes_parallel_and_legacy_blobs(manifest):
+    """Every golden case as bf16_parallel_v1 (N = 1, 32, 128), bf16_se_single_kernel
+    and bf16_se_tans blobs, all in ONE serial-format plan (BS_SE_PARALLEL next
+    to the legacy codecs): all streams run concurrently, every output is the
+    reference's decode."""
+    from bigsmall_b200 import gpu
+    kinds = (("par1", "bf16_parallel_v1"), ("par32", "bf16_parallel_v1"), ("par128", "bf16_parallel_v1"),
+             ("sk", "bf16_se_single_kernel"), ("tans", "bf16_se_tans"))
+    entries, want = [], []
+    for name, c in manifest["cases"].items():
+        raw = golden_bytes(f"{name}.raw")
+        for key, codec in kinds:
+            blob = golden_bytes(c["blobs"][key]["file"])
+            d = (torch.from_numpy(np.frombuffer(blob, dtype=np.uint8).copy()).cuda() if blob
+                 else torch.empty(0, dtype=torch.uint8, device="cuda"))
+            o = torch.empty(max(c["n"], 1), dtype=torch.int16, device="cuda")
+            entries.append((codec, blob, d, o, c["n"]))
+            want.append(raw)
+    with gpu.SePlan(entries) as p:
+        for _ in range(2):      # plans are reusable
+            for e in entries:
+                e[3].fill_(0)
+            p.run()
+            for (codec, _, _, o, n), raw in zip(entries, want):
+                assert o[:n].cpu().view(torch.uint8).numpy().tobytes() == raw, codec

@@ -81,3 +81,24 @@ def test_single_kernel_frequency_sum_enforced():
     assert _parse("sk", bytes(blob), 3000)[0] == _lib.BS_E_CORRUPT
     with pytest.raises(O.OracleError):
         O.sk_decode(bytes(blob), 3000)
+
+
+@pytest.mark.parametrize("key,ns", [("par1", 1), ("par32", 32), ("par128", 128)])
+def test_golden_parallel_blobs_parse_in_serial_plans(manifest, key, ns):
+    """bf16_parallel_v1 (BS_SE_PARALLEL in a serial-format batch): one (sign,
+    exp) stream per non-empty slice k::N plus one per exponent bucket of the
+    slice (bigsmall/codecs/bf16_parallel.py:262-352)."""
+    from bigsmall_b200 import _lib
+    L = _lib.load()
+    for name, c in manifest["cases"].items():
+        blob = golden_bytes(c["blobs"][key]["file"])
+        w = np.frombuffer(golden_bytes(f"{name}.raw"), dtype=np.uint16)
+        want = sum(1 + len(np.unique((w[k::ns] >> 7) & 0xFF)) for k in range(ns) if len(w[k::ns]))
+        out = ctypes.c_uint32()
+        buf = ctypes.create_string_buffer(blob, len(blob)) if blob else None
+        rc = L.bs_se_parse(_lib.SE_PARALLEL, buf, len(blob), c["n"], ctypes.byref(out))
+        assert rc == 0, (name, rc)
+        assert out.value == (want if c["n"] else 0), (name, out.value, want)
+        if c["n"]:
+            assert L.bs_se_parse(_lib.SE_PARALLEL, buf, len(blob), c["n"] + 1,
+                                 ctypes.byref(out)) == _lib.BS_E_COUNT_MISMATCH
