@@ -245,3 +245,28 @@ def test_handoff_call_chains_both_streams():
             torch.cuda.synchronize()
             assert got.cpu().view(torch.uint8).numpy().tobytes() == raw
         p.check()
+
+
+def test_tensor_past_2_32_values_round_trips():
+    """Maximum size: one tensor of 2^32 + 1001 values (every element offset
+    past 32 bits; odd, so the last pair is ragged), encoded and decoded on the
+    device with the defaults, bit-exact, header count intact.  The reference's
+    formats carry a u32 count; this one a u64.  About 40 GB of HBM."""
+    from bigsmall_b200 import gpu
+    free, _ = torch.cuda.mem_get_info()
+    if free < 48 * 2 ** 30:
+        pytest.skip("needs about 40 GB of free device memory")
+    n = (1 << 32) + 1001
+    x = torch.empty(n, dtype=torch.bfloat16, device="cuda")
+    g = torch.Generator(device="cuda").manual_seed(7)
+    step = 1 << 28
+    for i in range(0, n, step):
+        m = min(step, n - i)
+        x[i:i + m] = (torch.randn(m, generator=g, device="cuda") * 0.02).to(torch.bfloat16)
+    blob = gpu.encode_xc(x)
+    assert struct.unpack_from("<Q", blob[:16].cpu().numpy().tobytes(), 8)[0] == n
+    out = torch.empty_like(x)
+    gpu.decode_xc_into(blob, out, gpu.DEFAULT_CHUNK_ELEMS)
+    assert torch.equal(out.view(torch.int16), x.view(torch.int16))
+    del x, out, blob
+    torch.cuda.empty_cache()
