@@ -5,7 +5,6 @@ from __future__ import annotations
 
 import hashlib
 
-import numpy as np
 import pytest
 
 torch = pytest.importorskip("torch")
