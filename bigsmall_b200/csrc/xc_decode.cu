@@ -70,6 +70,15 @@ __device__ __forceinline__ uint32_t lds_u32(uint32_t a) {
 }
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;\n" ::: "memory"); }
+// wait until at most `pending` (0..3) of this thread's newest copy groups are in flight
+__device__ __forceinline__ void cp_async_wait_pending(uint32_t pending) {
+    switch (pending) {
+        case 0: asm volatile("cp.async.wait_group 0;\n" ::: "memory"); break;
+        case 1: asm volatile("cp.async.wait_group 1;\n" ::: "memory"); break;
+        case 2: asm volatile("cp.async.wait_group 2;\n" ::: "memory"); break;
+        default: asm volatile("cp.async.wait_group 3;\n" ::: "memory"); break;
+    }
+}
 
 __device__ __forceinline__ uint2 ld_plane8(const uint8_t *p) {
     uint2 v;
@@ -487,9 +496,13 @@ __device__ __forceinline__ void pair_ring_ensure(Ring &r, uint32_t consumed_byte
     uint32_t need = consumed_bytes + kPairMirror;
     if (need > r.bytes) need = r.bytes;
     if (need > r.landed) {
-        cp_async_wait_all();
+        // one copy group per kFill bytes, committed in order: the newest
+        // (fetched - need) / kFill groups may stay in flight
+        uint32_t pending = r.fetched > need ? (r.fetched - need) / kFill : 0u;
+        if (pending > 3) pending = 3;
+        cp_async_wait_pending(pending);
         __syncwarp();
-        r.landed = r.fetched;
+        r.landed = r.fetched - pending * kFill;
     }
 }
 
