@@ -546,8 +546,8 @@ __device__ __forceinline__ void decode_chunk_pair(uint32_t tab_s, uint8_t *ring_
     const uint32_t lt = lanemask_lt();
     const uint32_t smask = (1u << P) - 1;
     const uint32_t ring_s = static_cast<uint32_t>(__cvta_generic_to_shared(ring_buf));
-    if (rec_bytes == 0) {   // bad chunk offset table entry
-        if (lane == 0) atomicOr(err, BS_DEV_CHUNK_TABLE);
+    if (rec_bytes < kXcPairRecHdr) {   // bad chunk offset table entry, or a record too short for its header
+        if (lane == 0) atomicOr(err, rec_bytes ? BS_DEV_STREAM : BS_DEV_CHUNK_TABLE);
         return;
     }
     const uint32_t *rec32 = reinterpret_cast<const uint32_t *>(rec);

@@ -128,6 +128,9 @@ def test_corrupt_pair_records_raise_without_fault():
     b = bytearray(good); struct.pack_into("<I", b, co + 136, 1); variants["reserved"] = (bytes(b), 0x08)
     b = bytearray(good); b[co + 3] ^= 0x40; variants["lane_state"] = (bytes(b), 0x18)
     b = bytearray(good); struct.pack_into("<I", b, co + 128, 1 << 20); variants["n_words"] = (bytes(b), 0x08)
+    # chunk 0's record cut to 128 bytes, shorter than its own 144-byte header
+    b = bytearray(good); struct.pack_into("<I", b, 576 + 4, struct.unpack_from("<I", good, 576)[0] + 8)
+    variants["short_record"] = (bytes(b), 0x08)
     for name, (blob, bits) in variants.items():
         out = torch.empty(n, dtype=torch.bfloat16, device="cuda")
         with pytest.raises(BsCorruptError) as ei:
