@@ -85,6 +85,8 @@ struct bs_plan {
     // serial-stream formats (bf16_parallel_v1, bf16_se_single_kernel, bf16_se_tans)
     ParJob *d_jobs = nullptr;
     int n_jobs = 0;
+    uint2 *d_groups = nullptr;   // {first job, job count}: jobs sharing a decode table
+    int n_groups = 0;
     ParStream *d_streams = nullptr;
     int n_streams_total = 0;
     uint2 *d_buckets = nullptr;
@@ -296,7 +298,8 @@ static int plan_decode(bs_plan *p, void *stream, void *ev_start, void *ev_stop) 
         if (p->n_internal > 0) {
             if (e == cudaSuccess) e = cudaMemsetAsync(p->d_errs, 0, 4ull * p->n_internal, s);
             if (e == cudaSuccess)
-                e = launch_par_jobs(p->d_jobs, p->n_jobs, p->d_tabs, p->d_syms, p->d_se_sym, p->d_mant, p->d_errs, s);
+                e = launch_par_jobs(p->d_jobs, p->n_jobs, p->d_groups, p->n_groups, p->d_tabs, p->d_syms,
+                                    p->d_se_sym, p->d_mant, p->d_errs, s);
             if (e == cudaSuccess)
                 e = launch_par_merge(p->d_streams, p->n_streams_total, p->d_buckets, p->d_se_sym, p->d_mant,
                                      p->d_errs, s);
@@ -913,7 +916,38 @@ int parse_serial(int codec, SerialLayout &L, const SerialBlob &B) {
 // tensors; u2i maps them to status words (-1: nothing to decode).
 int make_serial_plan(SerialLayout &L, int device, int n_tensors, std::vector<int> u2i, int n_internal,
                      bs_plan **out_plan) {
-    std::stable_sort(L.jobs.begin(), L.jobs.end(), [](const ParJob &x, const ParJob &y) { return x.n_syms > y.n_syms; });
+    // Two schedules for the serial streams.  One stream per CTA (longest
+    // first) runs each chain fastest but holds a 40 KiB table per stream, so
+    // at most par_jobs_slots() run at once; streams sharing a table (the
+    // slices of a bf16_parallel_v1 tensor) can instead run one per warp,
+    // kJobGroup per CTA, at a per-chain cost measured 16 % higher.  Pick the
+    // smaller estimated makespan: max(longest stream, symbols in flight / slots).
+    std::stable_sort(L.jobs.begin(), L.jobs.end(), [](const ParJob &x, const ParJob &y) {
+        return x.tab_off != y.tab_off ? x.tab_off < y.tab_off : x.n_syms > y.n_syms;
+    });
+    std::vector<uint2> groups;
+    double longest = 0, total = 0, group_total = 0;
+    for (size_t i = 0; i < L.jobs.size(); i++) {
+        if (groups.empty() || L.jobs[i].tab_off != L.jobs[groups.back().x].tab_off || groups.back().y == kJobGroup) {
+            groups.push_back(make_uint2(static_cast<uint32_t>(i), 0));
+            group_total += L.jobs[i].n_syms;   // a group holds its CTA for its longest stream
+        }
+        groups.back().y++;
+        longest = std::max(longest, static_cast<double>(L.jobs[i].n_syms));
+        total += L.jobs[i].n_syms;
+    }
+    const double slots = L.jobs.empty() ? 1.0 : static_cast<double>(par_jobs_slots());
+    const double t_single = std::max(longest, total / slots);
+    const double t_grouped = 1.16 * std::max(longest, group_total / slots);
+    if (groups.size() < L.jobs.size() && t_grouped < t_single) {
+        std::stable_sort(groups.begin(), groups.end(), [&](const uint2 &a, const uint2 &b) {
+            return L.jobs[a.x].n_syms > L.jobs[b.x].n_syms;
+        });
+    } else {
+        groups.clear();
+        std::stable_sort(L.jobs.begin(), L.jobs.end(),
+                         [](const ParJob &x, const ParJob &y) { return x.n_syms > y.n_syms; });
+    }
     if (L.jobs.size() > 0x7FFFFFFFull || L.streams.size() > 0x7FFFFFFFull || L.seg_stream.size() > 0x7FFFFFFFull)
         return fail(BS_E_INVALID_ARG, "too many streams");
     auto *p = new bs_plan();
@@ -928,6 +962,7 @@ int make_serial_plan(SerialLayout &L, int device, int n_tensors, std::vector<int
     }
     Carve cv;
     const uint64_t o_j = cv.take(sizeof(ParJob) * L.jobs.size());
+    const uint64_t o_g = cv.take(sizeof(uint2) * groups.size());
     const uint64_t o_s = cv.take(sizeof(ParStream) * L.streams.size());
     const uint64_t o_b = cv.take(sizeof(uint2) * std::max<size_t>(1, L.buckets.size()));
     const uint64_t o_t = cv.take(sizeof(uint2) * std::max<size_t>(1, L.tabs.size()));
@@ -943,6 +978,8 @@ int make_serial_plan(SerialLayout &L, int device, int n_tensors, std::vector<int
     auto *base = static_cast<uint8_t *>(p->d_mem);
     p->d_jobs = reinterpret_cast<ParJob *>(base + o_j);
     p->n_jobs = static_cast<int>(L.jobs.size());
+    p->d_groups = reinterpret_cast<uint2 *>(base + o_g);
+    p->n_groups = static_cast<int>(groups.size());
     p->d_streams = reinterpret_cast<ParStream *>(base + o_s);
     p->n_streams_total = static_cast<int>(L.streams.size());
     p->d_buckets = reinterpret_cast<uint2 *>(base + o_b);
@@ -961,6 +998,7 @@ int make_serial_plan(SerialLayout &L, int device, int n_tensors, std::vector<int
         if (e == cudaSuccess && bytes) e = cudaMemcpy(dst, src, bytes, cudaMemcpyHostToDevice);
     };
     up(p->d_jobs, L.jobs.data(), sizeof(ParJob) * L.jobs.size());
+    up(p->d_groups, groups.data(), sizeof(uint2) * groups.size());
     up(p->d_streams, L.streams.data(), sizeof(ParStream) * L.streams.size());
     up(p->d_buckets, L.buckets.data(), sizeof(uint2) * L.buckets.size());
     up(p->d_tabs, L.tabs.data(), sizeof(uint2) * L.tabs.size());

@@ -170,8 +170,13 @@ cudaError_t launch_xc_noalloc(const XcTensorDev *h_tens, const uint32_t *range_c
                               uint32_t *h_status);
 uint64_t xc_noalloc_scratch_bytes();
 
-cudaError_t launch_par_jobs(const ParJob *d_jobs, int n_jobs, const uint2 *d_tabs, const uint16_t *d_syms,
-                            uint16_t *d_se_sym, uint8_t *d_mant, uint32_t *d_errs, cudaStream_t s);
+// The serial streams: one per CTA (n_groups == 0), or one per warp in groups
+// d_groups[g] = {first job, job count <= kJobGroup} of jobs sharing one table.
+cudaError_t launch_par_jobs(const ParJob *d_jobs, int n_jobs, const uint2 *d_groups, int n_groups,
+                            const uint2 *d_tabs, const uint16_t *d_syms, uint16_t *d_se_sym, uint8_t *d_mant,
+                            uint32_t *d_errs, cudaStream_t s);
+constexpr uint32_t kJobGroup = 4;   // serial streams per CTA of par_groups_kernel: one per warp
+int par_jobs_slots();               // concurrent CTAs of the job kernels on the current device
 cudaError_t launch_seg_merge(const SegStream *d_ss, int n_ss, const uint32_t *d_seg_stream, int n_segs,
                              uint32_t *d_hist, const uint2 *d_buckets, const uint16_t *d_se_sym,
                              const uint8_t *d_mant, uint32_t *d_errs, cudaStream_t s);

@@ -31,7 +31,7 @@ __device__ __forceinline__ uint32_t lanemask_lt_p() {
     return m;
 }
 
-constexpr int kJobThreads = 128;
+constexpr int kJobThreads = 32 * static_cast<int>(kJobGroup);
 
 __device__ __forceinline__ uint2 lds_entry(uint32_t a) {
     uint2 v;
@@ -119,6 +119,65 @@ __global__ void __launch_bounds__(kJobThreads) par_jobs_kernel(const ParJob *__r
     }
     __syncthreads();
     if (threadIdx.x != 0) return;
+    const uint8_t *d = reinterpret_cast<const uint8_t *>(J.data);
+    const uint32_t avail = J.avail, n_words = J.n_words;
+    uint32_t state, w = 0;
+    if (J.flags & kJobStateInStream) {
+        if (n_words < 2) {   // rans.py:176-177 / numba_rans: a stream shorter than its state
+            atomicOr(&errs[J.tensor], BS_DEV_STREAM);
+            return;
+        }
+        auto word = [&](uint32_t k) -> uint32_t {
+            const uint32_t i = 2 * k;
+            return (i < avail ? static_cast<uint32_t>(d[i]) : 0u) |
+                   (i + 1 < avail ? static_cast<uint32_t>(d[i + 1]) << 8 : 0u);
+        };
+        state = word(0) | (word(1) << 16);
+        w = 2;
+    } else {
+        state = J.state0;
+    }
+    const uint32_t tab_s = static_cast<uint32_t>(__cvta_generic_to_shared(s_tab));
+    const uint32_t sym_s = static_cast<uint32_t>(__cvta_generic_to_shared(s_sym));
+    const bool slow = (J.flags & kJobSlowRenorm) != 0;
+    if (is_se) {
+        if (slow) serial_stream<12, true>(tab_s, sym_s, d, avail, n_words, w, state, J.n_syms, se_sym + J.out_off);
+        else serial_stream<12, false>(tab_s, sym_s, d, avail, n_words, w, state, J.n_syms, se_sym + J.out_off);
+    } else {
+        if (slow) serial_stream<10, true>(tab_s, sym_s, d, avail, n_words, w, state, J.n_syms, mant + J.out_off);
+        else serial_stream<10, false>(tab_s, sym_s, d, avail, n_words, w, state, J.n_syms, mant + J.out_off);
+    }
+}
+
+// One CTA per group of up to kJobGroup serial streams that share a decode
+// table (all slices of a bf16_parallel_v1 tensor share its (sign,exp) table
+// and, per exponent, its mantissa table; a legacy stream has its own): the
+// CTA stages the table (slot -> {freq, slot - cum} and slot -> symbol) in
+// shared memory once, then one lane of each warp runs one stream (a stream
+// per lane would diverge on every renorm).  The state stays below 2^32
+// because the host rejects tables with a frequency above M, so 32-bit
+// arithmetic is exact.
+__global__ void __launch_bounds__(kJobThreads) par_groups_kernel(const ParJob *__restrict__ jobs,
+                                                                 const uint2 *__restrict__ groups,
+                                                               const uint2 *__restrict__ tabs,
+                                                               const uint16_t *__restrict__ syms,
+                                                               uint16_t *__restrict__ se_sym,
+                                                               uint8_t *__restrict__ mant, uint32_t *errs) {
+    extern __shared__ __align__(16) uint8_t s_mem[];
+    uint2 *s_tab = reinterpret_cast<uint2 *>(s_mem);
+    uint16_t *s_sym = reinterpret_cast<uint16_t *>(s_mem + 4096 * sizeof(uint2));
+    const uint2 G = groups[blockIdx.x];   // {first job, jobs (<= kJobGroup)}
+    const uint32_t warp = threadIdx.x >> 5;
+    const bool runs = warp < G.y && (threadIdx.x & 31) == 0;
+    const ParJob J = jobs[G.x + (warp < G.y ? warp : 0u)];   // every job of the group has the same table
+    const bool is_se = (J.flags & kJobSe) != 0;
+    const uint32_t M = is_se ? 4096u : 1024u;
+    for (uint32_t i = threadIdx.x; i < M; i += kJobThreads) {
+        s_tab[i] = tabs[J.tab_off + i];
+        s_sym[i] = syms[J.tab_off + i];
+    }
+    __syncthreads();
+    if (!runs || J.n_syms == 0) return;
     const uint8_t *d = reinterpret_cast<const uint8_t *>(J.data);
     const uint32_t avail = J.avail, n_words = J.n_words;
     uint32_t state, w = 0;
@@ -327,12 +386,30 @@ __global__ void __launch_bounds__(kMergeWarps * 32) par_merge_kernel(
     }
 }
 
-cudaError_t launch_par_jobs(const ParJob *d_jobs, int n_jobs, const uint2 *d_tabs, const uint16_t *d_syms,
-                            uint16_t *d_se_sym, uint8_t *d_mant, uint32_t *d_errs, cudaStream_t s) {
-    if (n_jobs <= 0) return cudaSuccess;
+// Concurrent CTAs of the job kernels on the current device (40 KiB of shared
+// memory each).
+int par_jobs_slots() {
+    int dev = 0, sms = 1, per_sm = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, par_jobs_kernel, kJobThreads,
+                                                      4096 * (sizeof(uint2) + sizeof(uint16_t))) != cudaSuccess)
+        cudaGetLastError();
+    return sms * (per_sm > 0 ? per_sm : 1);
+}
+
+cudaError_t launch_par_jobs(const ParJob *d_jobs, int n_jobs, const uint2 *d_groups, int n_groups,
+                            const uint2 *d_tabs, const uint16_t *d_syms, uint16_t *d_se_sym, uint8_t *d_mant,
+                            uint32_t *d_errs, cudaStream_t s) {
     // 40 KiB: the larger (SE, 4096-slot) tables; below the 48 KiB default limit
-    par_jobs_kernel<<<n_jobs, kJobThreads, 4096 * (sizeof(uint2) + sizeof(uint16_t)), s>>>(
-        d_jobs, d_tabs, d_syms, d_se_sym, d_mant, d_errs);
+    const size_t smem = 4096 * (sizeof(uint2) + sizeof(uint16_t));
+    if (n_groups > 0) {
+        par_groups_kernel<<<n_groups, kJobThreads, smem, s>>>(d_jobs, d_groups, d_tabs, d_syms, d_se_sym, d_mant,
+                                                              d_errs);
+    } else {
+        if (n_jobs <= 0) return cudaSuccess;
+        par_jobs_kernel<<<n_jobs, kJobThreads, smem, s>>>(d_jobs, d_tabs, d_syms, d_se_sym, d_mant, d_errs);
+    }
     return cudaGetLastError();
 }
 

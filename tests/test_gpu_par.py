@@ -91,3 +91,25 @@ def test_batched_serial_plan_mixes_parallel_and_legacy_blobs(manifest):
             p.run()
             for (codec, _, _, o, n), raw in zip(entries, want):
                 assert o[:n].cpu().view(torch.uint8).numpy().tobytes() == raw, codec
+
+
+def test_many_parallel_tensors_take_the_grouped_schedule():
+    """16 bf16_parallel_v1 tensors of 2^20 values (N = 128) in one serial-stream
+    plan: 2,048 slice streams sharing 16 (sign,exp) tables plus their bucket
+    streams, about 32M symbols -- far more than the job kernel's CTA slots can
+    hold one stream each, so the plan's cost model runs table-sharing streams
+    one per warp.  Every output must equal the reference decode."""
+    from bigsmall_b200 import gpu
+    n = 1 << 20
+    raws, entries = [], []
+    for k in range(16):
+        g = torch.Generator().manual_seed(100 + k)
+        raw = (torch.randn(n, generator=g) * 0.02).to(torch.bfloat16).view(torch.uint8).numpy().tobytes()
+        blob = O.par_encode(raw, 128)
+        d = torch.from_numpy(np.frombuffer(blob, dtype=np.uint8).copy()).cuda()
+        entries.append(("bf16_parallel_v1", blob, d, torch.empty(n, dtype=torch.int16, device="cuda"), n))
+        raws.append(raw)
+    with gpu.SePlan(entries) as p:
+        p.run()
+    for (_, _, _, o, _), raw in zip(entries, raws):
+        assert o.cpu().view(torch.uint8).numpy().tobytes() == raw
