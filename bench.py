@@ -681,7 +681,7 @@ def bench_mix(a, torch, dev, world, rank, dist, local):
 
 
 # ---------------------------------------------------------------------------
-# legacy serial formats on the device (SURVEY rank-4 row), with their CPU leg
+# serial-stream formats on the device (legacy bf16_se_*, bf16_parallel_v1), with their CPU leg
 # ---------------------------------------------------------------------------
 def legacy_cpu_leg(kind: str, raws: list, threads: int):
     """cpu_baseline leg of --config legacy: the reference's encoder for the
