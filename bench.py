@@ -1,10 +1,11 @@
-"""Benchmark: full-container bf16 decode on B200.
+"""Benchmark: full-container bf16 decode on B200 (benchmark configuration 2).
 
 Workload: a Llama-3-8B-shaped random-init bf16 container (32 layers, hidden
 4096, q/o 4096x4096, k/v 1024x4096, gate/up 14336x4096, down 4096x14336,
 embed + lm_head 128256x4096, RMSNorm 1.0+N(0,0.01), linear N(0, 1/sqrt(fan_in)),
 one CUDA generator seeded 0, tensors generated in name order), ~8.03 G values
-(16.06 GB of bf16), encoded on the device with bf16_exp_chunked_v1 (rANS).
+(16.06 GB of bf16), encoded on the device with bf16_exp_chunked_v1 (default
+coder: rANS over exponent pairs, 32,768-value chunks).
 
 One step = decode the whole container (this rank's share of it) into HBM.
   value : decoded bf16 GB/s with the compressed bytes already in HBM
@@ -234,7 +235,7 @@ def main():
                                                       "legacy"],
                     help="c2: the benchmark workload; small: one 2^27-value tensor of the same "
                          "distribution (compressed ~170 MB, above L2) for ncu captures; medium: one "
-                         "2^30-value tensor (fills every SM; ~3.5 GB on the device) for ncu captures; kv: BASELINE "
+                         "2^30-value tensor (fills every SM; ~3.5 GB on the device) for ncu captures; kv: "
                          "config 5 (KV cache encode+decode); sweep: config 3 (coders x chunk size); "
                          "stream: config 4; mix: HBM calibration of the decode's read:write mix; "
                          "legacy: the reference's serial-stream formats (bf16_se_single_kernel, bf16_se_tans, "
