@@ -16,6 +16,10 @@ Formats decoded on the device:
   * ``bf16_se_single_kernel`` / ``bf16_se_tans`` -- the reference's serial
     formats, bit-exact (one serial stream per tensor).
 
+Several GPUs: ``sharding`` cuts a container into per-rank chunk spans (decode
+needs no communication) and ``replicate`` materialises the whole model on
+every rank afterwards when wanted (NCCL point-to-point).
+
 Top-level names follow BigSmall ``bigsmall/__init__.py`` for the decode path
 (``decompress``, ``load``, ``verify``, ``info``, ``StreamingLoader``,
 ``BigSmallStreamingModel``) and are imported on first use, so importing the
