@@ -31,10 +31,14 @@ def partition(tensors: Iterable[Sequence], world: int, chunk_elems: int) -> Tupl
 
 
 def partition_chunks(tensors: Iterable[Tuple[str, int, int]], world: int) -> Tuple[List[Owned], List[int]]:
-    """As ``partition`` with a chunk size per tensor: (name, n_values, chunk_elems)."""
+    """As ``partition`` with a chunk size per tensor: (name, n_values, chunk_elems);
+    a tensor that cannot be split passes chunk_elems = n (or 0) and is owned whole."""
     if world < 1:
         raise ValueError(f"world must be >= 1, got {world}")
-    items = [(name, n, ce, -(-n // ce)) for name, n, ce in tensors]
+    items = []
+    for name, n, ce in tensors:
+        ce = int(ce) if ce else max(int(n), 1)
+        items.append((name, n, ce, max(1, -(-n // ce))))   # an empty tensor is still owned once
     total = sum(n for _, n, _, _ in items)
     owned: List[Owned] = [[] for _ in range(world)]
     load = [0] * world
@@ -62,10 +66,17 @@ def partition_chunks(tensors: Iterable[Tuple[str, int, int]], world: int) -> Tup
 
 
 def owned_for(header: dict, rank: int, world: int) -> Owned:
-    """Rank ``rank``'s share of a container header's bf16_exp_chunked_v1
-    tensors (container order); other codecs are not chunked and are left out."""
+    """Rank ``rank``'s share of a container header's tensors (container order):
+    bf16_exp_chunked_v1 tensors by chunk spans, every other stored tensor whole
+    (``tied_ref`` entries hold no data and go to no rank; a loader resolves
+    them to their master)."""
     if not 0 <= rank < world:
         raise ValueError(f"rank {rank} outside world {world}")
-    items = [(t["name"], _count(t["shape"]), int(t["extra"]["chunk_elems"]))
-             for t in header["tensors"] if t.get("codec") == "bf16_exp_chunked_v1"]
+    items = []
+    for t in header["tensors"]:
+        codec = t.get("codec")
+        if codec == "tied_ref":
+            continue
+        n = _count(t["shape"])
+        items.append((t["name"], n, int(t["extra"]["chunk_elems"]) if codec == "bf16_exp_chunked_v1" else 0))
     return partition_chunks(items, world)[0][rank]

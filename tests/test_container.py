@@ -93,7 +93,11 @@ def test_owned_for_header_mixed_chunk_sizes():
     sizes = [(f"t{i}", n, ce) for i, (n, ce) in
              enumerate([(5_000_000, 32768), (123_457, 65536), (40_000_000, 32768), (4096, 256), (9_999_999, 65536)])]
     hdr = {"tensors": [{"name": nm, "shape": [n], "codec": "bf16_exp_chunked_v1", "extra": {"chunk_elems": ce}}
-                       for nm, n, ce in sizes] + [{"name": "raw", "shape": [7], "codec": "raw", "extra": {}}]}
+                       for nm, n, ce in sizes] + [
+        {"name": "raw", "shape": [7], "codec": "raw", "extra": {}},
+        {"name": "par", "shape": [3000, 1000], "codec": "bf16_parallel_v1", "extra": {}},
+        {"name": "empty", "shape": [0], "codec": "raw", "extra": {}},
+        {"name": "tied", "shape": [7], "codec": "tied_ref", "extra": {"tied_to": "raw"}}]}
     for world in (1, 2, 3, 5, 8):
         owned = [owned_for(hdr, r, world) for r in range(world)]
         _, load = partition_chunks(sizes, world)
@@ -106,6 +110,8 @@ def test_owned_for_header_mixed_chunk_sizes():
                 assert c0 == pos
                 pos += cc
             assert pos == nc
-        assert all(name != "raw" for r in owned for name, _, _ in r)
+        for whole in ("raw", "par", "empty"):   # unsplittable tensors: exactly one owner, whole
+            assert [(c0, cc) for r in owned for name, c0, cc in r if name == whole] == [(0, 0)]
+        assert all(name != "tied" for r in owned for name, _, _ in r)
     with pytest.raises(ValueError):
         owned_for(hdr, 2, 2)

@@ -69,6 +69,47 @@ def test_loader_pipelined_groups_and_tied(tmp_path):
     ld.close()
 
 
+def test_ranks_shares_cover_the_container(tmp_path):
+    """sharding.owned_for + DeviceLoader(owned=...) for every rank of 2- and
+    3-way partitions, run one after another on one GPU: chunked tensors split
+    by chunk spans, raw / bf16_parallel_v1 tensors whole on one rank, tied
+    aliases on none; together the ranks' outputs reproduce every tensor once."""
+    from bigsmall_b200 import container as C, gpu
+    from bigsmall_b200.loader import ContainerImage, DeviceLoader
+    from bigsmall_b200.sharding import owned_for
+    sd = _model(2)
+    w = C.ContainerWriter()
+    for k, v in sd.items():
+        if v.dtype == torch.bfloat16 and v.numel() >= 256:
+            blob = gpu.encode_xc(v.reshape(-1).cuda(), chunk_elems=256).cpu().numpy().tobytes()
+            w.add(k, v.shape, "BF16", "bf16_exp_chunked_v1", blob, "", gpu.xc_extras(256))
+        else:
+            raw = v.reshape(-1).view(torch.uint8).numpy().tobytes()
+            w.add(k, v.shape, {torch.bfloat16: "BF16", torch.int64: "I64"}[v.dtype], "raw", raw, "")
+    raw = golden_bytes("gauss_8k.raw")
+    w.add("ref.par", [8192], "BF16", "bf16_parallel_v1", O.par_encode(raw, 32), "", {"n_streams": 32})
+    w.add("lm_head.weight", [1000, 64], "BF16", "tied_ref", b"", "", {"tied_to": "model.embed_tokens.weight"})
+    img = ContainerImage.from_bytes(w.to_bytes())
+    want = {k: v.reshape(-1).view(torch.uint8).numpy().tobytes() for k, v in sd.items()}
+    want["ref.par"] = raw
+    for world in (2, 3):
+        got = {k: bytearray(len(b)) for k, b in want.items()}
+        seen = {k: 0 for k in want}
+        for rank in range(world):
+            owned = owned_for(img.header, rank, world)
+            assert all(name != "lm_head.weight" for name, _, _ in owned)
+            ld = DeviceLoader(img, device=0, owned=owned)
+            out = ld.run()
+            for name, c0, cc in owned:
+                b = out[name].reshape(-1).cpu().view(torch.uint8).numpy().tobytes()
+                lo = 2 * 256 * c0 if cc else 0
+                got[name][lo:lo + len(b)] = b
+                seen[name] += len(b)
+            ld.close()
+        for k in want:
+            assert seen[k] == len(want[k]) and bytes(got[k]) == want[k], (world, k)
+
+
 def test_unknown_codec_raises_version_error():
     from bigsmall_b200 import decoder
     from bigsmall_b200.exceptions import BigSmallVersionError
