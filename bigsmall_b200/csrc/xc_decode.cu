@@ -589,10 +589,12 @@ __device__ __forceinline__ void decode_chunk_pair(uint32_t tab_s, uint8_t *ring_
         v.z = merge_pair2(y2, __byte_perm(sm.y, 0, 0x1100));
         v.w = merge_pair2(y3, __byte_perm(sm.y, 0, 0x3322));
         if (__any_sync(kFull, ((y0 | y1 | y2 | y3) & 0x80008000u) != 0)) {
-            v.x = pair_patch(v.x, y0, true, esc, n_esc, epos, lt, bad);
-            v.y = pair_patch(v.y, y1, true, esc, n_esc, epos, lt, bad);
-            v.z = pair_patch(v.z, y2, true, esc, n_esc, epos, lt, bad);
-            v.w = pair_patch(v.w, y3, true, esc, n_esc, epos, lt, bad);
+            // patch only the pair-steps that hold an escape (a step without
+            // one would add nothing to the escape position)
+            if (__any_sync(kFull, (y0 & 0x80008000u) != 0)) v.x = pair_patch(v.x, y0, true, esc, n_esc, epos, lt, bad);
+            if (__any_sync(kFull, (y1 & 0x80008000u) != 0)) v.y = pair_patch(v.y, y1, true, esc, n_esc, epos, lt, bad);
+            if (__any_sync(kFull, (y2 & 0x80008000u) != 0)) v.z = pair_patch(v.z, y2, true, esc, n_esc, epos, lt, bad);
+            if (__any_sync(kFull, (y3 & 0x80008000u) != 0)) v.w = pair_patch(v.w, y3, true, esc, n_esc, epos, lt, bad);
         }
         st_out16(out + g * 256 + lane * 8, v);
     };
