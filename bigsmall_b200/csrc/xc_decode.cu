@@ -561,6 +561,9 @@ __device__ __forceinline__ void decode_chunk_pair(uint32_t tab_s, uint8_t *ring_
         return;
     }
     const uint8_t *esc = rec + kXcPairRecHdr + 2ull * n_words;
+    // only the fix-up path reads the escape list, long after the chunk starts:
+    // bring its first line into L1 now (lane 0, nothing waits on it)
+    if (n_esc && lane == 0) asm volatile("prefetch.global.L1 [%0];" ::"l"(esc));
     uint32_t stage = (2 * n_words + 15) & ~15u;
     if (stage > rec_bytes - kXcPairRecHdr) stage = rec_bytes - kXcPairRecHdr;
     Ring r{ring_buf, rec + kXcPairRecHdr, stage, 0, 0};
