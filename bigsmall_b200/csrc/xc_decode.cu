@@ -56,7 +56,8 @@ __device__ __forceinline__ uint32_t lanemask_lt() {
 
 __device__ __forceinline__ void cp_async16(void *smem, const void *gmem) {
     uint32_t s = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(s), "l"(gmem) : "memory");
+    // records are read front to back: ask L2 to fill 256 bytes per miss
+    asm volatile("cp.async.cg.shared.global.L2::256B [%0], [%1], 16;\n" ::"r"(s), "l"(gmem) : "memory");
 }
 __device__ __forceinline__ uint32_t lds_u16(uint32_t a) {
     unsigned short v;
@@ -82,7 +83,7 @@ __device__ __forceinline__ void cp_async_wait_pending(uint32_t pending) {
 
 __device__ __forceinline__ uint2 ld_plane8(const uint8_t *p) {
     uint2 v;
-    asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p));
+    asm volatile("ld.global.nc.L1::no_allocate.L2::256B.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p));
     return v;
 }
 
