@@ -67,6 +67,16 @@ __device__ __forceinline__ uint32_t lanemask_gt_e() {
     return m;
 }
 
+// one streaming 16-byte read of the input (read once per pass: no L1
+// allocation, 256-byte L2 fills)
+__device__ __forceinline__ uint4 ld_stream16(const uint4 *p) {
+    uint4 v;
+    asm volatile("ld.global.nc.L1::no_allocate.L2::256B.v4.u32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p));
+    return v;
+}
+
 // 1. histogram + plane ------------------------------------------------------
 __global__ void __launch_bounds__(256) xc_enc_hist_kernel(const uint16_t *__restrict__ in, uint64_t n,
                                                           unsigned long long *counts,
@@ -78,7 +88,7 @@ __global__ void __launch_bounds__(256) xc_enc_hist_kernel(const uint16_t *__rest
     const uint64_t n8 = n / 8;
     const uint64_t stride = static_cast<uint64_t>(gridDim.x) * blockDim.x;
     for (uint64_t q = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; q < n8; q += stride) {
-        uint4 v = reinterpret_cast<const uint4 *>(in)[q];
+        uint4 v = ld_stream16(reinterpret_cast<const uint4 *>(in) + q);
         uint32_t wv[4] = {v.x, v.y, v.z, v.w};
         uint32_t pl[2] = {0, 0};
 #pragma unroll
@@ -311,7 +321,7 @@ __global__ void __launch_bounds__(256) xc_enc_pair_hist_kernel(const uint16_t *_
     const uint64_t n8 = n / 8;
     const uint64_t stride = static_cast<uint64_t>(gridDim.x) * blockDim.x;
     for (uint64_t q = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; q < n8; q += stride) {
-        const uint4 v = reinterpret_cast<const uint4 *>(in)[q];
+        const uint4 v = ld_stream16(reinterpret_cast<const uint4 *>(in) + q);
         const uint32_t wv[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
         for (int k = 0; k < 4; k++)
