@@ -45,13 +45,32 @@ for _name in se_legacy.CODECS:
     register_codec(_name, se_legacy.encode, se_legacy.decoder_for(_name))
 
 
-def install_into(reference_registry, legacy: bool = False) -> None:
+def install_into(reference_registry, legacy: bool = False) -> dict:
     """Register this package's codecs in a reference codec_registry module.
     The legacy serial formats are registered (device decode, the reference's
-    encoder kept) only with ``legacy``."""
+    encoder kept) only with ``legacy``.  Returns {name: previous entry or None}
+    for :func:`remove_from`."""
+    previous = {}
     for name, (enc, dec) in _REGISTRY.items():
         if name in se_legacy.CODECS and not legacy:
             continue
-        if (name == bf16_parallel.CODEC or name in se_legacy.CODECS) and reference_registry.get_codec(name) is not None:
-            enc = reference_registry.get_codec(name)[0]   # keep the reference encoder
+        prev = reference_registry.get_codec(name)
+        previous[name] = prev
+        if (name == bf16_parallel.CODEC or name in se_legacy.CODECS) and prev is not None:
+            enc = prev[0]   # keep the reference encoder
         reference_registry.register_codec(name, enc, dec)
+    return previous
+
+
+def remove_from(reference_registry, previous: dict) -> None:
+    """Undo :func:`install_into`: entries that existed before get their
+    original (encode, decode) pair back; names that did not exist are removed
+    from the module's registry dict (the reference has no unregister call; its
+    registry is the module-level ``_REGISTRY`` dict,
+    bigsmall/codec_registry.py:42)."""
+    table = getattr(reference_registry, "_REGISTRY", None)
+    for name, prev in previous.items():
+        if prev is not None:
+            reference_registry.register_codec(name, prev[0], prev[1])
+        elif isinstance(table, dict):
+            table.pop(name, None)

@@ -11,8 +11,9 @@ The three insertion points (BigSmall paths):
     the original function;
   * ``bigsmall/codec_registry.py:45-47`` ``register_codec`` -> the codec names
     are registered so ``verify_fast`` and encode-side selection know them.
-``StreamingLoader`` (``bigsmall/streaming.py:163-181``) and ``decompress``
-import ``_decode_blob`` by name, so their module attributes are patched too.
+``StreamingLoader`` (``bigsmall/streaming.py:22,181``) and the format migration
+tool (``bigsmall/migrate.py:36,134``) import ``_decode_blob`` by name, so their
+module attributes are patched too.
 """
 from __future__ import annotations
 
@@ -59,7 +60,7 @@ def install(bigsmall_pkg, legacy_on_device: bool = False) -> dict:
 
     _decode_blob.__wrapped__ = orig
     dec._decode_blob = _decode_blob
-    for mod_name in (f"{name}.streaming",):
+    for mod_name in (f"{name}.streaming", f"{name}.migrate"):
         m = sys.modules.get(mod_name)
         if isinstance(m, types.ModuleType) and getattr(m, "_decode_blob", None) is orig:
             saved[mod_name] = orig
@@ -67,7 +68,7 @@ def install(bigsmall_pkg, legacy_on_device: bool = False) -> dict:
     # 3. registry
     reg = sys.modules.get(f"{name}.codec_registry") or getattr(bigsmall_pkg, "codec_registry", None)
     if reg is not None:
-        _reg.install_into(reg, legacy=legacy_on_device)
+        saved["registry"] = _reg.install_into(reg, legacy=legacy_on_device)
     return saved
 
 
@@ -77,9 +78,20 @@ def uninstall(bigsmall_pkg, saved: dict) -> None:
     dec._decode_blob = saved["_decode_blob"]
     kern = sys.modules.get(f"{name}.kernels") or getattr(bigsmall_pkg, "kernels", None)
     if kern is not None:
-        if saved.get("ac_cuda") is None and hasattr(kern, "ac_cuda"):
-            delattr(kern, "ac_cuda")
-        sys.modules.pop(f"{name}.kernels.ac_cuda", None)
+        if saved.get("ac_cuda") is None:
+            if hasattr(kern, "ac_cuda"):
+                delattr(kern, "ac_cuda")
+            sys.modules.pop(f"{name}.kernels.ac_cuda", None)
+        else:
+            kern.ac_cuda = saved["ac_cuda"]
+            sys.modules[f"{name}.kernels.ac_cuda"] = saved["ac_cuda"]
     for mod_name, fn in saved.items():
-        if mod_name.endswith(".streaming") and mod_name in sys.modules:
+        if mod_name.endswith((".streaming", ".migrate")) and mod_name in sys.modules:
             sys.modules[mod_name]._decode_blob = fn
+    reg = sys.modules.get(f"{name}.codec_registry") or getattr(bigsmall_pkg, "codec_registry", None)
+    if reg is not None and "registry" in saved:
+        _reg.remove_from(reg, saved["registry"])
+    if kern is not None:
+        for attr in ("_GPU_BACKEND", "_GPU_DECODE_FN"):   # the next probe runs afresh
+            if hasattr(kern, attr):
+                setattr(kern, attr, None)

@@ -138,11 +138,16 @@ int bs_plan_destroy(bs_plan *plan);
  * 260 KiB) is a static device array that every GPU loading the library holds
  * until the process exits.  The first call on a device resolves that array's
  * address (with the device current); make that first call before any stream
- * capture.  All calls share the array, so calls whose GPU work overlaps race:
- * serialise them.  Synchronous: returns after `stream` has finished the
- * decode, with the per-tensor device status words in `status_out` (may be
- * NULL; else n_tensors entries).  More than BS_NOALLOC_MAX_TENSORS tensors is
- * BS_E_INVALID_ARG. */
+ * capture.  With CUDA's lazy module loading (the default in CUDA 12) the
+ * library's kernels and this array are loaded into a device's context on
+ * first use, which itself needs a little device memory: make one call (or set
+ * CUDA_MODULE_LOADING=EAGER) before the caller reserves its HBM.  The resolved
+ * address belongs to the device's current context; after cudaDeviceReset the
+ * process must not call this entry point again on that device.  All calls
+ * share the array, so calls whose GPU work overlaps race: serialise them.
+ * Synchronous: returns after `stream` has finished the decode, with the
+ * per-tensor device status words in `status_out` (may be NULL; else n_tensors
+ * entries).  More than BS_NOALLOC_MAX_TENSORS tensors is BS_E_INVALID_ARG. */
 #define BS_NOALLOC_MAX_TENSORS 8
 int bs_xc_decode_noalloc(const bs_xc_tensor *tensors, int n_tensors, void *stream,
                          uint32_t *status_out);

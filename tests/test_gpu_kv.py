@@ -82,6 +82,27 @@ def test_config5_distribution_device_encoder_matches_oracle():
         assert torch.equal(k2.cpu().view(torch.int16), k.view(torch.int16)), coder
 
 
+def test_config5_full_tensor_encode_matches_oracle_and_decodes_exactly():
+    """One whole config-5 K/V tensor, [16, 8, 8192, 128] = 16.8M values (N(0,1)
+    times a per-channel log-normal scale, seed 0): the device encoder's blob
+    equals the CPU oracle's byte for byte and the device decode is bit-exact
+    (reference bigsmall/codecs/kv_cache.py:41-117 round-trips the same layout)."""
+    from bigsmall_b200 import gpu
+    from bigsmall_b200.kv_cache import KVEncoder, decode_kv
+    g = torch.Generator().manual_seed(0)
+    scale = torch.exp(torch.randn(1, 8, 1, 128, generator=g))
+    k = (torch.randn(16, 8, 8192, 128, generator=g) * scale).to(torch.bfloat16)
+    raw = k.view(torch.uint8).numpy().tobytes()
+    kd = k.cuda()
+    for coder, cid in (("pair", 2), ("rans", 0)):
+        enc = KVEncoder(0, coder=coder)
+        kb = enc.encode(kd)
+        assert kb.cpu().numpy().tobytes() == O.xc_encode(raw, cid, 12, gpu.DEFAULT_CHUNK_ELEMS), coder
+        k2, v2 = decode_kv(kb, kb, k.shape, k.shape, coder=coder)
+        assert torch.equal(k2.view(torch.int16), kd.view(torch.int16)), coder
+        assert torch.equal(v2.view(torch.int16), kd.view(torch.int16)), coder
+
+
 def test_legacy_kv_versions_rejected_clearly():
     from bigsmall_b200.kv_cache import decompress_kv_entry
     blob = struct.pack("<BB", 2, 1) + struct.pack("<i", 4) + struct.pack("<I", 0)

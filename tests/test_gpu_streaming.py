@@ -18,10 +18,10 @@ def _cfg(layers=4, tie=False):
                        tie_word_embeddings=tie, rope_theta=10000.0)
 
 
-def _image(weights):
+def _image(weights, chunk_elems=4096):
     from bigsmall_b200 import decoder
     from bigsmall_b200.loader import ContainerImage
-    return ContainerImage.from_bytes(decoder.compress_tensors(weights, chunk_elems=4096, with_md5=False))
+    return ContainerImage.from_bytes(decoder.compress_tensors(weights, chunk_elems=chunk_elems, with_md5=False))
 
 
 @pytest.mark.parametrize("layers,tie,prefetch", [(4, False, 1), (5, True, 1), (4, False, 0)])
@@ -69,3 +69,36 @@ def test_streaming_loader_api():
         with pytest.raises(KeyError):
             ld.load_tensor("nope")
     assert layer_index("transformer.h.11.mlp.c_fc.bias") == 11 and layer_index("model.norm.weight") is None
+
+
+def test_streaming_config4_layer_width_logits_bit_identical():
+    """BASELINE config 4's shapes (Qwen2.5-14B: hidden 5120, intermediate 13824,
+    40 Q / 8 KV heads x 128, q/k/v biases, vocab 152064, untied embeddings) at 3
+    layers, default chunk size: the side-stream pipeline's logits equal the
+    resident model's bit for bit (reference bigsmall/streaming_inference.py:
+    152-199, 272-348 swap decoded layers in the same way)."""
+    from transformers import Qwen2Config
+    from bigsmall_b200 import gpu, synthetic
+    from bigsmall_b200.streaming import StreamingLoader
+    from bigsmall_b200.streaming_inference import BigSmallStreamingModel
+    torch.use_deterministic_algorithms(True, warn_only=True)
+    cfg = Qwen2Config(vocab_size=152064, hidden_size=5120, intermediate_size=13824, num_hidden_layers=3,
+                      num_attention_heads=40, num_key_value_heads=8, max_position_embeddings=4096,
+                      tie_word_embeddings=False, rope_theta=1000000.0, rms_norm_eps=1e-6)
+    w = synthetic.random_weights(cfg, seed=0)
+    assert w["model.layers.0.mlp.gate_proj.weight"].shape == (13824, 5120)
+    assert w["model.layers.0.self_attn.k_proj.weight"].shape == (1024, 5120)
+    g = torch.Generator(device="cuda").manual_seed(0)
+    prompt = torch.randint(0, cfg.vocab_size, (1, 64), generator=g, device="cuda")
+    ref = synthetic.resident_model(cfg, w)
+    ids_r, lg_r, _, _ = synthetic.greedy(ref, prompt, 4)
+    del ref
+    sm = BigSmallStreamingModel(StreamingLoader(_image(w, gpu.DEFAULT_CHUNK_ELEMS)), cfg, prefetch=1)
+    try:
+        for _ in range(2):
+            ids_s, lg_s, _, _ = synthetic.greedy(sm.model, prompt, 4)
+            sm.check()
+            assert torch.equal(ids_r, ids_s)
+            assert torch.equal(lg_r.view(torch.int16), lg_s.view(torch.int16))
+    finally:
+        sm.close()

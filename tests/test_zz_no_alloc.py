@@ -10,7 +10,9 @@ status words) is a static device array instead of plan memory.
 These tests call it through the C ABI, two calls in a row -- the second call
 runs on the scratch the first one left behind -- and check every output bit
 for bit against the plan-based entry point (bs_xc_plan_create /
-bs_plan_decode).  The file is named to be collected last.
+bs_plan_decode) and against the values that were encoded.  One test checks
+the promise itself: after a warm-up call, a further call leaves the device's
+free memory unchanged.  The file is named to be collected last.
 """
 from __future__ import annotations
 
@@ -36,15 +38,24 @@ def _blob(x, coder, ce):
     return torch.from_numpy(np.frombuffer(b, dtype=np.uint8).copy()).cuda()
 
 
-def _cases(seed0):
-    """(blob, n_total, chunk_elems, chunk_begin, chunk_count) per tensor."""
+def _cases(seed0, with_values=False):
+    """(blob, n_total, chunk_elems, chunk_begin, chunk_count) per tensor, and
+    with `with_values` also the encoded values (host bf16) of each tensor."""
     specs = [(300_001, 0, 65536, 0, 0), (4096, 1, 256, 0, 0), (1_000_003, 0, 4096, 10, 50),
              (77, 1, 256, 0, 0), (200_000, 0, 65536, 1, 0), (150_001, 2, 4096, 3, 20), (9_999, 2, 256, 0, 0)]
-    out = []
+    out, values = [], []
     for i, (n, coder, ce, c0, cc) in enumerate(specs):
         x = _tensor(n, seed0 + i, scale=0.01 * (i + 1))
         out.append((_blob(x, coder, ce), n, ce, c0, cc))
-    return out
+        values.append(x)
+    return (out, values) if with_values else out
+
+
+def _expected_slice(x, n, ce, c0, cc):
+    """The values a chunk range [c0, c0 + cc) decodes to (cc 0: to the end)."""
+    nc = -(-n // ce)
+    cnt = cc if cc else nc - c0
+    return x.view(torch.int16)[c0 * ce:min(n, (c0 + cnt) * ce)]
 
 
 def _outputs(cases):
@@ -85,14 +96,33 @@ def _with_plan(cases):
 
 
 def test_noalloc_matches_plan_entry_point_on_consecutive_calls():
-    a, b = _cases(100), _cases(200)[:3]
-    for cases in (a, b, a):   # consecutive calls reuse the shared scratch
+    a, va = _cases(100, with_values=True)
+    b, vb = _cases(200, with_values=True)
+    b, vb = b[:3], vb[:3]
+    for cases, values in ((a, va), (b, vb), (a, va)):   # consecutive calls reuse the shared scratch
         want = _with_plan(cases)
         got = _outputs(cases)
         rc, st = _noalloc(cases, got)
         assert rc == 0 and st == [0] * len(cases), (rc, st)
-        for w, g in zip(want, got):
+        for w, g, x, (_, n, ce, c0, cc) in zip(want, got, values, cases):
             assert torch.equal(w, g)    # bit-exact, as every decode test here
+            assert torch.equal(g.cpu(), _expected_slice(x, n, ce, c0, cc))   # and equal to the encoded values
+
+
+def test_noalloc_call_allocates_no_device_memory():
+    cases, values = _cases(500, with_values=True)
+    outs = _outputs(cases)
+    rc, _ = _noalloc(cases, outs)             # warm-up: resolves the scratch address once
+    assert rc == 0
+    torch.cuda.synchronize()
+    free0 = torch.cuda.mem_get_info()[0]
+    for _ in range(2):
+        rc, st = _noalloc(cases, outs)
+        assert rc == 0 and st == [0] * len(cases)
+    torch.cuda.synchronize()
+    assert torch.cuda.mem_get_info()[0] == free0
+    for o, x, (_, n, ce, c0, cc) in zip(outs, values, cases):
+        assert torch.equal(o.cpu(), _expected_slice(x, n, ce, c0, cc))
 
 
 def test_noalloc_rejects_more_tensors_than_its_scratch_holds():
