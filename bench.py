@@ -611,8 +611,10 @@ def bench_kv(a, torch, dev, world, rank, dist, local):
 # config 3: codec sweep
 # ---------------------------------------------------------------------------
 def bench_sweep(a, torch, dev, world, rank, dist, local):
-    """2^30 Laplace(0, b) values, b in {0.005, 0.02, 0.1}; rANS vs tANS; chunks
-    of 64 KiB / 256 KiB / 1 MiB / 4 MiB of bf16.  One JSON line per case."""
+    """2^30 Laplace(0, b) values, b in {0.005, 0.02, 0.1}; rANS vs tANS (and the
+    exponent-pair coder); chunks of 64 KiB / 256 KiB / 1 MiB / 4 MiB of bf16,
+    each with one state group per chunk and, above 64 KiB, with the chunk cut
+    into state groups of 32,768 values (64 KiB).  One JSON line per case."""
     from bigsmall_b200 import gpu
     n = int(os.environ.get("BS_SWEEP_N", str(1 << 30)))
     peak, peak_kind = measured_peak()
@@ -626,17 +628,19 @@ def bench_sweep(a, torch, dev, world, rank, dist, local):
         pr = hist[hist > 0] / n
         h_exp = float(-(pr * pr.log2()).sum())
         for coder in ("rans", "tans", "pair"):
-            for cbytes in (64 << 10, 256 << 10, 1 << 20, 4 << 20):
+            for cbytes, groups in ((64 << 10, 1), (256 << 10, 1), (256 << 10, 4), (1 << 20, 1), (1 << 20, 16),
+                                   (4 << 20, 1), (4 << 20, 64)):
                 ce = cbytes // 2
-                blob = gpu.encode_xc(x, coder=coder, chunk_elems=ce)
+                blob = gpu.encode_xc(x, coder=coder, chunk_elems=ce, groups=groups)
                 out = torch.empty_like(x)
-                plan = gpu.XcPlan([(blob, out.view(torch.int16), ce)], device=local, coders=coder)
+                plan = gpu.XcPlan([(blob, out.view(torch.int16), ce)], device=local, coders=coder, groups=groups)
                 ms = _timed(torch, lambda: plan.decode(stream), a.steps, a.warmup, stream)
                 plan.check(stream)
                 ok = torch.equal(out.view(torch.int16), x.view(torch.int16))
                 algo = blob.numel() + 2 * n
                 print(json.dumps({"config": "BASELINE config 3 sweep", "laplace_b": bscale, "H_exp_bits": round(h_exp, 3),
-                                  "coder": coder, "chunk_bytes": cbytes, "values": n,
+                                  "coder": coder, "chunk_bytes": cbytes, "groups_per_chunk": groups,
+                                  "group_values": ce // groups, "values": n,
                                   "ratio": round(blob.numel() / (2 * n), 5), "decode_ms": round(ms, 4),
                                   "decoded_GBs": round(2 * n / ms / 1e6, 1),
                                   "hbm_frac": round(algo / ms / 1e6 / peak, 4), "peak": f"{peak} ({peak_kind})",
@@ -655,8 +659,11 @@ def bench_mix(a, torch, dev, world, rank, dist, local):
     read per 16 GB written on config 2) and 0:1 (write only), 5 GiB per
     stream, best launch shape of 4/8/16 CTAs per SM.  One JSON line."""
     import ctypes
-    from bigsmall_b200 import _lib
-    L = _lib.load()
+    # the probe is bench tooling: its own library, not part of libbsgpu.so
+    L = ctypes.CDLL(os.path.join(ROOT, "bigsmall_b200", "libbscalib.so"))
+    L.bs_stream_probe.restype = ctypes.c_int
+    L.bs_stream_probe.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_uint64, ctypes.c_int, ctypes.c_int,
+                                  ctypes.c_int, ctypes.c_void_p]
     units = (5 << 30) // 16
     src = torch.empty(2 * units * 16, dtype=torch.uint8, device=dev).fill_(1)
     dst = torch.empty(3 * units * 16, dtype=torch.uint8, device=dev)
@@ -668,8 +675,10 @@ def bench_mix(a, torch, dev, world, rank, dist, local):
         best = None
         for per_sm in (4, 8, 16):
             def launch():
-                _lib.check(L.bs_stream_probe(src.data_ptr(), dst.data_ptr(), units, rd, wr, sms * per_sm,
-                                             ctypes.c_void_p(stream.cuda_stream)), "bs_stream_probe")
+                rc = L.bs_stream_probe(src.data_ptr(), dst.data_ptr(), units, rd, wr, sms * per_sm,
+                                       ctypes.c_void_p(stream.cuda_stream))
+                if rc:
+                    raise RuntimeError(f"bs_stream_probe failed with status {rc}")
             ms = _timed(torch, launch, a.steps, a.warmup, stream)
             gbs = 16 * units * (rd + wr) / ms / 1e6
             if best is None or gbs > best["GBs"]:

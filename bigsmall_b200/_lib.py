@@ -49,6 +49,8 @@ class XcTensor(ctypes.Structure):
         ("chunk_begin", ctypes.c_uint32),
         ("chunk_count", ctypes.c_uint32),
         ("coder_mask", ctypes.c_uint32),
+        ("groups", ctypes.c_uint32),
+        ("reserved", ctypes.c_uint32),
     ]
 
 
@@ -81,10 +83,9 @@ SIGNATURES = {
     "bs_plan_destroy": (_I, [_P]),
     "bs_xc_decode_noalloc": (_I, [ctypes.POINTER(XcTensor), _I, _P, ctypes.POINTER(_U32)]),
     "bs_par_plan_create": (_I, [_P, _U64, _U64, _P, _P, _I, ctypes.POINTER(_P)]),
-    "bs_xc_encode_bound": (_I, [_U64, _U32, ctypes.POINTER(_U64)]),
-    "bs_xc_encode_workspace": (_I, [_U64, _U32, _I, ctypes.POINTER(_U64)]),
-    "bs_xc_encode": (_I, [_P, _U64, _I, _I, _U32, _P, _U64, _P, _P, _U64, _P]),
-    "bs_stream_probe": (_I, [_P, _P, _U64, _I, _I, _I, _P]),
+    "bs_xc_encode_bound": (_I, [_U64, _U32, _U32, ctypes.POINTER(_U64)]),
+    "bs_xc_encode_workspace": (_I, [_U64, _U32, _U32, _I, ctypes.POINTER(_U64)]),
+    "bs_xc_encode": (_I, [_P, _U64, _I, _I, _U32, _U32, _P, _U64, _P, _P, _U64, _P]),
     "bs_se_plan_create": (_I, [_I, _P, _U64, _U64, _P, _P, _I, ctypes.POINTER(_P)]),
     "bs_se_parse": (_I, [_I, _P, _U64, _U64, ctypes.POINTER(_U32)]),
     "bs_se_plan_create_many": (_I, [ctypes.POINTER(SeBlob), _I, _I, ctypes.POINTER(_P)]),

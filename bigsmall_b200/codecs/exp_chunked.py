@@ -24,15 +24,15 @@ def _device(device=None) -> torch.device:
 
 
 def encode(raw: bytes, coder: str = gpu.DEFAULT_CODER, prec: int = gpu.DEFAULT_PREC,
-           chunk_elems: int = gpu.DEFAULT_CHUNK_ELEMS, device=None, **_) -> tuple[bytes, dict]:
+           chunk_elems: int = gpu.DEFAULT_CHUNK_ELEMS, device=None, groups: int = 1, **_) -> tuple[bytes, dict]:
     if len(raw) % 2 != 0:
         raise ValueError(f"BF16 byte length must be even, got {len(raw)}")
     if len(raw) == 0:
-        return b"", gpu.xc_extras(chunk_elems, coder, prec)
+        return b"", gpu.xc_extras(chunk_elems, coder, prec, groups)
     dev = _device(device)
     x = torch.from_numpy(np.frombuffer(raw, dtype=np.int16).copy()).to(dev)
-    blob = gpu.encode_xc(x, coder=coder, prec=prec, chunk_elems=chunk_elems)
-    return blob.cpu().numpy().tobytes(), gpu.xc_extras(chunk_elems, coder, prec)
+    blob = gpu.encode_xc(x, coder=coder, prec=prec, chunk_elems=chunk_elems, groups=groups)
+    return blob.cpu().numpy().tobytes(), gpu.xc_extras(chunk_elems, coder, prec, groups)
 
 
 def decode_to_device(blob, extras: dict, n_weights: int, device=None) -> torch.Tensor:
@@ -48,7 +48,7 @@ def decode_to_device(blob, extras: dict, n_weights: int, device=None) -> torch.T
     if d.data_ptr() % 16:
         d = d.clone()
     ce = int((extras or {}).get("chunk_elems", gpu.DEFAULT_CHUNK_ELEMS))
-    gpu.decode_xc_into(d, out, ce, coder=(extras or {}).get("coder"))
+    gpu.decode_xc_into(d, out, ce, coder=(extras or {}).get("coder"), groups=gpu.extras_groups(extras))
     return out
 
 

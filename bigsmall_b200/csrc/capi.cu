@@ -134,11 +134,56 @@ void free_plan(bs_plan *p) {
     delete p;
 }
 
+// Validate one bf16_exp_chunked_v1 descriptor and turn it into the device
+// descriptor of its state groups: the decode kernels work per group, so the
+// chunk range [chunk_begin, chunk_begin + chunk_count) becomes the group range
+// [*g_begin, *g_begin + *g_count).  `who` prefixes error messages.
+int xc_describe(const bs_xc_tensor &t, int device, const std::string &who, XcTensorDev *d, uint32_t *g_begin,
+                uint32_t *g_count) {
+    if (t.coder_mask & ~kXcAllCoders) return fail(BS_E_INVALID_ARG, who + "coder_mask has unknown coder bits");
+    if (t.reserved) return fail(BS_E_INVALID_ARG, who + "reserved field must be 0");
+    if (!t.d_blob || !t.d_out) return fail(BS_E_INVALID_ARG, who + "NULL pointer");
+    if ((reinterpret_cast<uintptr_t>(t.d_blob) | reinterpret_cast<uintptr_t>(t.d_out)) & 15)
+        return fail(BS_E_INVALID_ARG, who + "blob and output must be 16-byte aligned");
+    const uint32_t G = t.groups ? t.groups : 1u;
+    if (t.chunk_elems == 0 || t.chunk_elems % G || (t.chunk_elems / G) < 256 || ((t.chunk_elems / G) & 255))
+        return fail(BS_E_INVALID_ARG, who + "chunk_elems / groups must be a positive multiple of 256");
+    const uint32_t ge = t.chunk_elems / G;
+    const uint64_t nc = (t.n_elems + t.chunk_elems - 1) / t.chunk_elems;
+    const uint64_t ng = (t.n_elems + ge - 1) / ge;
+    if (ng > 0x7FFFFFFFull) return fail(BS_E_INVALID_ARG, who + "too many chunks");
+    if (t.chunk_begin >= nc) return fail(BS_E_INVALID_ARG, who + "chunk_begin beyond the last chunk");
+    const uint64_t cnt = t.chunk_count ? t.chunk_count : nc - t.chunk_begin;
+    if (t.chunk_begin + cnt > nc) return fail(BS_E_INVALID_ARG, who + "chunk range beyond the last chunk");
+    const uint64_t min_bytes = rup(kXcTabOff + 4 * (ng + 1), 16) + rup(t.n_elems, 16) + 128 * ng;
+    if (t.blob_bytes < min_bytes) return fail(BS_E_TRUNCATED, who + "blob shorter than its framing");
+    if (!on_device(t.d_blob, device) || !on_device(t.d_out, device))
+        return fail(BS_E_INVALID_ARG, who + "pointers must be device memory of device " + std::to_string(device));
+    const uint64_t gb = static_cast<uint64_t>(t.chunk_begin) * G;
+    const uint64_t ge_end = std::min<uint64_t>(ng, (t.chunk_begin + cnt) * G);
+    XcTensorDev x{};
+    x.blob = static_cast<const uint8_t *>(t.d_blob);
+    x.blob_bytes = t.blob_bytes;
+    x.out = static_cast<uint16_t *>(t.d_out);
+    x.n = t.n_elems;
+    x.chunk_elems = ge;
+    x.n_chunks = static_cast<uint32_t>(ng);
+    x.chunk_begin = static_cast<uint32_t>(gb);
+    x.aux = 0;
+    x.groups = G;
+    x.coder = 0xFFFFFFFFu;
+    x.coder_mask = t.coder_mask;
+    *d = x;
+    *g_begin = static_cast<uint32_t>(gb);
+    *g_count = static_cast<uint32_t>(ge_end - gb);
+    return BS_OK;
+}
+
 }  // namespace
 
 extern "C" {
 
-int bs_version(void) { return 100; }
+int bs_version(void) { return 101; }
 
 const char *bs_last_error(void) { return g_err.c_str(); }
 
@@ -192,36 +237,13 @@ int bs_xc_plan_create(const bs_xc_tensor *tensors, int n_tensors, int device, bs
     for (int i = 0; i < n_tensors; i++) {
         const bs_xc_tensor &t = tensors[i];
         if (t.n_elems == 0) continue;
-        const std::string who = "tensor " + std::to_string(i) + ": ";
-        if (t.coder_mask & ~kXcAllCoders) return fail(BS_E_INVALID_ARG, who + "coder_mask has unknown coder bits");
-        if (!t.d_blob || !t.d_out) return fail(BS_E_INVALID_ARG, who + "NULL pointer");
-        if ((reinterpret_cast<uintptr_t>(t.d_blob) | reinterpret_cast<uintptr_t>(t.d_out)) & 15)
-            return fail(BS_E_INVALID_ARG, who + "blob and output must be 16-byte aligned");
-        if (t.chunk_elems < 256 || (t.chunk_elems & 255))
-            return fail(BS_E_INVALID_ARG, who + "chunk_elems must be a positive multiple of 256");
-        uint64_t nc = (t.n_elems + t.chunk_elems - 1) / t.chunk_elems;
-        if (nc > 0x7FFFFFFFull) return fail(BS_E_INVALID_ARG, who + "too many chunks");
-        if (t.chunk_begin >= nc) return fail(BS_E_INVALID_ARG, who + "chunk_begin beyond the last chunk");
-        const uint64_t cnt = t.chunk_count ? t.chunk_count : nc - t.chunk_begin;
-        if (t.chunk_begin + cnt > nc) return fail(BS_E_INVALID_ARG, who + "chunk range beyond the last chunk");
-        uint64_t min_bytes = rup(kXcTabOff + 4 * (nc + 1), 16) + rup(t.n_elems, 16) + 128 * nc;
-        if (t.blob_bytes < min_bytes) return fail(BS_E_TRUNCATED, who + "blob shorter than its framing");
-        if (!on_device(t.d_blob, device) || !on_device(t.d_out, device))
-            return fail(BS_E_INVALID_ARG, who + "pointers must be device memory of device " + std::to_string(device));
-        XcTensorDev d{};
-        d.blob = static_cast<const uint8_t *>(t.d_blob);
-        d.blob_bytes = t.blob_bytes;
-        d.out = static_cast<uint16_t *>(t.d_out);
-        d.n = t.n_elems;
-        d.chunk_elems = t.chunk_elems;
-        d.n_chunks = static_cast<uint32_t>(nc);
-        d.chunk_begin = t.chunk_begin;
-        d.aux = 0;
-        d.coder = 0xFFFFFFFFu;
-        d.coder_mask = t.coder_mask;
+        XcTensorDev d;
+        uint32_t gb = 0, gc = 0;
+        const int rc = xc_describe(t, device, "tensor " + std::to_string(i) + ": ", &d, &gb, &gc);
+        if (rc) return rc;
         u2i[i] = static_cast<int>(ht.size());
         ht.push_back(d);
-        ranges.push_back({t.chunk_begin, static_cast<uint32_t>(cnt)});
+        ranges.push_back({gb, gc});
     }
     // work items: <= warps-per-CTA chunks of one tensor; big tensors first so
     // small ones fill the tail of the grid
@@ -406,34 +428,10 @@ int bs_xc_decode_noalloc(const bs_xc_tensor *tensors, int n_tensors, void *strea
         const bs_xc_tensor &t = tensors[i];
         u2i[i] = -1;
         if (t.n_elems == 0) continue;
-        const std::string who = "tensor " + std::to_string(i) + ": ";
-        if (t.coder_mask & ~kXcAllCoders) return fail(BS_E_INVALID_ARG, who + "coder_mask has unknown coder bits");
-        if (!t.d_blob || !t.d_out) return fail(BS_E_INVALID_ARG, who + "NULL pointer");
-        if ((reinterpret_cast<uintptr_t>(t.d_blob) | reinterpret_cast<uintptr_t>(t.d_out)) & 15)
-            return fail(BS_E_INVALID_ARG, who + "blob and output must be 16-byte aligned");
-        if (t.chunk_elems < 256 || (t.chunk_elems & 255))
-            return fail(BS_E_INVALID_ARG, who + "chunk_elems must be a positive multiple of 256");
-        const uint64_t nc = (t.n_elems + t.chunk_elems - 1) / t.chunk_elems;
-        if (nc > 0x7FFFFFFFull) return fail(BS_E_INVALID_ARG, who + "too many chunks");
-        if (t.chunk_begin >= nc) return fail(BS_E_INVALID_ARG, who + "chunk_begin beyond the last chunk");
-        const uint64_t cnt = t.chunk_count ? t.chunk_count : nc - t.chunk_begin;
-        if (t.chunk_begin + cnt > nc) return fail(BS_E_INVALID_ARG, who + "chunk range beyond the last chunk");
-        const uint64_t min_bytes = rup(kXcTabOff + 4 * (nc + 1), 16) + rup(t.n_elems, 16) + 128 * nc;
-        if (t.blob_bytes < min_bytes) return fail(BS_E_TRUNCATED, who + "blob shorter than its framing");
-        if (!on_device(t.d_blob, device) || !on_device(t.d_out, device))
-            return fail(BS_E_INVALID_ARG, who + "pointers must be device memory of the current device");
-        XcTensorDev d{};
-        d.blob = static_cast<const uint8_t *>(t.d_blob);
-        d.blob_bytes = t.blob_bytes;
-        d.out = static_cast<uint16_t *>(t.d_out);
-        d.n = t.n_elems;
-        d.chunk_elems = t.chunk_elems;
-        d.n_chunks = static_cast<uint32_t>(nc);
-        d.chunk_begin = t.chunk_begin;
-        d.coder = 0xFFFFFFFFu;
-        d.coder_mask = t.coder_mask;
-        ht[n] = d;
-        rc_count[n] = static_cast<uint32_t>(cnt);
+        uint32_t gb = 0, gc = 0;
+        const int rc = xc_describe(t, device, "tensor " + std::to_string(i) + ": ", &ht[n], &gb, &gc);
+        if (rc) return rc;
+        rc_count[n] = gc;
         u2i[i] = n++;
     }
     uint32_t st[BS_NOALLOC_MAX_TENSORS] = {};
@@ -1098,23 +1096,41 @@ int bs_se_plan_create(int codec, const uint8_t *h, uint64_t len, uint64_t n_weig
 // --------------------------------------------------------------------------
 // encoder
 // --------------------------------------------------------------------------
-int bs_xc_encode_bound(uint64_t n, uint32_t ce, uint64_t *bytes) {
-    if (!bytes || ce < 256 || (ce & 255)) return fail(BS_E_INVALID_ARG, "bad encode_bound arguments");
-    *bytes = n ? xc_encode_bound(n, ce) : 0;
+}  // extern "C"
+
+namespace {
+// values per state group, or 0 when (chunk_elems, groups) is not valid
+uint32_t group_elems(uint32_t ce, uint32_t groups) {
+    const uint32_t G = groups ? groups : 1u;
+    if (ce == 0 || ce % G) return 0;
+    const uint32_t ge = ce / G;
+    return (ge >= 256 && !(ge & 255)) ? ge : 0u;
+}
+}  // namespace
+
+extern "C" {
+
+int bs_xc_encode_bound(uint64_t n, uint32_t ce, uint32_t groups, uint64_t *bytes) {
+    const uint32_t ge = group_elems(ce, groups);
+    if (!bytes || !ge) return fail(BS_E_INVALID_ARG, "bad encode_bound arguments");
+    *bytes = n ? xc_encode_bound(n, ge) : 0;
     return BS_OK;
 }
 
-int bs_xc_encode_workspace(uint64_t n, uint32_t ce, int coder, uint64_t *bytes) {
-    if (!bytes || ce < 256 || (ce & 255) || coder < BS_CODER_RANS || coder > BS_CODER_RANS_PAIR)
+int bs_xc_encode_workspace(uint64_t n, uint32_t ce, uint32_t groups, int coder, uint64_t *bytes) {
+    const uint32_t ge = group_elems(ce, groups);
+    if (!bytes || !ge || coder < BS_CODER_RANS || coder > BS_CODER_RANS_PAIR)
         return fail(BS_E_INVALID_ARG, "bad encode_workspace arguments");
-    *bytes = n ? xc_encode_workspace(n, ce, coder) : 0;
+    *bytes = n ? xc_encode_workspace(n, ge, coder) : 0;
     return BS_OK;
 }
 
-int bs_xc_encode(const void *d_in, uint64_t n, int coder, int prec, uint32_t ce, void *d_out, uint64_t out_cap,
-                 uint64_t *d_out_len, void *d_ws, uint64_t ws_bytes, void *stream) {
+int bs_xc_encode(const void *d_in, uint64_t n, int coder, int prec, uint32_t ce_chunk, uint32_t groups,
+                 void *d_out, uint64_t out_cap, uint64_t *d_out_len, void *d_ws, uint64_t ws_bytes, void *stream) {
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    if (ce < 256 || (ce & 255)) return fail(BS_E_INVALID_ARG, "chunk_elems must be a positive multiple of 256");
+    const uint32_t ce = group_elems(ce_chunk, groups);   // the encoder codes state groups
+    const uint32_t G = groups ? groups : 1u;
+    if (!ce) return fail(BS_E_INVALID_ARG, "chunk_elems / groups must be a positive multiple of 256");
     if (prec < 8 || prec > 12) return fail(BS_E_INVALID_ARG, "precision must be in [8, 12]");
     if (coder < BS_CODER_RANS || coder > BS_CODER_RANS_PAIR)
         return fail(BS_E_INVALID_ARG, "coder must be 0 (rANS), 1 (tANS) or 2 (rANS over exponent pairs)");
@@ -1135,28 +1151,10 @@ int bs_xc_encode(const void *d_in, uint64_t n, int coder, int prec, uint32_t ce,
     if ((n + ce - 1) / ce > 0x7FFFFFFFull) return fail(BS_E_INVALID_ARG, "too many chunks");
     if (out_cap < xc_encode_bound(n, ce)) return fail(BS_E_INVALID_ARG, "out_cap below bs_xc_encode_bound");
     if (ws_bytes < xc_encode_workspace(n, ce, coder)) return fail(BS_E_INVALID_ARG, "workspace below bs_xc_encode_workspace");
-    cudaError_t e = launch_xc_encode(static_cast<const uint16_t *>(d_in), n, coder, prec, ce,
+    cudaError_t e = launch_xc_encode(static_cast<const uint16_t *>(d_in), n, coder, prec, ce, G,
                                      static_cast<uint8_t *>(d_out), out_cap, d_out_len,
                                      static_cast<uint8_t *>(d_ws), ws_bytes, s);
     if (e != cudaSuccess) return cuda_fail(e, "encode launch");
-    return BS_OK;
-}
-
-int bs_stream_probe(const void *d_in, void *d_out, uint64_t units, int rd, int wr, int grid, void *stream) {
-    if (!((rd == 1 && wr == 1) || (rd == 2 && wr == 3) || (rd == 0 && wr == 1)))
-        return fail(BS_E_INVALID_ARG, "bs_stream_probe: (rd, wr) must be (1,1), (2,3) or (0,1)");
-    if (grid <= 0 || units == 0 || (rd && !d_in) || !d_out) return fail(BS_E_INVALID_ARG, "bs_stream_probe: bad arguments");
-    if ((reinterpret_cast<uintptr_t>(d_in) | reinterpret_cast<uintptr_t>(d_out)) & 15)
-        return fail(BS_E_INVALID_ARG, "bs_stream_probe: buffers must be 16-byte aligned");
-    int device = 0;
-    if (cudaGetDevice(&device) != cudaSuccess) {
-        cudaGetLastError();
-        return fail(BS_E_CUDA, "no current CUDA device");
-    }
-    if ((rd && !on_device(d_in, device)) || !on_device(d_out, device))
-        return fail(BS_E_INVALID_ARG, "bs_stream_probe: buffers must be device memory of the current device");
-    cudaError_t e = launch_stream_mix(d_in, d_out, units, rd, wr, grid, static_cast<cudaStream_t>(stream));
-    if (e != cudaSuccess) return cuda_fail(e, "bs_stream_probe");
     return BS_OK;
 }
 

@@ -13,15 +13,21 @@ constexpr uint32_t kFull = 0xFFFFFFFFu;
 
 // ---- bf16_exp_chunked_v1 layout (little-endian; sections in this order, each
 // 16-byte aligned):
-//   0 "BSXC" | 4 u16 version=1 | 6 u8 coder (0 rANS, 1 tANS, 2 rANS over
-//   exponent pairs) | 7 u8 P
+//   0 "BSXC" | 4 u16 version (1; 2 with groups) | 6 u8 coder (0 rANS, 1 tANS,
+//   2 rANS over exponent pairs) | 7 u8 P
 //   8 u64 n | 16 u32 chunk_elems | 20 u32 n_chunks | 24 u32 lanes=32
 //   28 u32 aux (coder 2: window base e_lo; else 0)
-//   32 u64 chunks_off | 40 u64 plane_off | 48 u64 blob_bytes | 56 u64 0
-//   64 u16 freq[256] | 576 u32 chunk_start[n_chunks+1] (16 B units)
-//   plane_off = rup16(576 + 4*(n_chunks+1)): n bytes of (sign << 7) | mantissa
-//   chunks_off = plane_off + rup16(n): per chunk [u32 init[32]][u16 words...]
-//   zero-padded to 16 B; blob_bytes = end of the last chunk record.
+//   32 u64 chunks_off | 40 u64 plane_off | 48 u64 blob_bytes
+//   56 version 1: u64 0; version 2: u32 groups G | u32 0
+//   64 u16 freq[256] | 576 u32 group_start[n_groups+1] (16 B units)
+//   A chunk is G state groups of ge = chunk_elems / G values (a multiple of
+//   256; version 1 is G = 1): group k holds elements [k*ge, min(n, (k+1)*ge)),
+//   n_groups = ceil(n / ge), so chunk size (framing) and the number of
+//   independently decodable groups (parallelism) are separate choices.
+//   plane_off = rup16(576 + 4*(n_groups+1)): n bytes of (sign << 7) | mantissa
+//   chunks_off = plane_off + rup16(n): per group [u32 init[32]][u16 words...]
+//   zero-padded to 16 B; blob_bytes = end of the last group record.
+//   Everything the decode kernels call a "chunk" below is one group.
 //   Coder 2 codes the pair (2k, 2k+1) as one symbol a*16 + b, a = e - e_lo
 //   for e in [e_lo, e_lo + 14] else 15 (escape; the exponent byte is stored in
 //   the record's escape list); its records are [u32 init[32]][u32 n_words]
@@ -36,16 +42,18 @@ constexpr uint32_t kXcTableWords = 2 * kXcMaxTable;   // u32 words per tensor's 
 constexpr uint32_t kXcPairRecHdr = 144;     // pair-coder record: 128 B states + 16 B counts
 
 // Device-side tensor descriptor of a decode plan.  The host fills the first
-// block; the table-build kernel fills the parsed header fields.
+// block; the table-build kernel fills the parsed header fields.  Its "chunks"
+// are the blob's state groups (chunk_elems / groups values each).
 struct XcTensorDev {
     const uint8_t *blob;
     uint64_t blob_bytes;
     uint16_t *out;
     uint64_t n;
-    uint32_t chunk_elems;
-    uint32_t n_chunks;
-    uint32_t chunk_begin;     // d_out holds element chunk_begin * chunk_elems first
+    uint32_t chunk_elems;     // values per group
+    uint32_t n_chunks;        // groups in the tensor
+    uint32_t chunk_begin;     // first group decoded; d_out holds element chunk_begin * chunk_elems first
     uint32_t aux;             // pair coder: first exponent of the 15-wide window (from the header)
+    uint32_t groups;          // groups per chunk in the header (1: format version 1)
     // parsed from the blob header by xc_prepare_kernel
     uint64_t chunks_off;
     uint64_t plane_off;
@@ -157,8 +165,6 @@ struct ParStream {
 namespace bsg {
 cudaError_t launch_xc_prepare(XcTensorDev *d_tens, int n_tensors, uint32_t *d_tables,
                               uint32_t *d_errs, cudaStream_t s);
-cudaError_t launch_stream_mix(const void *d_in, void *d_out, uint64_t units, int rd, int wr, int grid,
-                              cudaStream_t s);
 constexpr uint32_t kXcAllCoders = 7u;   // BS_CODER_RANS | TANS | RANS_PAIR bits
 // Union of the tensors' coder masks (a zero mask counts as every coder).
 uint32_t xc_launch_mask(const XcTensorDev *h_tens, int n);
@@ -185,9 +191,12 @@ cudaError_t launch_par_merge(const ParStream *d_streams, int n_streams_total, co
                              cudaStream_t s);
 
 cudaError_t launch_xc_encode(const uint16_t *d_in, uint64_t n, int coder, int prec,
-                             uint32_t chunk_elems, uint8_t *d_out, uint64_t out_cap,
+                             uint32_t chunk_elems, uint32_t groups, uint8_t *d_out, uint64_t out_cap,
                              uint64_t *d_out_len, uint8_t *d_ws, uint64_t ws_bytes,
                              cudaStream_t s);
 uint64_t xc_encode_workspace(uint64_t n, uint32_t chunk_elems, int coder);
 uint64_t xc_encode_bound(uint64_t n, uint32_t chunk_elems);
+// (workspace and bound take the values per group; launch_xc_encode codes
+// groups of chunk_elems values and writes a header of chunks of
+// chunk_elems * groups values)
 }  // namespace bsg

@@ -124,9 +124,15 @@ __global__ void __launch_bounds__(256) xc_prepare_kernel(XcTensorDev *tens, uint
             uint64_t n = h64[1];
             uint32_t ce = h32[4], nc = h32[5], lanes = h32[6], aux = h32[7];
             uint64_t co = h64[4], po = h64[5], total = h64[6];
-            const uint64_t po_want = (kXcTabOff + 4ull * (nc + 1ull) + 15) & ~15ull;
-            if (h32[0] != kXcMagic || ver != 1 || coder > 2 || prec < 8 || prec > 12 || n != T.n ||
-                ce != T.chunk_elems || nc != T.n_chunks || lanes != kXcLanes || po != po_want ||
+            // the offset table has one entry per group (T.n_chunks) plus one
+            const uint64_t po_want = (kXcTabOff + 4ull * (T.n_chunks + 1ull) + 15) & ~15ull;
+            // version 1: one group per chunk; version 2: G groups per chunk
+            const uint32_t G = ver == 2 ? h32[14] : 1u;
+            const uint64_t ce_want = static_cast<uint64_t>(T.chunk_elems) * T.groups;
+            const bool groups_ok = (ver == 1 && T.groups == 1) ||
+                                   (ver == 2 && G == T.groups && h32[15] == 0);
+            if (h32[0] != kXcMagic || !groups_ok || coder > 2 || prec < 8 || prec > 12 || n != T.n ||
+                ce != ce_want || nc != (n + ce_want - 1) / ce_want || lanes != kXcLanes || po != po_want ||
                 co != po + ((n + 15) & ~15ull) || total < co || (total & 15) || total > T.blob_bytes ||
                 (coder == 2 ? aux > 241 : aux != 0) ||
                 (T.coder_mask != 0 && coder <= 2 && !((T.coder_mask >> coder) & 1u)))

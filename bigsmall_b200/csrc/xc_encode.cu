@@ -120,10 +120,12 @@ __global__ void __launch_bounds__(256) xc_enc_hist_kernel(const uint16_t *__rest
 // for present symbols; a positive remainder goes to the most frequent symbol
 // (lowest index on ties); an excess is taken from the most frequent symbols,
 // never below 1; a single present symbol gets M-1 plus a phantom neighbour.
+// `ce` / `nc` are the values per state group and the group count (the coded
+// units); the header names chunks of ce * groups values.
 __global__ void __launch_bounds__(256) xc_enc_setup_kernel(const unsigned long long *counts, uint64_t n,
                                                            int coder, int prec, uint32_t ce, uint32_t nc,
-                                                           uint8_t *out, uint32_t *enc_tab, uint16_t *slot_list,
-                                                           const uint32_t *aux) {
+                                                           uint32_t groups, uint8_t *out, uint32_t *enc_tab,
+                                                           uint16_t *slot_list, const uint32_t *aux) {
     __shared__ int64_t f[256];
     __shared__ uint32_t s_cum[256];
     __shared__ uint8_t s_spread[kXcMaxTable];
@@ -217,16 +219,17 @@ __global__ void __launch_bounds__(256) xc_enc_setup_kernel(const unsigned long l
     if (tid == 0) {
         uint32_t *h32 = reinterpret_cast<uint32_t *>(out);
         uint64_t *h64 = reinterpret_cast<uint64_t *>(out);
+        const uint64_t ce_hdr = static_cast<uint64_t>(ce) * groups;
         h32[0] = kXcMagic;
-        h32[1] = 1u | (static_cast<uint32_t>(coder) << 16) | (static_cast<uint32_t>(prec) << 24);
+        h32[1] = (groups > 1 ? 2u : 1u) | (static_cast<uint32_t>(coder) << 16) | (static_cast<uint32_t>(prec) << 24);
         h64[1] = n;
-        h32[4] = ce;
-        h32[5] = nc;
+        h32[4] = static_cast<uint32_t>(ce_hdr);
+        h32[5] = static_cast<uint32_t>((n + ce_hdr - 1) / ce_hdr);
         h32[6] = kXcLanes;
         h32[7] = coder == BS_CODER_RANS_PAIR ? *aux : 0u;
         h64[4] = chunks_off;
         h64[5] = plane_off;
-        h64[7] = 0;
+        h64[7] = groups > 1 ? groups : 0u;   // version 2: u32 groups, u32 0
     }
     reinterpret_cast<uint16_t *>(out + kXcFreqOff)[tid] = static_cast<uint16_t>(f[tid]);
     // zero the two alignment pads
@@ -705,7 +708,7 @@ __global__ void __launch_bounds__(256) xc_enc_compact_kernel(const uint8_t *__re
     }
 }
 
-cudaError_t launch_xc_encode(const uint16_t *d_in, uint64_t n, int coder, int prec, uint32_t ce,
+cudaError_t launch_xc_encode(const uint16_t *d_in, uint64_t n, int coder, int prec, uint32_t ce, uint32_t groups,
                              uint8_t *d_out, uint64_t out_cap, uint64_t *d_out_len, uint8_t *d_ws,
                              uint64_t ws_bytes, cudaStream_t s) {
     const uint64_t nc = (n + ce - 1) / ce;
@@ -738,8 +741,8 @@ cudaError_t launch_xc_encode(const uint16_t *d_in, uint64_t n, int coder, int pr
         xc_enc_pair_hist_kernel<<<grid, 256, 0, s>>>(d_in, n, aux, pcounts);
         qcounts = pcounts;
     }
-    xc_enc_setup_kernel<<<1, 256, 0, s>>>(qcounts, n, coder, prec, ce, static_cast<uint32_t>(nc), d_out, tab,
-                                          slot_list, aux);
+    xc_enc_setup_kernel<<<1, 256, 0, s>>>(qcounts, n, coder, prec, ce, static_cast<uint32_t>(nc), groups, d_out,
+                                          tab, slot_list, aux);
     const unsigned enc_blocks = static_cast<unsigned>((nc + kEncWarps - 1) / kEncWarps);
     if (coder == BS_CODER_RANS_PAIR) {
         xc_enc_chunks_pair_kernel<<<enc_blocks, kEncWarps * 32, 0, s>>>(d_in, n, ce, static_cast<uint32_t>(nc), prec,

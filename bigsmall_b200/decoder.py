@@ -119,7 +119,7 @@ def verify(src) -> bool:
 
 def compress_tensors(tensors: dict, dst=None, coder: Optional[str] = None, prec: int = 12,
                      chunk_elems: int = exp_chunked.gpu.DEFAULT_CHUNK_ELEMS, raw_tiny: int = 512,
-                     with_md5: bool = True):
+                     with_md5: bool = True, groups: int = 1):
     """Encode a {name: torch.Tensor} dict into a container on the device.
 
     bf16 tensors of at least ``raw_tiny`` bytes use bf16_exp_chunked_v1 (the
@@ -144,9 +144,10 @@ def compress_tensors(tensors: dict, dst=None, coder: Optional[str] = None, prec:
         if tt.dtype == torch.bfloat16 and nbytes >= raw_tiny:
             x = tt.reshape(-1).cuda()
             if enc is None or enc.max_elems < x.numel():
-                enc = gpu.XcEncoder(x.numel(), chunk_elems, coder, prec, device=x.device.index)
+                enc = gpu.XcEncoder(x.numel(), chunk_elems, coder, prec, device=x.device.index, groups=groups)
             blob = enc.encode(x).cpu().numpy().tobytes()
-            w.add(name, tt.shape, raw_dtype, exp_chunked.CODEC, blob, md5, gpu.xc_extras(chunk_elems, coder, prec))
+            w.add(name, tt.shape, raw_dtype, exp_chunked.CODEC, blob, md5,
+                  gpu.xc_extras(chunk_elems, coder, prec, groups))
         else:
             w.add(name, tt.shape, raw_dtype, "raw", tt.reshape(-1).view(torch.uint8).cpu().numpy().tobytes(), md5)
     if dst is not None:

@@ -170,16 +170,25 @@ class XcPlan(_Plan):
     entry; None (or a None element) means unknown, which launches every
     decode kernel.  A blob whose header names another coder fails with
     BS_DEV_HEADER rather than being skipped.
+
+    ``groups``: state groups per chunk of each blob (the container's
+    ``extra["groups"]``; 1 or None for a one-group, format-version-1 blob),
+    one for all entries or a sequence with one per entry.
     """
 
     def __init__(self, entries: Iterable[tuple], device: Optional[int] = None, coders=None,
-                 max_ctas: Optional[int] = None):
+                 max_ctas: Optional[int] = None, groups=None):
         entries = list(entries)
         if coders is None or isinstance(coders, (str, int)):
             coders = [coders] * len(entries)
         coders = list(coders)
         if len(coders) != len(entries):
             raise ValueError("coders must have one element per entry")
+        if groups is None or isinstance(groups, int):
+            groups = [groups] * len(entries)
+        groups = list(groups)
+        if len(groups) != len(entries):
+            raise ValueError("groups must have one element per entry")
         keep = []
         arr = (_lib.XcTensor * max(1, len(entries)))()
         dev = device
@@ -205,6 +214,7 @@ class XcPlan(_Plan):
             arr[i].chunk_begin = int(c0)
             arr[i].chunk_count = int(cc)
             arr[i].coder_mask = coder_mask(coders[i])
+            arr[i].groups = int(groups[i] or 1)
             keep += [blob, out]
         if dev is None:
             dev = torch.cuda.current_device()
@@ -305,9 +315,9 @@ def decode_se_into(codec: str, host_blob: bytes, d_blob: torch.Tensor, out: torc
 
 
 def decode_xc_into(blob: torch.Tensor, out: torch.Tensor, chunk_elems: int,
-                   stream=None, check: bool = True, coder=None) -> torch.Tensor:
+                   stream=None, check: bool = True, coder=None, groups: int = 1) -> torch.Tensor:
     """Decode one bf16_exp_chunked_v1 blob (device) into ``out`` (device)."""
-    with XcPlan([(blob, out, chunk_elems)], coders=coder) as p:
+    with XcPlan([(blob, out, chunk_elems)], coders=coder, groups=groups) as p:
         p.decode(stream)
         if check:
             p.check(stream)
@@ -324,34 +334,39 @@ def decode_par_into(host_blob: bytes, d_blob: torch.Tensor, out: torch.Tensor, n
 # ---------------------------------------------------------------------------
 # encoder
 # ---------------------------------------------------------------------------
-def encode_bound(n: int, chunk_elems: int = DEFAULT_CHUNK_ELEMS) -> int:
+def encode_bound(n: int, chunk_elems: int = DEFAULT_CHUNK_ELEMS, groups: int = 1) -> int:
     v = ctypes.c_uint64()
-    _lib.check(_lib.load().bs_xc_encode_bound(n, chunk_elems, ctypes.byref(v)), "bs_xc_encode_bound")
+    _lib.check(_lib.load().bs_xc_encode_bound(n, chunk_elems, groups, ctypes.byref(v)), "bs_xc_encode_bound")
     return int(v.value)
 
 
-def encode_workspace(n: int, chunk_elems: int = DEFAULT_CHUNK_ELEMS, coder: str = DEFAULT_CODER) -> int:
+def encode_workspace(n: int, chunk_elems: int = DEFAULT_CHUNK_ELEMS, coder: str = DEFAULT_CODER,
+                     groups: int = 1) -> int:
     v = ctypes.c_uint64()
     c = CODERS[coder] if isinstance(coder, str) else int(coder)
-    _lib.check(_lib.load().bs_xc_encode_workspace(n, chunk_elems, c, ctypes.byref(v)), "bs_xc_encode_workspace")
+    _lib.check(_lib.load().bs_xc_encode_workspace(n, chunk_elems, groups, c, ctypes.byref(v)),
+               "bs_xc_encode_workspace")
     return int(v.value)
 
 
 class XcEncoder:
     """Reusable device encoder: owns an output buffer and a workspace sized for
-    tensors of up to ``max_elems`` values (no allocation per call)."""
+    tensors of up to ``max_elems`` values (no allocation per call).  Chunks of
+    ``chunk_elems`` values are cut into ``groups`` state groups."""
 
     def __init__(self, max_elems: int, chunk_elems: int = DEFAULT_CHUNK_ELEMS, coder: str = DEFAULT_CODER,
-                 prec: int = DEFAULT_PREC, device=None):
+                 prec: int = DEFAULT_PREC, device=None, groups: int = 1):
         self.chunk_elems = int(chunk_elems)
+        self.groups = int(groups or 1)
         self.coder = CODERS[coder] if isinstance(coder, str) else int(coder)
         self.prec = int(prec)
         self.max_elems = int(max_elems)
         dev = torch.device("cuda", device if device is not None else torch.cuda.current_device())
         self.device = dev
-        self.out = torch.empty(max(16, encode_bound(max_elems, chunk_elems)), dtype=torch.uint8, device=dev)
-        self.ws = torch.empty(max(16, encode_workspace(max_elems, chunk_elems, self.coder)), dtype=torch.uint8,
-                              device=dev)
+        self.out = torch.empty(max(16, encode_bound(max_elems, chunk_elems, self.groups)), dtype=torch.uint8,
+                               device=dev)
+        self.ws = torch.empty(max(16, encode_workspace(max_elems, chunk_elems, self.coder, self.groups)),
+                              dtype=torch.uint8, device=dev)
         self.out_len = torch.zeros(2, dtype=torch.int64, device=dev)
 
     def encode_async(self, x: torch.Tensor, stream=None) -> None:
@@ -363,7 +378,7 @@ class XcEncoder:
         if n > self.max_elems:
             raise ValueError(f"tensor of {n} values exceeds encoder capacity {self.max_elems}")
         L = _lib.load()
-        rc = L.bs_xc_encode(x.data_ptr() if n else None, n, self.coder, self.prec, self.chunk_elems,
+        rc = L.bs_xc_encode(x.data_ptr() if n else None, n, self.coder, self.prec, self.chunk_elems, self.groups,
                             self.out.data_ptr(), self.out.numel(), self.out_len.data_ptr(),
                             self.ws.data_ptr(), self.ws.numel(), _stream_ptr(stream, self.device))
         _lib.check(rc, "bs_xc_encode")
@@ -378,7 +393,7 @@ class XcEncoder:
         if n > self.max_elems:
             raise ValueError(f"tensor of {n} values exceeds encoder capacity {self.max_elems}")
         L = _lib.load()
-        rc = L.bs_xc_encode(x.data_ptr() if n else None, n, self.coder, self.prec, self.chunk_elems,
+        rc = L.bs_xc_encode(x.data_ptr() if n else None, n, self.coder, self.prec, self.chunk_elems, self.groups,
                             out.data_ptr(), out.numel(), out_len.data_ptr(), self.ws.data_ptr(), self.ws.numel(),
                             _stream_ptr(stream, self.device))
         _lib.check(rc, "bs_xc_encode")
@@ -391,15 +406,25 @@ class XcEncoder:
 
 
 def encode_xc(x: torch.Tensor, coder: str = DEFAULT_CODER, prec: int = DEFAULT_PREC,
-              chunk_elems: int = DEFAULT_CHUNK_ELEMS, stream=None) -> torch.Tensor:
+              chunk_elems: int = DEFAULT_CHUNK_ELEMS, stream=None, groups: int = 1) -> torch.Tensor:
     """Encode a bf16 CUDA tensor into a bf16_exp_chunked_v1 blob on the device."""
-    enc = XcEncoder(max(1, x.numel()), chunk_elems, coder, prec, device=_dev_index(x))
+    enc = XcEncoder(max(1, x.numel()), chunk_elems, coder, prec, device=_dev_index(x), groups=groups)
     return enc.encode(x.reshape(-1), stream)
 
 
-def xc_extras(chunk_elems: int = DEFAULT_CHUNK_ELEMS, coder: str = DEFAULT_CODER, prec: int = DEFAULT_PREC) -> dict:
-    """The per-tensor ``extra`` dict the container header stores for the codec."""
-    return {"chunk_elems": int(chunk_elems), "coder": coder, "prec": int(prec)}
+def xc_extras(chunk_elems: int = DEFAULT_CHUNK_ELEMS, coder: str = DEFAULT_CODER, prec: int = DEFAULT_PREC,
+              groups: int = 1) -> dict:
+    """The per-tensor ``extra`` dict the container header stores for the codec
+    (``groups`` only when a chunk holds more than one state group)."""
+    d = {"chunk_elems": int(chunk_elems), "coder": coder, "prec": int(prec)}
+    if int(groups or 1) > 1:
+        d["groups"] = int(groups)
+    return d
+
+
+def extras_groups(extra: Optional[dict]) -> int:
+    """State groups per chunk recorded in a tensor's ``extra`` dict (1 if absent)."""
+    return int((extra or {}).get("groups", 1) or 1)
 
 
 def aligned_view(buf: torch.Tensor, offset: int, nbytes: int) -> torch.Tensor:
@@ -417,5 +442,5 @@ def sync(device=None) -> None:
 
 __all__: Sequence[str] = [
     "DEFAULT_CHUNK_ELEMS", "DEFAULT_PREC", "DEFAULT_CODER", "SePlan", "decode_se_into", "SE_CODECS", "SERIAL_CODECS", "XcPlan", "ParPlan", "XcEncoder", "decode_xc_into",
-    "decode_par_into", "encode_xc", "encode_bound", "encode_workspace", "xc_extras", "aligned_view",
+    "decode_par_into", "encode_xc", "encode_bound", "encode_workspace", "xc_extras", "extras_groups", "aligned_view",
 ]

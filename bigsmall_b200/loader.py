@@ -198,7 +198,7 @@ class DeviceLoader:
         for g in groups:
             g.host_spans = [(layout[p.name][0], layout[p.name][1], layout[p.name][2])
                             for p in g.parts if p.meta["codec"] != "tied_ref"]
-            xc_entries, xc_coders, se_entries = [], [], []
+            xc_entries, xc_coders, xc_groups, se_entries = [], [], [], []
             for p in g.parts:
                 m = p.meta
                 _, d, nb = layout[p.name]
@@ -208,6 +208,7 @@ class DeviceLoader:
                     out = self.out[p.name].reshape(-1).view(torch.int16)
                     xc_entries.append((blob, out, ce, _ct.n_elements(m["shape"]), p.chunk_begin, p.chunk_count))
                     xc_coders.append((m.get("extra") or {}).get("coder"))
+                    xc_groups.append(gpu.extras_groups(m.get("extra")))
                 elif m["codec"] in gpu.SERIAL_CODECS:
                     n = _ct.n_elements(m["shape"])
                     out = self.out[p.name].reshape(-1).view(torch.int16)
@@ -220,7 +221,8 @@ class DeviceLoader:
             if se_entries:   # serial-stream tensors of the group: one plan, all streams concurrent
                 g.plans.append(gpu.SePlan(se_entries, device=self.device.index))
             if xc_entries:
-                g.plans.insert(0, gpu.XcPlan(xc_entries, device=self.device.index, coders=xc_coders))
+                g.plans.insert(0, gpu.XcPlan(xc_entries, device=self.device.index, coders=xc_coders,
+                                             groups=xc_groups))
             g.event = torch.cuda.Event()
 
     # -- run -------------------------------------------------------------------
@@ -411,7 +413,7 @@ class ResidentContainer:
         """outputs: {name: device tensor of the tensor's shape/dtype}.
         ``max_ctas`` caps the bf16_exp_chunked_v1 decode grid (see
         :meth:`bigsmall_b200.gpu.XcPlan.set_max_ctas`)."""
-        xc, coders, se, plans, copies = [], [], [], [], []
+        xc, coders, groups, se, plans, copies = [], [], [], [], [], []
         for name, out in outputs.items():
             real = self.resolve(name)
             m = self.image.tensors[real]
@@ -420,6 +422,7 @@ class ResidentContainer:
             if m["codec"] == "bf16_exp_chunked_v1":
                 xc.append((blob, flat.view(torch.int16), int((m.get("extra") or {})["chunk_elems"])))
                 coders.append((m.get("extra") or {}).get("coder"))
+                groups.append(gpu.extras_groups(m.get("extra")))
             elif m["codec"] in gpu.SERIAL_CODECS:
                 se.append((m["codec"], bytes(self.image.blob_host(real)), blob, flat.view(torch.int16),
                            _ct.n_elements(m["shape"])))
@@ -428,7 +431,8 @@ class ResidentContainer:
         if se:
             plans.append(gpu.SePlan(se, device=self.device.index))
         if xc:
-            plans.insert(0, gpu.XcPlan(xc, device=self.device.index, coders=coders, max_ctas=max_ctas))
+            plans.insert(0, gpu.XcPlan(xc, device=self.device.index, coders=coders, max_ctas=max_ctas,
+                                       groups=groups))
         return Bundle(plans, copies)
 
     def decode(self, names, stream=None) -> dict:

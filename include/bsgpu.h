@@ -56,11 +56,14 @@ typedef struct bs_plan bs_plan;
 
 /* One bf16_exp_chunked_v1 tensor (or a chunk range of one) to decode.  Both
  * pointers must be 16-byte aligned device addresses on the plan's device.
- * chunk_elems comes from the container header's per-tensor "extra" dict
- * (bigsmall/container.py:17-38 keeps codec extras there) and must match the
- * blob header.  Chunks [chunk_begin, chunk_begin + chunk_count) are decoded
- * (chunk_count 0: through the last chunk); d_out receives the value of element
- * chunk_begin * chunk_elems first.  Ranges let several GPUs share one tensor. */
+ * chunk_elems and groups come from the container header's per-tensor "extra"
+ * dict (bigsmall/container.py:17-38 keeps codec extras there) and must match
+ * the blob header.  A chunk is `groups` state groups of chunk_elems / groups
+ * values (a multiple of 256), each decoded by its own warp; groups 0 or 1 is a
+ * format-version-1 blob (one group per chunk).  Chunks [chunk_begin,
+ * chunk_begin + chunk_count) are decoded (chunk_count 0: through the last
+ * chunk); d_out receives the value of element chunk_begin * chunk_elems first.
+ * Ranges let several GPUs share one tensor. */
 typedef struct bs_xc_tensor {
     const void *d_blob;
     uint64_t    blob_bytes;
@@ -74,10 +77,12 @@ typedef struct bs_xc_tensor {
                                   of each coder its tensors may use; a blob whose
                                   coder is not in a nonzero mask fails with
                                   BS_DEV_HEADER instead of being decoded. */
+    uint32_t    groups;        /* state groups per chunk (0 or 1: one) */
+    uint32_t    reserved;      /* must be 0 */
 } bs_xc_tensor;
 
 /* ---- library ------------------------------------------------------------ */
-int         bs_version(void);                 /* 100*major + minor           */
+int         bs_version(void);                 /* 100*major + minor (1.01)    */
 const char *bs_last_error(void);              /* thread-local, never NULL    */
 const char *bs_status_string(int status);
 
@@ -198,27 +203,23 @@ int bs_se_parse(int codec, const uint8_t *h_blob, uint64_t blob_bytes,
                 uint64_t n_weights, uint32_t *n_streams_out);
 
 /* ---- bf16_exp_chunked_v1 encode (KV-cache compression) ------------------ */
-/* Worst-case blob size, and scratch size for one tensor with a given coder. */
-int bs_xc_encode_bound(uint64_t n_elems, uint32_t chunk_elems, uint64_t *bytes);
-int bs_xc_encode_workspace(uint64_t n_elems, uint32_t chunk_elems, int coder, uint64_t *bytes);
+/* Worst-case blob size, and scratch size for one tensor with a given coder,
+ * for chunks of chunk_elems values in `groups` state groups (0 or 1: one). */
+int bs_xc_encode_bound(uint64_t n_elems, uint32_t chunk_elems, uint32_t groups, uint64_t *bytes);
+int bs_xc_encode_workspace(uint64_t n_elems, uint32_t chunk_elems, uint32_t groups, int coder,
+                           uint64_t *bytes);
 
 /* Encode n_elems bf16 values at d_in into a bf16_exp_chunked_v1 blob at d_out
- * (capacity out_cap >= bs_xc_encode_bound).  The exact blob length is written
+ * (capacity out_cap >= bs_xc_encode_bound).  Chunks of chunk_elems values are
+ * cut into `groups` state groups (chunk_elems / groups must be a multiple of
+ * 256; groups > 1 writes format version 2).  The exact blob length is written
  * to the device u64 at d_out_len.  Deterministic: the bytes equal the CPU
  * reference encoder's.  Asynchronous on `stream`.
  * Replaces: bigsmall/codecs/kv_cache.py:41-83 compress_kv_entry's CPU encode. */
 int bs_xc_encode(const void *d_in, uint64_t n_elems, int coder, int prec,
-                 uint32_t chunk_elems, void *d_out, uint64_t out_cap,
+                 uint32_t chunk_elems, uint32_t groups, void *d_out, uint64_t out_cap,
                  uint64_t *d_out_len, void *d_workspace, uint64_t ws_bytes,
                  void *stream);
-
-/* ---- measurement helper (no reference counterpart) ------------------------
- * HBM calibration probe: `units` x 16-byte words per stream; reads rd streams
- * of d_in and writes wr streams of d_out (d_in holds rd*units*16 bytes, d_out
- * wr*units*16), grid-stride over `grid` CTAs of 256 threads, with the
- * decoder's load/store instructions.  (rd, wr) in {(1,1), (2,3), (0,1)}: 2:3 is
- * the decode's DRAM read:write mix, so its rate is that mix's practical ceiling. */
-int bs_stream_probe(const void *d_in, void *d_out, uint64_t units, int rd, int wr, int grid, void *stream);
 
 #ifdef __cplusplus
 }

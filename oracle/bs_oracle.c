@@ -856,20 +856,25 @@ int bso_tans_decode(const uint8_t *blob, int64_t len, int64_t n_weights, uint16_
 /* bf16_exp_chunked_v1 -- this project's chunked format (no reference       */
 /* counterpart).  Layout (little-endian; sections in this fixed order, each  */
 /* 16-byte aligned):                                                         */
-/*   0   "BSXC"   4 u16 version=1   6 u8 coder (0 rANS, 1 tANS)   7 u8 P     */
+/*   0   "BSXC"   4 u16 version (1, or 2 with groups)   6 u8 coder (0 rANS, */
+/*       1 tANS, 2 pair rANS)   7 u8 P                                       */
 /*   8   u64 n    16 u32 chunk_elems   20 u32 n_chunks   24 u32 lanes=32     */
-/*   28  u32 flags=0  32 u64 chunks_off  40 u64 plane_off  48 u64 blob_bytes */
-/*   56  u64 0    64 u16 freq[256]                                           */
-/*   576 u32 chunk_start[n_chunks+1] (16-byte units from chunks_off)         */
-/*   plane_off  = rup16(576 + 4*(n_chunks+1)): n bytes (sign<<7 | mantissa)  */
-/*   chunks_off = plane_off + rup16(n): per chunk [u32 init[32]][u16 words]  */
+/*   28  u32 aux  32 u64 chunks_off  40 u64 plane_off  48 u64 blob_bytes     */
+/*   56  version 1: u64 0; version 2: u32 groups G, u32 0                    */
+/*   64  u16 freq[256]                                                       */
+/* A chunk of chunk_elems values is G state groups of chunk_elems/G values   */
+/* (a multiple of 256; version 1 is G = 1); group k holds elements           */
+/* [k*ge, min(n, (k+1)*ge)), ge = chunk_elems/G, n_groups = ceil(n/ge).      */
+/*   576 u32 group_start[n_groups+1] (16-byte units from chunks_off)         */
+/*   plane_off  = rup16(576 + 4*(n_groups+1)): n bytes (sign<<7 | mantissa)  */
+/*   chunks_off = plane_off + rup16(n): per group [u32 init[32]][u16 words]  */
 /*                zero-padded to 16 bytes; blob_bytes = end of last record.  */
-/* Element e of a chunk belongs to lane (e%256)/8 at step (e/256)*8 + e%8.  */
+/* Element e of a group belongs to lane (e%256)/8 at step (e/256)*8 + e%8.  */
 /* Coder 2 (rANS over exponent pairs): header u32 at 28 = e_lo; exponent e  */
 /* maps to a = e - e_lo when 0 <= e - e_lo <= 14, else a = 15 (escape); the */
 /* symbol of elements (2k, 2k+1) is a*16 + b (b = 0 for a missing second    */
 /* element); lane l codes pair-steps s2 (element (s2/4)*256 + l*8 +         */
-/* 2*(s2%4)); a chunk record is [u32 init[32]][u32 n_words][u32 n_esc][u32  */
+/* 2*(s2%4)); a group record is [u32 init[32]][u32 n_words][u32 n_esc][u32  */
 /* 0][u32 0][u16 words][u8 escape exponents, in step/lane/a-then-b order].  */
 /* ======================================================================== */
 #define XC_HDR 64
@@ -1170,7 +1175,17 @@ static int xc2_decode_chunk(const uint8_t *rec, int64_t rec_bytes, int64_t cn, i
 
 int64_t bso_xc_encode(const uint16_t *w, int64_t n, int coder, int prec, uint32_t chunk_elems,
                       uint8_t *out, int64_t cap) {
+    return bso_xc_encode_groups(w, n, coder, prec, chunk_elems, 1, out, cap);
+}
+
+/* The records of a G-group blob are those of a one-group blob with       */
+/* chunk_elems / G values per chunk; only the header's chunk fields and    */
+/* version differ.  Below, "chunk" is the coded unit (the group).           */
+int64_t bso_xc_encode_groups(const uint16_t *w, int64_t n, int coder, int prec, uint32_t chunk_elems_hdr,
+                             uint32_t groups, uint8_t *out, int64_t cap) {
     if (n == 0) return 0;
+    if (groups == 0 || chunk_elems_hdr == 0 || chunk_elems_hdr % groups) return BSO_E_ARG;
+    const uint32_t chunk_elems = chunk_elems_hdr / groups;   /* values per group */
     if (coder < 0 || coder > 2 || prec < 8 || prec > 12 || chunk_elems == 0 || (chunk_elems & 255))
         return BSO_E_ARG;
     int64_t nc64 = (n + chunk_elems - 1) / chunk_elems;
@@ -1230,18 +1245,18 @@ int64_t bso_xc_encode(const uint16_t *w, int64_t n, int coder, int prec, uint32_
     wr32(out + XC_TAB_OFF + 4 * nc, (uint32_t)((pos - chunks_off) / 16));
     int64_t total = pos;
     memcpy(out, "BSXC", 4);
-    wr16(out + 4, 1);
+    wr16(out + 4, groups > 1 ? 2 : 1);
     out[6] = (uint8_t)coder;
     out[7] = (uint8_t)prec;
     wr64(out + 8, (uint64_t)n);
-    wr32(out + 16, chunk_elems);
-    wr32(out + 20, nc);
+    wr32(out + 16, chunk_elems_hdr);
+    wr32(out + 20, (uint32_t)((n + chunk_elems_hdr - 1) / chunk_elems_hdr));
     wr32(out + 24, XC_LANES);
     wr32(out + 28, (uint32_t)e_lo);
     wr64(out + 32, (uint64_t)chunks_off);
     wr64(out + 40, (uint64_t)plane_off);
     wr64(out + 48, (uint64_t)total);
-    wr64(out + 56, 0);
+    wr64(out + 56, groups > 1 ? (uint64_t)groups : 0);
     for (int s = 0; s < 256; s++) wr16(out + XC_FREQ_OFF + 2 * s, freq[s]);
     return total;
 }
@@ -1250,18 +1265,25 @@ int bso_xc_decode(const uint8_t *blob, int64_t len, int64_t n_weights, uint16_t 
     if (n_weights == 0 || len == 0) return BSO_OK;
     if (len < XC_TAB_OFF) return BSO_E_TRUNC;
     if (memcmp(blob, "BSXC", 4) != 0) return BSO_E_MAGIC;
-    if (rd16(blob + 4) != 1) return BSO_E_CORRUPT;
+    const uint32_t ver = rd16(blob + 4);
+    if (ver != 1 && ver != 2) return BSO_E_CORRUPT;
     int coder = blob[6], P = blob[7];
     int64_t n = (int64_t)rd64(blob + 8);
-    uint32_t ce = rd32(blob + 16), nc = rd32(blob + 20), lanes = rd32(blob + 24);
+    uint32_t ce_hdr = rd32(blob + 16), nc_hdr = rd32(blob + 20), lanes = rd32(blob + 24);
     int64_t chunks_off = (int64_t)rd64(blob + 32), plane_off = (int64_t)rd64(blob + 40);
     int64_t total = (int64_t)rd64(blob + 48);
     if (n != n_weights) return BSO_E_COUNT;
     const uint32_t aux = rd32(blob + 28);
+    /* version 2: G groups per chunk; decode works per group ("chunk" below) */
+    const uint32_t G = ver == 2 ? rd32(blob + 56) : 1u;
+    if (G == 0 || (ver == 2 && rd32(blob + 60) != 0) || ce_hdr == 0 || ce_hdr % G) return BSO_E_CORRUPT;
+    if ((int64_t)nc_hdr != (n + ce_hdr - 1) / ce_hdr) return BSO_E_CORRUPT;
+    const uint32_t ce = ce_hdr / G;
     if (coder < 0 || coder > 2 || P < 8 || P > 12 || lanes != XC_LANES || ce == 0 || (ce & 255))
         return BSO_E_CORRUPT;
     if (coder == 2 ? aux > 241 : aux != 0) return BSO_E_CORRUPT;
-    if ((int64_t)nc != (n + ce - 1) / ce) return BSO_E_CORRUPT;
+    if ((n + ce - 1) / ce > 0x7FFFFFFFll) return BSO_E_CORRUPT;
+    const uint32_t nc = (uint32_t)((n + ce - 1) / ce);
     if (plane_off != rup16(XC_TAB_OFF + 4 * ((int64_t)nc + 1)) || chunks_off != plane_off + rup16(n) ||
         (total & 15) || total < chunks_off)
         return BSO_E_CORRUPT;

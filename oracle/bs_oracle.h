@@ -77,6 +77,10 @@ int bso_tans_decode(const uint8_t *blob, int64_t len, int64_t n_weights,
 int64_t bso_xc_bound(int64_t n, uint32_t chunk_elems);
 int64_t bso_xc_encode(const uint16_t *w, int64_t n, int coder, int prec,
                       uint32_t chunk_elems, uint8_t *out, int64_t cap);
+/* chunk_elems values per chunk in `groups` state groups (format version 2
+ * when groups > 1; groups == 1 is bso_xc_encode). */
+int64_t bso_xc_encode_groups(const uint16_t *w, int64_t n, int coder, int prec,
+                             uint32_t chunk_elems, uint32_t groups, uint8_t *out, int64_t cap);
 int bso_xc_decode(const uint8_t *blob, int64_t len, int64_t n_weights,
                   uint16_t *out);
 /* Quantised exponent frequencies the format uses (for tests). */

@@ -67,6 +67,7 @@ def lib():
         "bso_tans_decode_many": (I32, [P, P, P, P, I32, I32]),
         "bso_xc_bound": (I64, [I64, U32]),
         "bso_xc_encode": (I64, [P, I64, I32, I32, U32, P, I64]),
+        "bso_xc_encode_groups": (I64, [P, I64, I32, I32, U32, U32, P, I64]),
         "bso_xc_decode": (I32, [P, I64, I64, P]),
         "bso_xc_quantise": (I32, [P, I32, P]),
         "bso_xc_decode_many": (I32, [P, P, P, P, I32, I32]),
@@ -173,8 +174,19 @@ def tans_decode(blob, n_weights: int) -> bytes:
     return _dec("tans", blob, n_weights)
 
 
-def xc_encode(raw, coder: int = 0, prec: int = 12, chunk_elems: int = 65536) -> bytes:
-    return _enc("xc", raw, coder, prec, chunk_elems)
+def xc_encode(raw, coder: int = 0, prec: int = 12, chunk_elems: int = 65536, groups: int = 1) -> bytes:
+    """bf16_exp_chunked_v1 blob; `groups` > 1 cuts each chunk into that many
+    state groups (format version 2)."""
+    if groups == 1:
+        return _enc("xc", raw, coder, prec, chunk_elems)
+    w = _u16(raw)
+    n = len(w)
+    L = lib()
+    ge = chunk_elems // groups if groups > 0 else 0
+    out = np.empty(max(L.bso_xc_bound(n, ge) if ge else 16, 16), dtype=np.uint8)
+    nb = _check(L.bso_xc_encode_groups(_ptr(w), n, coder, prec, chunk_elems, groups, _ptr(out), len(out)),
+                "xc_encode_groups")
+    return out[:nb].tobytes()
 
 
 def xc_decode(blob, n_weights: int) -> bytes:

@@ -24,11 +24,16 @@ def test_library_loads_and_exports_every_symbol():
     lib = _lib.load()
     for name in _declared():
         assert hasattr(lib, name), name
-    assert lib.bs_version() == 100
+    assert lib.bs_version() == 101
     assert lib.bs_status_string(5) == b"corrupt stream"
     out = subprocess.run(["nm", "-D", "--defined-only", _lib.LIB_PATH], capture_output=True, text=True).stdout
     exported = set(re.findall(r" T (bs_\w+)", out))
     assert _declared() <= exported
+    # measurement tooling lives in its own library, outside the product ABI
+    assert "bs_stream_probe" not in exported
+    calib = os.path.join(os.path.dirname(_lib.LIB_PATH), "libbscalib.so")
+    out = subprocess.run(["nm", "-D", "--defined-only", calib], capture_output=True, text=True).stdout
+    assert re.findall(r" T (bs_\w+)", out) == ["bs_stream_probe"]
 
 
 def test_host_side_validation_without_gpu():
@@ -37,13 +42,15 @@ def test_host_side_validation_without_gpu():
     from bigsmall_b200 import _lib
     lib = _lib.load()
     v = ctypes.c_uint64()
-    assert lib.bs_xc_encode_bound(1000, 100, ctypes.byref(v)) == _lib.BS_E_INVALID_ARG
-    assert lib.bs_xc_encode_bound(1000, 256, ctypes.byref(v)) == 0 and v.value > 2000
+    assert lib.bs_xc_encode_bound(1000, 100, 1, ctypes.byref(v)) == _lib.BS_E_INVALID_ARG
+    assert lib.bs_xc_encode_bound(1000, 256, 1, ctypes.byref(v)) == 0 and v.value > 2000
+    assert lib.bs_xc_encode_bound(1000, 256, 0, ctypes.byref(v)) == 0      # 0 groups: one
+    # chunk_elems / groups must be a positive multiple of 256
+    for ce, g, ok in ((8192, 4, True), (8192, 3, False), (1024, 8, False), (1 << 22, 128, True)):
+        assert (lib.bs_xc_encode_bound(1000, ce, g, ctypes.byref(v)) == 0) == ok, (ce, g)
     for coder, ok in ((0, True), (1, True), (2, True), (3, False), (-1, False)):
-        rc = lib.bs_xc_encode_workspace(100_000, 4096, coder, ctypes.byref(v))
+        rc = lib.bs_xc_encode_workspace(100_000, 4096, 1, coder, ctypes.byref(v))
         assert (rc == 0) == ok, coder
-    assert lib.bs_stream_probe(None, None, 16, 3, 3, 1, None) == _lib.BS_E_INVALID_ARG
-    assert lib.bs_stream_probe(None, None, 16, 2, 3, 1, None) == _lib.BS_E_INVALID_ARG
     h = ctypes.c_void_p()
     # no CUDA device in a CPU-only container: creation must fail cleanly
     rc = lib.bs_xc_plan_create(None, 0, 0, ctypes.byref(h))

@@ -170,3 +170,40 @@ def test_xc_special_value_distributions(kind, coder, prec):
         raw = _special(kind, n)
         blob = O.xc_encode(raw, coder, prec, 4096)
         assert O.xc_decode(blob, n) == raw, (kind, coder, prec, n)
+
+
+# ---- state groups per chunk (format version 2) -----------------------------
+@pytest.mark.parametrize("coder", [0, 1, 2])
+@pytest.mark.parametrize("chunk,groups", [(4096, 2), (65536, 8), (65536, 256), (1 << 20, 32), (1 << 21, 64)])
+def test_xc_groups_roundtrip_and_layout(manifest, coder, chunk, groups):
+    """A chunk of `chunk` values in `groups` state groups: the blob decodes
+    exactly, and everything past the header equals the one-group blob with
+    chunk / groups values per chunk (the group records, offset table, plane
+    and frequency table are the same bytes)."""
+    for name, c in manifest["cases"].items():
+        raw = golden_bytes(f"{name}.raw")
+        blob = O.xc_encode(raw, coder, 12, chunk, groups)
+        assert md5(O.xc_decode(blob, c["n"])) == c["raw_md5"], (name, coder, chunk, groups)
+        one = O.xc_encode(raw, coder, 12, chunk // groups)
+        assert blob[64:] == one[64:] and len(blob) == len(one)
+        ver = struct.unpack_from("<H", blob, 4)[0]
+        n, ce, nc = struct.unpack_from("<QII", blob, 8)
+        g, zero = struct.unpack_from("<II", blob, 56)
+        assert (ver, ce, nc, g, zero) == (2, chunk, -(-c["n"] // chunk), groups, 0)
+
+
+@pytest.mark.parametrize("coder", [0, 2])
+def test_xc_groups_header_checked(coder):
+    rng = np.random.default_rng(7)
+    raw = (rng.standard_normal(70001).astype(np.float32).view(np.uint32) >> 16).astype(np.uint16).tobytes()
+    blob = O.xc_encode(raw, coder, 12, 65536, 8)
+    assert O.xc_decode(blob, 70001) == raw
+    for off, val in ((56, 0), (56, 3), (56, 16), (60, 1), (16, 65536 + 256), (20, 1), (4, 3)):
+        bad = bytearray(blob)
+        struct.pack_into("<H" if off == 4 else "<I", bad, off, val)
+        with pytest.raises(O.OracleError):
+            O.xc_decode(bytes(bad), 70001)
+    with pytest.raises(O.OracleError):       # chunk / groups below 256 values
+        O.xc_encode(raw, coder, 12, 4096, 32)
+    with pytest.raises(O.OracleError):       # chunk not a multiple of groups
+        O.xc_encode(raw, coder, 12, 65536, 3)

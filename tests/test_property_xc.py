@@ -38,9 +38,10 @@ def bf16_tensors(draw):
 
 @settings(max_examples=150, deadline=None)
 @given(raw=bf16_tensors(), coder=st.sampled_from([0, 1, 2]), prec=st.integers(8, 12),
-       chunk=st.sampled_from([256, 512, 4096, 32768]))
-def test_any_tensor_round_trips(raw, coder, prec, chunk):
-    blob = O.xc_encode(raw, coder, prec, chunk)
+       chunk=st.sampled_from([256, 512, 4096, 32768]), groups=st.sampled_from([1, 1, 2, 4, 16]))
+def test_any_tensor_round_trips(raw, coder, prec, chunk, groups):
+    chunk *= groups                       # `groups` state groups of `chunk` values per chunk
+    blob = O.xc_encode(raw, coder, prec, chunk, groups)
     assert len(blob) % 16 == 0
     assert O.xc_decode(blob, len(raw) // 2) == raw
 
