@@ -418,12 +418,14 @@ def main():
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     # per step, events around the decode kernels alone (after the table build)
     kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(a.steps)]
+    launches0 = plan.launch_count()
     with ClockSampler(local) as clk:
         s.record(stream)
         for k0, k1 in kev:
             plan.decode_timed(k0, k1, stream)
         e.record(stream)
         torch.cuda.synchronize()
+    timed_launches = plan.launch_count() - launches0
     plan.check(stream)
     local_ms = s.elapsed_time(e) / a.steps
     kernel_ms = sum(k0.elapsed_time(k1) for k0, k1 in kev) / a.steps
@@ -472,6 +474,7 @@ def main():
                "verified": "per-span 16-bit checksums equal on every rank and equal to the owners' originals"
                if rep_ok else "MISMATCH"}
     total_elems = sum_over_ranks(dec_elems)
+    total_launches = int(sum_over_ranks(timed_launches))
     total_comp = sum_over_ranks(sum(int(image.tensors[n]["compressed_bytes"]) for n in image.tensors))
     h2d = loader.h2d_bytes()
     if rank == 0:
@@ -501,7 +504,10 @@ def main():
                 "ms_per_step": round(e2e_ms, 3),
                 "path": "bigsmall_b200.loader.DeviceLoader.run_async (pinned H2D of compressed blobs "
                         f"in {n_groups} groups overlapped with decode) + status check"},
-            "gpu_launches": 2 * a.steps,
+            "gpu_launches": total_launches,
+            "gpu_launches_note": "kernels the decode plans launched in the timed region on all ranks, counted by "
+                                 "the library (bs_plan_launch_count): per step the table build plus one decode "
+                                 "kernel per coder",
             "replicate": rep,
             "clocks": clk.summary(),
             "verified": f"bitwise equal on device for all {len(tensors)} tensors" if n_bad == 0 else f"MISMATCH in {n_bad} parts",

@@ -79,6 +79,7 @@ SIGNATURES = {
     "bs_plan_decode_handoff": (_I, [_P, _P, _P, _P, _P, _P]),
     "bs_plan_check": (_I, [_P, _P, ctypes.POINTER(_U32)]),
     "bs_plan_n_tensors": (_I, [_P]),
+    "bs_plan_launch_count": (_I, [_P, ctypes.POINTER(_U64)]),
     "bs_plan_set_max_ctas": (_I, [_P, _I]),
     "bs_plan_destroy": (_I, [_P]),
     "bs_xc_decode_noalloc": (_I, [ctypes.POINTER(XcTensor), _I, _P, ctypes.POINTER(_U32)]),

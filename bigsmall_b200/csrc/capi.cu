@@ -99,6 +99,7 @@ struct bs_plan {
     uint32_t *d_seg_stream = nullptr;
     int n_segs = 0;
     uint32_t *d_hist = nullptr;
+    uint64_t launches = 0;          // kernels this plan has launched (bs_plan_launch_count)
 };
 
 namespace {
@@ -213,6 +214,12 @@ int bs_plan_set_max_ctas(bs_plan *p, int max_ctas) {
 
 int bs_plan_n_tensors(const bs_plan *plan) { return plan ? plan->n_tensors : 0; }
 
+int bs_plan_launch_count(const bs_plan *plan, uint64_t *count) {
+    if (!plan || !count) return fail(BS_E_INVALID_ARG, "plan or count is NULL");
+    *count = plan->launches;
+    return BS_OK;
+}
+
 int bs_plan_destroy(bs_plan *plan) {
     free_plan(plan);
     return BS_OK;
@@ -310,24 +317,36 @@ static int plan_decode(bs_plan *p, void *stream, void *ev_start, void *ev_stop) 
     if (p->kind == kPlanXc) {
         if (p->n_internal == 0) { mark(ev_start); mark(ev_stop); return e == cudaSuccess ? BS_OK : cuda_fail(e, "event"); }
         e = launch_xc_prepare(p->d_tens, p->n_internal, p->d_tables, p->d_errs, s);
+        if (e == cudaSuccess) p->launches += 1;
         mark(ev_start);
-        if (e == cudaSuccess)
+        if (e == cudaSuccess) {
             e = launch_xc_decode(p->d_tens, p->d_items, p->n_items, p->d_tables, p->d_errs, p->coders,
                                  p->max_ctas, s);
+            // one decode kernel per coder family the plan may meet
+            if (e == cudaSuccess && p->n_items > 0)
+                p->launches += ((p->coders & ((1u << BS_CODER_RANS) | (1u << BS_CODER_TANS))) ? 1 : 0) +
+                               ((p->coders & (1u << BS_CODER_RANS_PAIR)) ? 1 : 0);
+        }
         mark(ev_stop);
     } else if (p->kind == kPlanPar) {
         mark(ev_start);
         if (p->n_internal > 0) {
             if (e == cudaSuccess) e = cudaMemsetAsync(p->d_errs, 0, 4ull * p->n_internal, s);
-            if (e == cudaSuccess)
+            if (e == cudaSuccess) {
                 e = launch_par_jobs(p->d_jobs, p->n_jobs, p->d_groups, p->n_groups, p->d_tabs, p->d_syms,
                                     p->d_se_sym, p->d_mant, p->d_errs, s);
-            if (e == cudaSuccess)
+                if (e == cudaSuccess && (p->n_groups > 0 || p->n_jobs > 0)) p->launches += 1;
+            }
+            if (e == cudaSuccess) {
                 e = launch_par_merge(p->d_streams, p->n_streams_total, p->d_buckets, p->d_se_sym, p->d_mant,
                                      p->d_errs, s);
-            if (e == cudaSuccess)
+                if (e == cudaSuccess && p->n_streams_total > 0) p->launches += 1;
+            }
+            if (e == cudaSuccess) {
                 e = launch_seg_merge(p->d_ss, p->n_ss, p->d_seg_stream, p->n_segs, p->d_hist, p->d_buckets,
                                      p->d_se_sym, p->d_mant, p->d_errs, s);
+                if (e == cudaSuccess && p->n_ss > 0 && p->n_segs > 0) p->launches += 3;
+            }
         }
         mark(ev_stop);
     } else {

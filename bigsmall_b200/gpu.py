@@ -109,6 +109,12 @@ class _Plan:
                 _lib.check(rc, "bs_plan_decode_handoff")
         return call
 
+    def launch_count(self) -> int:
+        """Kernels this plan has launched so far (a count kept by the library)."""
+        v = ctypes.c_uint64()
+        _lib.check(_lib.load().bs_plan_launch_count(self._h, ctypes.byref(v)), "bs_plan_launch_count")
+        return int(v.value)
+
     def check(self, stream: Optional[torch.cuda.Stream] = None) -> list[int]:
         """Synchronise `stream` and raise BsCorruptError if any tensor failed."""
         L = _lib.load()

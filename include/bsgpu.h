@@ -124,6 +124,9 @@ int bs_plan_decode_handoff(bs_plan *plan, void *main_stream, void *side_stream, 
 int bs_plan_check(bs_plan *plan, void *stream, uint32_t *status_out);
 
 int bs_plan_n_tensors(const bs_plan *plan);
+/* Number of kernels this plan has launched so far (every decode call adds the
+ * kernels it enqueued), for measurement.  No reference counterpart. */
+int bs_plan_launch_count(const bs_plan *plan, uint64_t *count);
 /* Cap the decode grid of a bf16_exp_chunked_v1 plan at max_ctas CTAs (0: one
  * CTA per work item, the default).  A capped plan leaves SM room to kernels on
  * other streams, e.g. a layer decode overlapped with the previous layer's

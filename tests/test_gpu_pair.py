@@ -273,3 +273,27 @@ def test_tensor_past_2_32_values_round_trips():
     assert torch.equal(out.view(torch.int16), x.view(torch.int16))
     del x, out, blob
     torch.cuda.empty_cache()
+
+
+def test_plan_counts_the_kernels_it_launches():
+    """bs_plan_launch_count: the table build plus one decode kernel per coder
+    family the plan may meet, per decode call (bench.py reports this count)."""
+    from bigsmall_b200 import gpu
+    n = 50_001
+    raw = _normal(n, 5)
+    pair, rans = _dev(O.xc_encode(raw, 2, 12, 4096)), _dev(O.xc_encode(raw, 0, 12, 4096))
+    outs = [torch.empty(n, dtype=torch.bfloat16, device="cuda") for _ in range(2)]
+    with gpu.XcPlan([(pair, outs[0], 4096), (rans, outs[1], 4096)], coders=["pair", "rans"]) as p:
+        assert p.launch_count() == 0
+        p.run()
+        assert p.launch_count() == 3
+        for _ in range(4):
+            p.decode()
+        p.check()
+        assert p.launch_count() == 15
+    with gpu.XcPlan([(pair, outs[0], 4096)], coders="pair") as p:
+        p.run()
+        p.run()
+        assert p.launch_count() == 4
+    for o in outs:
+        assert o.cpu().view(torch.uint8).numpy().tobytes() == raw
