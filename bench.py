@@ -192,7 +192,8 @@ def reference_arm(a, torch, world, rank):
     from bigsmall_b200 import gpu
     ce = a.chunk_elems or gpu.DEFAULT_CHUNK_ELEMS
     config = {"workload": "llama3-8b-shaped bf16 container (BASELINE config 2), full-container decode",
-              "codec": "bf16_exp_chunked_v1", "coder": a.coder, "chunk_elems": ce, "prec": a.prec,
+              "codec": "bf16_exp_chunked_v1", "coder": a.coder, "chunk_elems": ce, "groups_per_chunk": a.groups,
+              "prec": a.prec,
               "partition": "contiguous chunk-span ownership, no collective", "ranks": world,
               "l2": "inputs (~10.6 GB compressed) far larger than the 126 MB L2; no flush"}
     device = "cuda:0" if torch.cuda.is_available() else "cpu"
@@ -217,6 +218,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--chunk-elems", type=int, default=None)
+    ap.add_argument("--groups", type=int, default=1,
+                    help="state groups per chunk (format version 2 when > 1; each group is one warp's work)")
     ap.add_argument("--coder", default="pair", choices=["rans", "tans", "pair"])
     ap.add_argument("--prec", type=int, default=None, help="log2 of the coder's table size (default: the library's)")
     ap.add_argument("--max-ctas", type=int, default=0, help="cap the decode grid (0: one CTA per work item)")
@@ -267,7 +270,8 @@ def main():
 
     ce = a.chunk_elems or gpu.DEFAULT_CHUNK_ELEMS
     config = {"workload": "llama3-8b-shaped bf16 container (BASELINE config 2), full-container decode",
-              "codec": "bf16_exp_chunked_v1", "coder": a.coder, "chunk_elems": ce, "prec": a.prec,
+              "codec": "bf16_exp_chunked_v1", "coder": a.coder, "chunk_elems": ce, "groups_per_chunk": a.groups,
+              "prec": a.prec,
               "partition": "contiguous chunk-span ownership, no collective", "ranks": world,
               "l2": "inputs (~10.6 GB compressed) far larger than the 126 MB L2; no flush"}
 
@@ -298,7 +302,7 @@ def main():
     g = torch.Generator(device=dev).manual_seed(0)
     originals, blobs = {}, {}
     max_n = max(math.prod(s) for n, s, _ in tensors if n in owned_names)
-    enc = gpu.XcEncoder(max_n, ce, a.coder, a.prec, device=local)
+    enc = gpu.XcEncoder(max_n, ce, a.coder, a.prec, device=local, groups=a.groups)
     for name, shape, kind in tensors:
         x = gen_tensor(torch, g, shape, kind, dev)
         if name in owned_names:
@@ -321,7 +325,7 @@ def main():
         host[offs[name]:offs[name] + b.numel()].copy_(b)
         metas.append({"name": name, "shape": list(shape), "dtype": "BF16", "codec": "bf16_exp_chunked_v1",
                       "special": None, "compressed_bytes": int(b.numel()), "offset": offs[name], "md5": "",
-                      "extra": gpu.xc_extras(ce, a.coder, a.prec)})
+                      "extra": gpu.xc_extras(ce, a.coder, a.prec, a.groups)})
     header = {"format": "bf16", "mode": "balanced", "model_type": "llm", "base_model": None,
               "tensor_count": len(metas), "tensors": metas}
     image = ContainerImage(header, host, pin=True)
@@ -410,7 +414,7 @@ def main():
         _, d, nb = loader.layout[name]
         entries.append((loader.dev_data[d:d + nb], loader.out[name].reshape(-1).view(torch.int16), ce,
                         math.prod(m["shape"]), c0, cc))
-    plan = gpu.XcPlan(entries, device=local, coders=a.coder, max_ctas=a.max_ctas)
+    plan = gpu.XcPlan(entries, device=local, coders=a.coder, max_ctas=a.max_ctas, groups=a.groups)
     for _ in range(a.warmup):
         plan.decode(stream)
     plan.check(stream)
@@ -792,11 +796,11 @@ def bench_stream(a, torch, dev, world, rank, dist, local):
     t0 = time.time()
     w = synthetic.random_weights(cfg, seed=0, device=dev)
     ce = a.chunk_elems or gpu.DEFAULT_CHUNK_ELEMS
-    enc = gpu.XcEncoder(max(t.numel() for t in w.values()), ce, a.coder, a.prec, device=local)
+    enc = gpu.XcEncoder(max(t.numel() for t in w.values()), ce, a.coder, a.prec, device=local, groups=a.groups)
     wr = ContainerWriter()
     for n, t in w.items():
         wr.add(n, t.shape, "BF16", "bf16_exp_chunked_v1", enc.encode(t.reshape(-1)).cpu().numpy().tobytes(), "",
-               gpu.xc_extras(ce, a.coder, a.prec))
+               gpu.xc_extras(ce, a.coder, a.prec, a.groups))
     del enc
     image = ContainerImage.from_bytes(wr.to_bytes())
     del wr
@@ -847,7 +851,8 @@ def bench_stream(a, torch, dev, world, rank, dist, local):
             "hbm_resident_GB": {"compressed_model": round(comp_bytes / 1e9, 2), "full_model": round(raw_bytes / 1e9, 2)},
             "ratio": round(comp_bytes / raw_bytes, 5), "higher_is_better": False, "n_gpus": 1,
             "config": {"model": "Qwen2.5-14B-shaped random init (seed 0)", "layers": layers, "prompt": 512,
-                       "new_tokens": steps, "slots": 2, "chunk_elems": ce, "coder": a.coder,
+                       "new_tokens": steps, "slots": 2, "chunk_elems": ce, "groups_per_chunk": a.groups,
+                       "coder": a.coder,
                        "decode_ctas_per_sm": k or "uncapped", "decode_max_ctas": sm.decode_max_ctas,
                        "model_stream": "high priority" if prio else "default priority (same as the decode)",
                        "resident_run": "high-priority stream"},
