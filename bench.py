@@ -232,6 +232,10 @@ def main():
     ap.add_argument("--stream-priority", default="1",
                     help="config 4: comma list of 0/1: run the model on a high-priority stream (1) or not")
     ap.add_argument("--kv-layers", type=int, default=32, help="config kv: layers of K and V (32 = config 5)")
+    ap.add_argument("--prefill-timeline", action="store_true",
+                    help="config stream: also record one prefill of each model with the CUDA profiler (CUPTI "
+                         "kernel records) and report GPU busy time, decode/model overlap and the launch "
+                         "resources of the model's GEMM kernels")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=8.0)
     ap.add_argument("--config", default="c2", choices=["c2", "small", "medium", "kv", "sweep", "stream", "mix",
@@ -775,6 +779,73 @@ def bench_legacy(a, torch, dev, world, rank, dist, local):
 # ---------------------------------------------------------------------------
 # config 4: streaming layer-wise inference
 # ---------------------------------------------------------------------------
+def _intervals_union(iv):
+    tot, cur = 0.0, None
+    for s, e in sorted(iv):
+        if cur is None or s > cur[1]:
+            if cur is not None:
+                tot += cur[1] - cur[0]
+            cur = [s, e]
+        else:
+            cur[1] = max(cur[1], e)
+    return tot + (cur[1] - cur[0] if cur else 0.0)
+
+
+def _intervals_overlap(a, b):
+    def norm(iv):
+        out = []
+        for s, e in sorted(iv):
+            if out and s <= out[-1][1]:
+                out[-1][1] = max(out[-1][1], e)
+            else:
+                out.append([s, e])
+        return out
+    A, B, i, j, tot = norm(a), norm(b), 0, 0, 0.0
+    while i < len(A) and j < len(B):
+        lo, hi = max(A[i][0], B[j][0]), min(A[i][1], B[j][1])
+        tot += max(0.0, hi - lo)
+        if A[i][1] < B[j][1]:
+            i += 1
+        else:
+            j += 1
+    return tot
+
+
+def prefill_timeline(torch, model, prompt, stream):
+    """One prefill under the CUDA profiler: wall time, the union of the model's
+    kernel intervals (GPU busy), of this library's decode kernels, their
+    overlap, and the largest shared-memory footprint among the GEMM kernels
+    (which decides whether a decode CTA can share an SM with them)."""
+    import tempfile
+    from torch.profiler import ProfilerActivity, profile
+    with torch.cuda.stream(stream), torch.no_grad():
+        model(input_ids=prompt, use_cache=True)
+        torch.cuda.synchronize()
+        with profile(activities=[ProfilerActivity.CUDA]) as prof:
+            t0 = time.perf_counter()
+            model(input_ids=prompt, use_cache=True)
+            torch.cuda.synchronize()
+            wall = (time.perf_counter() - t0) * 1e3
+    with tempfile.NamedTemporaryFile(suffix=".json") as f:
+        prof.export_chrome_trace(f.name)
+        with open(f.name) as fh:
+            trace = json.load(fh)
+    dec, mod, gemm = [], [], {"max_smem_bytes": 0, "regs_per_thread": None, "threads": None}
+    for ev in trace["traceEvents"]:
+        if ev.get("cat") != "kernel":
+            continue
+        iv = (ev["ts"], ev["ts"] + ev.get("dur", 0))
+        (dec if "bsg::" in ev["name"] else mod).append(iv)
+        arg = ev.get("args", {})
+        if ("nvjet" in ev["name"] or "gemm" in ev["name"].lower()) and \
+                (arg.get("shared memory") or 0) > gemm["max_smem_bytes"]:
+            gemm = {"max_smem_bytes": arg.get("shared memory"), "regs_per_thread": arg.get("registers per thread"),
+                    "threads": (arg.get("block") or [0])[0], "kernel": ev["name"][:48]}
+    return {"wall_ms_under_profiler": round(wall, 3), "model_kernels_busy_ms": round(_intervals_union(mod) / 1e3, 3),
+            "decode_kernels_busy_ms": round(_intervals_union(dec) / 1e3, 3),
+            "decode_overlapping_model_ms": round(_intervals_overlap(dec, mod) / 1e3, 3), "gemm_launch": gemm}
+
+
 def bench_stream(a, torch, dev, world, rank, dist, local):
     """Qwen2.5-14B-shaped random-init bf16 model (48 layers, hidden 5120,
     intermediate 13824, 40 Q / 8 KV heads x 128, vocab 152064), batch 1,
@@ -817,6 +888,7 @@ def bench_stream(a, torch, dev, world, rank, dist, local):
     with torch.cuda.stream(hp):
         synthetic.greedy(ref, prompt, steps)
         ids_r, lg_r, pre_r, dec_r = synthetic.greedy(ref, prompt, steps)
+    tl_r = prefill_timeline(torch, ref, prompt, hp) if a.prefill_timeline else None
     del ref
 
     loader = StreamingLoader(image, device=dev)
@@ -859,6 +931,9 @@ def bench_stream(a, torch, dev, world, rank, dist, local):
             "setup_s": round(setup_s, 1)}
         res["hbm_resident_GB"]["streaming"] = round((comp_bytes + sum(
             2 * t.numel() for n, t in w.items() if ".layers." not in n) + 2 * layer_raw) / 1e9, 2)
+        if a.prefill_timeline:
+            res["prefill_timeline"] = {"resident": tl_r,
+                                       "streaming": prefill_timeline(torch, sm.model, prompt, run_stream)}
         print(json.dumps(res), flush=True)
         sm.close()
         del sm
