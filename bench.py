@@ -239,14 +239,16 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=8.0)
     ap.add_argument("--config", default="c2", choices=["c2", "small", "medium", "kv", "sweep", "stream", "mix",
-                                                      "legacy"],
+                                                      "legacy", "triton-ref"],
                     help="c2: the benchmark workload; small: one 2^27-value tensor of the same "
                          "distribution (compressed ~170 MB, above L2) for ncu captures; medium: one "
                          "2^30-value tensor (fills every SM; ~3.5 GB on the device) for ncu captures; kv: "
                          "config 5 (KV cache encode+decode); sweep: config 3 (coders x chunk size); "
                          "stream: config 4; mix: HBM calibration of the decode's read:write mix; "
                          "legacy: the reference's serial-stream formats (bf16_se_single_kernel, bf16_se_tans, "
-                         "bf16_parallel_v1) on the config-1 tensor and on a batch of config-2 k/v tensors")
+                         "bf16_parallel_v1) on the config-1 tensor and on a batch of config-2 k/v tensors; "
+                         "triton-ref: the reference's own GPU decoder (ac_triton, from baseline/_ref) on the config-1 "
+                         "tensor's bf16_parallel_v1 blob beside this library's decode of the same blob")
     a = ap.parse_args()
     a.warmup = max(3, a.warmup)
     if a.prec is None:
@@ -289,6 +291,8 @@ def main():
         return bench_mix(a, torch, dev, world, rank, dist, local)
     if a.config == "legacy":
         return bench_legacy(a, torch, dev, world, rank, dist, local)
+    if a.config == "triton-ref":
+        return bench_triton_ref(a, torch, dev, world, rank, dist, local)
     if a.config == "small":
         tensors = [("model.layers.0.mlp.small_proj.weight", (1 << 15, 4096), "linear")]
         config["workload"] = "one 2^27-value bf16 tensor, config-2 distribution (profiling case)"
@@ -844,6 +848,76 @@ def prefill_timeline(torch, model, prompt, stream):
     return {"wall_ms_under_profiler": round(wall, 3), "model_kernels_busy_ms": round(_intervals_union(mod) / 1e3, 3),
             "decode_kernels_busy_ms": round(_intervals_union(dec) / 1e3, 3),
             "decode_overlapping_model_ms": round(_intervals_overlap(dec, mod) / 1e3, 3), "gemm_launch": gemm}
+
+
+def bench_triton_ref(a, torch, dev, world, rank, dist, local):
+    """The reference's own GPU path for its GPU format: the unmodified reference
+    installed in baseline/_ref (``bigsmall.kernels.ac_triton.decode``, Triton SE
+    streams plus its CPU-side work, bytes in and bytes out), timed on the
+    config-1 tensor's bf16_parallel_v1 blob (128 streams, minted by the
+    reference's own encoder), next to this library's decode of the same blob
+    through the same bytes -> bytes contract (``kernels.ac_cuda.decode``) and
+    device-resident (blob and output in HBM, CUDA events).  One JSON line."""
+    if rank != 0:
+        return
+    import types
+    ref_dir = os.path.join(ROOT, "baseline", "_ref")
+    name = "reference GPU path: bigsmall.kernels.ac_triton.decode (bf16_parallel_v1, config-1 tensor)"
+    if not os.path.isfile(os.path.join(ref_dir, "bigsmall", "kernels", "ac_triton.py")):
+        print(json.dumps({"config": name, "impl": "reference", "unavailable":
+                          "the reference is not installed in baseline/_ref (pip install --no-index --no-deps "
+                          "--target baseline/_ref <reference checkout>)"}), flush=True)
+        return
+    for m in ("constriction", "zstandard", "blosc2"):   # optional native deps the PAR1 path does not use
+        try:
+            __import__(m)
+        except ImportError:
+            sys.modules[m] = types.ModuleType(m)
+    os.environ.setdefault("BIGSMALL_DISABLE_VERSION_CHECK", "1")
+    sys.path.insert(0, ref_dir)
+    from bigsmall.codecs import bf16_parallel as ref_par
+    from bigsmall.kernels import ac_triton
+    from bigsmall_b200 import gpu
+    from bigsmall_b200.kernels import ac_cuda
+    n = 4096 * 4096
+    g = torch.Generator().manual_seed(0)
+    x = torch.randn(n, generator=g) * 0.02
+    idx = torch.randperm(n, generator=g)[: n // 1000]
+    x[idx] *= 30
+    raw = x.to(torch.bfloat16).view(torch.uint8).numpy().tobytes()
+    t0 = time.perf_counter()
+    blob, extras = ref_par.encode(raw)
+    enc_s = time.perf_counter() - t0
+
+    def wall(fn, k):
+        fn()                                   # warm-up (Triton JIT, plan caches)
+        ts = []
+        for _ in range(k):
+            t = time.perf_counter()
+            out = fn()
+            ts.append(time.perf_counter() - t)
+        return statistics.median(ts), out
+    ref_s, ref_out = wall(lambda: ac_triton.decode(blob, extras, n), max(1, min(a.steps, 3)))
+    ours_s, ours_out = wall(lambda: ac_cuda.decode(blob, extras, n), max(3, a.steps))
+    d_blob = torch.from_numpy(__import__("numpy").frombuffer(blob, dtype="uint8").copy()).to(dev)
+    out = torch.empty(n, dtype=torch.bfloat16, device=dev)
+    plan = gpu.ParPlan(blob, d_blob, out, n)
+    stream = torch.cuda.current_stream(dev)
+    dev_ms = _timed(torch, lambda: plan.decode(stream), max(3, a.steps), a.warmup, stream)
+    plan.check(stream)
+    dev_ok = out.view(torch.uint8).cpu().numpy().tobytes() == raw
+    plan.close()
+    mbs = lambda s: round(2 * n / s / 1e6, 2)
+    print(json.dumps({
+        "config": name, "values": n, "n_streams": extras.get("n_streams"), "blob_bytes": len(blob),
+        "ratio": round(len(blob) / (2 * n), 5), "reference_encode_s": round(enc_s, 2),
+        "reference_ac_triton": {"s": round(ref_s, 4), "decoded_MBs": mbs(ref_s), "exact": ref_out == raw},
+        "ours_ac_cuda_bytes_to_bytes": {"s": round(ours_s, 4), "decoded_MBs": mbs(ours_s), "exact": ours_out == raw,
+                                        "speedup_vs_reference": round(ref_s / ours_s, 1)},
+        "ours_device_resident": {"ms": round(dev_ms, 4), "decoded_MBs": round(2 * n / dev_ms / 1e3, 1),
+                                 "exact": dev_ok},
+        "note": "bytes->bytes timings include each path's host<->device copies; the reference leaves "
+                "part of the work on the CPU"}), flush=True)
 
 
 def bench_stream(a, torch, dev, world, rank, dist, local):
