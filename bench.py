@@ -134,6 +134,17 @@ def measured_peak():
         return FALLBACK_HBM_GBS, "fallback"
 
 
+def kernel_sources_digest() -> str:
+    """sha256 (first 16 hex digits) of the decode kernels' sources; a profile
+    records it, so a traffic figure captured from other sources shows as stale."""
+    import hashlib
+    h = hashlib.sha256()
+    for f in ("xc_decode.cu", "common.cuh"):
+        with open(os.path.join(ROOT, "bigsmall_b200", "csrc", f), "rb") as fh:
+            h.update(fh.read())
+    return h.hexdigest()[:16]
+
+
 def profile_traffic(coder: str):
     """dram bytes per config-2 decode launch from the committed ncu summary
     of this coder's kernel, if any."""
@@ -517,9 +528,13 @@ def main():
         value = 2 * total_elems / (ms * 1e-3) / 1e9
         achieved = algo_bytes / (kernel_ms * 1e-3) / 1e9
         prof = profile_traffic(a.coder) if a.config == "c2" else None
-        traffic = None
-        if prof and prof.get("chunk_elems") == ce and world == 1:
+        traffic, traffic_src = None, None
+        if prof and prof.get("chunk_elems") == ce and world == 1 and a.groups == 1:
             traffic = prof.get("traffic_bytes_per_launch")
+            cur = kernel_sources_digest()
+            traffic_src = {"profile": f"profiles/xc_decode_c2_{a.coder}.json",
+                           "kernel_sources_at_capture": prof.get("kernel_sources_sha256_16"),
+                           "kernel_sources_now": cur, "stale": prof.get("kernel_sources_sha256_16") != cur}
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": a.steps,
             "warmup": a.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "strong",
@@ -527,7 +542,7 @@ def main():
             "config": config,
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_source": f"hbm_gbs of {peak_kind}",
-                         "traffic": traffic,
+                         "traffic": traffic, "traffic_source": traffic_src,
                          "kernel": f"{'xc_decode_pair_kernel' if a.coder == 'pair' else 'xc_decode_kernel'}",
                          "kernel_ms": round(kernel_ms, 4),
                          "timing": "CUDA events recorded on the launching stream around the decode kernel of "
