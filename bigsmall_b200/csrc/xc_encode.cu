@@ -383,8 +383,8 @@ __global__ void __launch_bounds__(kEncWarps * 32) xc_enc_chunks_pair_kernel(
         const uint32_t da = ((w >> 7) & 0xFF) - e_lo, db = ((w >> 23) & 0xFF) - e_lo;
         const bool ea = act && da > 14, eb = has_b && db > 14;
         const uint32_t a = act ? min(da, 15u) : 0u, b = has_b ? min(db, 15u) : 0u;
-        const uint32_t ba = __ballot_sync(kFull, ea), bb = __ballot_sync(kFull, eb);
-        if (ba | bb) {
+        if (__ballot_sync(kFull, ea || eb)) {   // rare: only then the per-value ballots
+            const uint32_t ba = __ballot_sync(kFull, ea), bb = __ballot_sync(kFull, eb);
             const int64_t k = static_cast<int64_t>(ecur) + __popc(ba) + __popc(bb);
             const int64_t pa = static_cast<int64_t>(__popc(ba & lt) + __popc(bb & lt)) - k;
             if (ea) eend[pa] = static_cast<uint8_t>((w >> 7) & 0xFF);
