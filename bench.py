@@ -266,6 +266,9 @@ def main():
     ap.add_argument("--stream-priority", default="1",
                     help="config 4: comma list of 0/1: run the model on a high-priority stream (1) or not")
     ap.add_argument("--kv-layers", type=int, default=32, help="config kv: layers of K and V (32 = config 5)")
+    ap.add_argument("--enc-streams", type=int, default=1,
+                    help="config kv: encoders (each with its own workspace) on as many streams, tensors "
+                         "assigned round-robin, so consecutive tensors' encodes overlap")
     ap.add_argument("--prefill-timeline", action="store_true",
                     help="config stream: also record one prefill of each model with the CUDA profiler (CUPTI "
                          "kernel records) and report GPU busy time, decode/model overlap and the launch "
@@ -617,9 +620,17 @@ def bench_kv(a, torch, dev, world, rank, dist, local):
     lens = torch.zeros(len(kv), 2, dtype=torch.int64, device=dev)
     stream = torch.cuda.current_stream(dev)
 
+    encs = [enc] + [gpu.XcEncoder(n, ce, a.coder, a.prec, device=local) for _ in range(a.enc_streams - 1)]
+    streams = [stream] + [torch.cuda.Stream(dev) for _ in range(a.enc_streams - 1)]
+
     def encode_all():
+        for s in streams[1:]:
+            s.wait_stream(stream)
         for i, x in enumerate(kv):
-            enc.encode_into(x, outs[i], lens[i], stream)
+            k = i % len(encs)
+            encs[k].encode_into(x, outs[i], lens[i], streams[k])
+        for s in streams[1:]:
+            stream.wait_stream(s)
 
     enc_ms = _timed(torch, encode_all, a.steps, a.warmup, stream)
     ln = lens[:, 0].tolist()
@@ -655,7 +666,7 @@ def bench_kv(a, torch, dev, world, rank, dist, local):
             "config": {"workload": f"{L} layers x {{K,V}} [16,8,8192,128] bf16, N(0,1) x log-normal per-channel "
                                    "scale, seed 0; batch sharded across ranks"
                                    + ("" if L == 32 else " (reduced case; config 5 is 32 layers)"),
-                       "chunk_elems": ce, "coder": a.coder},
+                       "chunk_elems": ce, "coder": a.coder, "encode_streams": a.enc_streams},
             "verified": "bitwise equal" if bad == 0 else f"MISMATCH on {int(bad)} ranks"}), flush=True)
     plan.close()
     if dist:
