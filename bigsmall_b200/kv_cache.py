@@ -33,7 +33,12 @@ def _check_bf16(t: torch.Tensor, what: str) -> None:
 
 
 class KVEncoder:
-    """Reusable device encoder for K/V tensors (grows its buffers on demand)."""
+    """Reusable device encoder for K/V tensors (grows its buffers on demand).
+
+    A layer's K and V are encoded concurrently by two encoders (each with its
+    own workspace and output buffer), the second on a side stream: one
+    tensor's per-chunk encode kernel leaves most of the GPU idle (one warp per
+    chunk), so two in flight keep more SMs busy."""
 
     def __init__(self, device=None, chunk_elems: int = KV_CHUNK_ELEMS, coder: str = gpu.DEFAULT_CODER):
         self.device = torch.device("cuda", device if isinstance(device, int) else
@@ -42,19 +47,39 @@ class KVEncoder:
             self.device = torch.device("cuda", torch.cuda.current_device())
         self.chunk_elems = chunk_elems
         self.coder = coder
-        self._enc: Optional[gpu.XcEncoder] = None
+        self._encs: list = [None, None]
+        self._side: Optional[torch.cuda.Stream] = None
 
-    def encoder(self, n: int) -> gpu.XcEncoder:
-        if self._enc is None or self._enc.max_elems < n:
-            self._enc = gpu.XcEncoder(max(n, 1), self.chunk_elems, self.coder, device=self.device.index)
-        return self._enc
+    def encoder(self, n: int, k: int = 0) -> gpu.XcEncoder:
+        e = self._encs[k]
+        if e is None or e.max_elems < n:
+            e = self._encs[k] = gpu.XcEncoder(max(n, 1), self.chunk_elems, self.coder, device=self.device.index)
+        return e
+
+    def _flat(self, t: torch.Tensor) -> torch.Tensor:
+        x = t.detach().contiguous().reshape(-1)
+        return x if x.device == self.device else x.to(self.device)
 
     def encode(self, t: torch.Tensor) -> torch.Tensor:
         """Right-sized device blob of one tensor (synchronises to read the size)."""
-        x = t.detach().contiguous().reshape(-1)
-        if x.device != self.device:
-            x = x.to(self.device)
+        x = self._flat(t)
         return self.encoder(x.numel()).encode(x)
+
+    def encode_pair(self, keys: torch.Tensor, values: torch.Tensor):
+        """Right-sized device blobs of K and V, encoded concurrently on the
+        current stream and a side stream (one synchronisation for both sizes)."""
+        xk, xv = self._flat(keys), self._flat(values)
+        ek, ev = self.encoder(xk.numel(), 0), self.encoder(xv.numel(), 1)
+        main = torch.cuda.current_stream(self.device)
+        if self._side is None:
+            self._side = torch.cuda.Stream(self.device)
+        self._side.wait_stream(main)
+        ek.encode_async(xk, main)
+        ev.encode_async(xv, self._side)
+        main.wait_stream(self._side)
+        xv.record_stream(self._side)
+        nk, nv = (int(v) for v in torch.stack([ek.out_len[0], ev.out_len[0]]).tolist())
+        return ek.out[:nk].clone(), ev.out[:nv].clone()
 
 
 def encode_kv(keys: torch.Tensor, values: torch.Tensor, enc: Optional[KVEncoder] = None):
@@ -62,7 +87,7 @@ def encode_kv(keys: torch.Tensor, values: torch.Tensor, enc: Optional[KVEncoder]
     _check_bf16(keys, "keys")
     _check_bf16(values, "values")
     enc = enc or KVEncoder(keys.device if keys.is_cuda else None)
-    return enc.encode(keys), enc.encode(values)
+    return enc.encode_pair(keys, values)
 
 
 def decode_kv(k_blob: torch.Tensor, v_blob: torch.Tensor, k_shape, v_shape, device=None,

@@ -30,8 +30,7 @@ class CompressedKVCache:
     def set(self, layer_idx: int, keys, values) -> None:
         if keys.dtype != torch.bfloat16 or values.dtype != torch.bfloat16:
             raise ValueError("CompressedKVCache.set: keys and values must be BF16")
-        kb = self._enc.encode(keys)
-        vb = self._enc.encode(values)
+        kb, vb = self._enc.encode_pair(keys, values)
         self._store[layer_idx] = (kb, vb, tuple(keys.shape), tuple(values.shape))
         self._raw[layer_idx] = keys.element_size() * keys.numel() + values.element_size() * values.numel()
 
