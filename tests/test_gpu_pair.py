@@ -297,3 +297,29 @@ def test_plan_counts_the_kernels_it_launches():
         assert p.launch_count() == 4
     for o in outs:
         assert o.cpu().view(torch.uint8).numpy().tobytes() == raw
+
+
+@pytest.mark.parametrize("lead_scale", [None, 1e-6, 1e3])
+def test_device_encoder_on_tensors_whose_scale_changes(lead_scale):
+    """A tensor whose first 65,536 values have a far smaller or larger scale
+    than the rest (so its exponents fall in two distant windows): the pair
+    coder's device blob equals the CPU encoder's byte for byte, with one and
+    with four state groups per chunk, and decodes exactly."""
+    from bigsmall_b200 import gpu
+    g = torch.Generator().manual_seed(17)
+    body = torch.randn(1_000_003, generator=g)
+    if lead_scale is not None:
+        body = torch.cat([torch.randn(65_536, generator=g) * lead_scale, body])
+    x = body.to(torch.bfloat16)
+    raw = x.view(torch.uint8).numpy().tobytes()
+    for ce, groups in ((32768, 1), (65536, 4)):
+        blob = gpu.encode_xc(x.cuda(), coder="pair", chunk_elems=ce, groups=groups)
+        assert blob.cpu().numpy().tobytes() == O.xc_encode(raw, 2, 12, ce, groups), (lead_scale, ce)
+        assert _decode_g(blob, x.numel(), ce, groups) == raw
+
+
+def _decode_g(blob, n, ce, groups):
+    from bigsmall_b200 import gpu
+    out = torch.empty(n, dtype=torch.bfloat16, device="cuda")
+    gpu.decode_xc_into(blob, out, ce, groups=groups)
+    return out.cpu().view(torch.uint8).numpy().tobytes()
