@@ -69,11 +69,13 @@ def test_loader_pipelined_groups_and_tied(tmp_path):
     ld.close()
 
 
-def test_ranks_shares_cover_the_container(tmp_path):
+@pytest.mark.parametrize("ce,groups", [(256, 1), (1024, 4)])
+def test_ranks_shares_cover_the_container(tmp_path, ce, groups):
     """sharding.owned_for + DeviceLoader(owned=...) for every rank of 2- and
     3-way partitions, run one after another on one GPU: chunked tensors split
-    by chunk spans, raw / bf16_parallel_v1 tensors whole on one rank, tied
-    aliases on none; together the ranks' outputs reproduce every tensor once."""
+    by chunk spans (chunks of one or of four state groups), raw /
+    bf16_parallel_v1 tensors whole on one rank, tied aliases on none; together
+    the ranks' outputs reproduce every tensor once."""
     from bigsmall_b200 import container as C, gpu
     from bigsmall_b200.loader import ContainerImage, DeviceLoader
     from bigsmall_b200.sharding import owned_for
@@ -81,8 +83,8 @@ def test_ranks_shares_cover_the_container(tmp_path):
     w = C.ContainerWriter()
     for k, v in sd.items():
         if v.dtype == torch.bfloat16 and v.numel() >= 256:
-            blob = gpu.encode_xc(v.reshape(-1).cuda(), chunk_elems=256).cpu().numpy().tobytes()
-            w.add(k, v.shape, "BF16", "bf16_exp_chunked_v1", blob, "", gpu.xc_extras(256))
+            blob = gpu.encode_xc(v.reshape(-1).cuda(), chunk_elems=ce, groups=groups).cpu().numpy().tobytes()
+            w.add(k, v.shape, "BF16", "bf16_exp_chunked_v1", blob, "", gpu.xc_extras(ce, groups=groups))
         else:
             raw = v.reshape(-1).view(torch.uint8).numpy().tobytes()
             w.add(k, v.shape, {torch.bfloat16: "BF16", torch.int64: "I64"}[v.dtype], "raw", raw, "")
@@ -102,7 +104,7 @@ def test_ranks_shares_cover_the_container(tmp_path):
             out = ld.run()
             for name, c0, cc in owned:
                 b = out[name].reshape(-1).cpu().view(torch.uint8).numpy().tobytes()
-                lo = 2 * 256 * c0 if cc else 0
+                lo = 2 * ce * c0 if cc else 0
                 got[name][lo:lo + len(b)] = b
                 seen[name] += len(b)
             ld.close()
