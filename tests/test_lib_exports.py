@@ -57,3 +57,26 @@ def test_host_side_validation_without_gpu():
     assert rc in (_lib.BS_OK, _lib.BS_E_INVALID_ARG)
     if rc == _lib.BS_OK:
         lib.bs_plan_destroy(h)
+
+
+def test_ctypes_mirrors_match_the_c_layout(tmp_path):
+    """The ctypes mirrors of the ABI's structs have the C compiler's size and
+    field offsets (a stale mirror would mis-stride descriptor arrays)."""
+    import ctypes
+    from bigsmall_b200 import _lib
+    structs = {"bs_xc_tensor": _lib.XcTensor, "bs_se_blob": _lib.SeBlob}
+    lines = ['#include <stdio.h>', '#include <stddef.h>', '#include "bsgpu.h"', 'int main(void) {']
+    for cname, py in structs.items():
+        lines.append(f'printf("{cname} %zu\\n", sizeof({cname}));')
+        for f, _ in py._fields_:
+            lines.append(f'printf("{cname}.{f} %zu\\n", offsetof({cname}, {f}));')
+    lines += ["return 0; }"]
+    src = tmp_path / "layout.c"
+    src.write_text("\n".join(lines))
+    exe = tmp_path / "layout"
+    subprocess.run(["gcc", "-I", os.path.join(ROOT, "include"), str(src), "-o", str(exe)], check=True)
+    got = dict(l.split() for l in subprocess.run([str(exe)], capture_output=True, text=True).stdout.splitlines())
+    for cname, py in structs.items():
+        assert int(got[cname]) == ctypes.sizeof(py), cname
+        for f, _ in py._fields_:
+            assert int(got[f"{cname}.{f}"]) == getattr(py, f).offset, (cname, f)
