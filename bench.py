@@ -1029,6 +1029,17 @@ def bench_stream(a, torch, dev, world, rank, dist, local):
         # standalone decode time of one layer with the same grid (hidden-fraction accounting)
         side = torch.cuda.current_stream(dev)
         layer_ms = _timed(torch, lambda: sm._bundles[(1, 1)].decode(side), 10, 3, side)
+        # host time of the per-layer hand-off call (the model's host loop pays it once per layer)
+        hmain = torch.cuda.Stream(dev)
+        call = sm._handoff[(1, 1)]
+        for _ in range(10):
+            call(hmain)
+        torch.cuda.synchronize()
+        t_h = time.perf_counter()
+        for _ in range(100):
+            call(hmain)
+        handoff_us = (time.perf_counter() - t_h) / 100 * 1e6
+        torch.cuda.synchronize()
         layer_raw = sum(2 * sm._slots[0][kk].numel() for kk in sm._slots[0])
         dec_work = layers * layer_ms
 
@@ -1041,6 +1052,7 @@ def bench_stream(a, torch, dev, world, rank, dist, local):
             "value": round(dec_s / steps, 3), "resident_ms_per_token": round(dec_r / steps, 3),
             "prefill_ms": {"streaming": round(pre_s, 2), "resident": round(pre_r, 2)},
             "layer_decode_ms": round(layer_ms, 4), "layer_decoded_GBs": round(layer_raw / layer_ms / 1e6, 1),
+            "handoff_host_us_per_layer": round(handoff_us, 2),
             "hidden_fraction": {"prefill": hidden(pre_s, pre_r, 1), "decode": hidden(dec_s, dec_r, steps)},
             "logits_bit_identical": same_logits, "tokens_identical": same_ids,
             "hbm_resident_GB": {"compressed_model": round(comp_bytes / 1e9, 2), "full_model": round(raw_bytes / 1e9, 2)},

@@ -172,6 +172,7 @@ cudaError_t launch_xc_decode(const XcTensorDev *d_tens, const XcItem *d_items, i
                              const uint32_t *d_tables, uint32_t *d_errs, uint32_t coders, int max_ctas,
                              cudaStream_t s);
 int xc_warps_per_cta();
+cudaError_t xc_decode_attrs(uint32_t coders);   // decode kernels' shared-memory opt-in
 cudaError_t launch_xc_noalloc(const XcTensorDev *h_tens, const uint32_t *range_count, int n, cudaStream_t s,
                               uint32_t *h_status);
 uint64_t xc_noalloc_scratch_bytes();

@@ -781,6 +781,18 @@ static cudaError_t smem_opt_in(K kernel, size_t bytes, std::atomic<uint8_t> *don
 }
 static std::atomic<uint8_t> g_attr_rans[128], g_attr_pair[128], g_attr_na_pair[128];
 
+// The decode kernels' shared-memory opt-in for the coder families in
+// `coders` (what launch_xc_decode does first), so a stream capture of
+// launch_xc_decode records kernel launches only.
+cudaError_t xc_decode_attrs(uint32_t coders) {
+    cudaError_t e = cudaSuccess;
+    if (coders & ((1u << BS_CODER_RANS) | (1u << BS_CODER_TANS)))
+        e = smem_opt_in(xc_decode_kernel, kXcMaxTable * 4 + kRansWarps * kWarpRing, g_attr_rans);
+    if (e == cudaSuccess && (coders & (1u << BS_CODER_RANS_PAIR)))
+        e = smem_opt_in(xc_decode_pair_kernel, kPairTableBytes + kWarps * kPairWarpRing, g_attr_pair);
+    return e;
+}
+
 uint32_t xc_launch_mask(const XcTensorDev *h_tens, int n) {
     uint32_t m = 0;
     for (int i = 0; i < n; i++) m |= h_tens[i].coder_mask ? h_tens[i].coder_mask : kXcAllCoders;

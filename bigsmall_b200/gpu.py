@@ -81,7 +81,12 @@ class _Plan:
     def decode_after(self, stream: torch.cuda.Stream, wait: Optional[torch.cuda.Event] = None,
                      done: Optional[torch.cuda.Event] = None) -> None:
         """``stream`` waits for ``wait``, decodes, then records ``done``: one
-        library call (events must have been recorded once, which creates them)."""
+        library call.  torch creates an event on its first record, so an event
+        not yet created is recorded on ``stream`` first (a wait on it is then
+        already satisfied, as a wait on an unrecorded event is)."""
+        for ev in (wait, done):
+            if ev is not None and not ev.cuda_event:
+                ev.record(stream)
         L = _lib.load()
         _lib.check(L.bs_plan_decode_after(self._h, _stream_ptr(stream, self.device),
                                           ctypes.c_void_p(wait.cuda_event) if wait is not None else None,

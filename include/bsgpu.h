@@ -106,7 +106,12 @@ int bs_plan_decode_timed(bs_plan *plan, void *stream, void *ev_start, void *ev_s
 /* One call for an event-chained decode on a side stream: the stream waits for
  * `wait_event` (cudaEvent_t, may be NULL), the plan decodes, then `done_event`
  * (may be NULL) is recorded.  Used by the streaming model's per-layer prefetch
- * to keep host work per layer to one call.  No reference counterpart. */
+ * to keep host work per layer to one call.  For a bf16_exp_chunked_v1 plan the
+ * decode's kernels run as one CUDA graph launch (about a quarter of the host
+ * time of launching them one by one): the graph is captured on a private
+ * stream at the plan's first event-chained call and again after
+ * bs_plan_set_max_ctas changes the cap, so make that first call outside any
+ * stream capture.  No reference counterpart. */
 int bs_plan_decode_after(bs_plan *plan, void *stream, void *wait_event, void *done_event);
 /* The whole per-layer hand-off of a two-stream prefetch in one call:
  * `release_event` is recorded on `main_stream` (the running layer is done with

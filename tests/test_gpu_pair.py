@@ -323,3 +323,28 @@ def _decode_g(blob, n, ce, groups):
     out = torch.empty(n, dtype=torch.bfloat16, device="cuda")
     gpu.decode_xc_into(blob, out, ce, groups=groups)
     return out.cpu().view(torch.uint8).numpy().tobytes()
+
+
+def test_event_chained_decode_runs_as_one_captured_graph():
+    """bs_plan_decode_after runs the plan's table build and decode kernels as
+    one CUDA graph (captured on first use, again after the CTA cap changes):
+    outputs stay exact, events order it against the caller's stream, and the
+    plan's launch count still counts both kernels per decode."""
+    from bigsmall_b200 import gpu
+    n = 500_001
+    raw = _normal(n, 8)
+    blob = _dev(O.xc_encode(raw, 2, 12, 4096))
+    out = torch.empty(n, dtype=torch.bfloat16, device="cuda")
+    main = torch.cuda.current_stream()
+    side = torch.cuda.Stream()
+    go, done = torch.cuda.Event(), torch.cuda.Event()   # created by decode_after on first use
+    with gpu.XcPlan([(blob, out, 4096)], coders="pair") as p:
+        for k, cap in enumerate((0, 0, 3, 3, 0)):
+            p.set_max_ctas(cap)
+            out.fill_(0)
+            go.record(main)
+            p.decode_after(side, go, done)
+            main.wait_event(done)
+            assert out.cpu().view(torch.uint8).numpy().tobytes() == raw, (k, cap)
+            assert p.launch_count() == 2 * (k + 1)
+        p.check()
