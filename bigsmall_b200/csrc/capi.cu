@@ -308,6 +308,14 @@ int bs_xc_plan_create(const bs_xc_tensor *tensors, int n_tensors, int device, bs
     return BS_OK;
 }
 
+// Kernels one decode of a bf16_exp_chunked_v1 plan launches: the table build
+// plus one decode kernel per coder family the plan may meet.
+static uint64_t xc_kernels_per_decode(const bs_plan *p) {
+    if (p->n_items <= 0) return 1;
+    return 1 + ((p->coders & ((1u << BS_CODER_RANS) | (1u << BS_CODER_TANS))) ? 1 : 0) +
+           ((p->coders & (1u << BS_CODER_RANS_PAIR)) ? 1 : 0);
+}
+
 // The decode step of a plan; `ev_start` / `ev_stop` (cudaEvent_t, optional)
 // are recorded on the stream right before and after the decode kernels, after
 // the table build, so a caller can time the decode kernels alone.
@@ -322,16 +330,11 @@ static int plan_decode(bs_plan *p, void *stream, void *ev_start, void *ev_stop) 
     if (p->kind == kPlanXc) {
         if (p->n_internal == 0) { mark(ev_start); mark(ev_stop); return e == cudaSuccess ? BS_OK : cuda_fail(e, "event"); }
         e = launch_xc_prepare(p->d_tens, p->n_internal, p->d_tables, p->d_errs, s);
-        if (e == cudaSuccess) p->launches += 1;
         mark(ev_start);
-        if (e == cudaSuccess) {
+        if (e == cudaSuccess)
             e = launch_xc_decode(p->d_tens, p->d_items, p->n_items, p->d_tables, p->d_errs, p->coders,
                                  p->max_ctas, s);
-            // one decode kernel per coder family the plan may meet
-            if (e == cudaSuccess && p->n_items > 0)
-                p->launches += ((p->coders & ((1u << BS_CODER_RANS) | (1u << BS_CODER_TANS))) ? 1 : 0) +
-                               ((p->coders & (1u << BS_CODER_RANS_PAIR)) ? 1 : 0);
-        }
+        if (e == cudaSuccess) p->launches += xc_kernels_per_decode(p);
         mark(ev_stop);
     } else if (p->kind == kPlanPar) {
         mark(ev_start);
@@ -402,9 +405,7 @@ static int plan_decode_graph(bs_plan *p, cudaStream_t s) {
     }
     e = cudaGraphLaunch(p->graph, s);
     if (e != cudaSuccess) return cuda_fail(e, "decode graph launch");
-    p->launches += 1 + (p->n_items > 0 ? ((p->coders & ((1u << BS_CODER_RANS) | (1u << BS_CODER_TANS))) ? 1 : 0) +
-                                             ((p->coders & (1u << BS_CODER_RANS_PAIR)) ? 1 : 0)
-                                       : 0);
+    p->launches += xc_kernels_per_decode(p);
     return BS_OK;
 }
 
