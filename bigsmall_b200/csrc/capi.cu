@@ -104,6 +104,7 @@ struct bs_plan {
     // captured on first use by the event-chained calls (decode_after, handoff)
     cudaGraphExec_t graph = nullptr;
     int graph_ctas = -1;            // max_ctas the graph was captured with
+    bool graph_failed = false;      // capture not possible here: plain launches from then on
 };
 
 namespace {
@@ -372,7 +373,7 @@ int bs_plan_decode(bs_plan *p, void *stream) { return plan_decode(p, stream, nul
 // private stream (thread-local capture mode) the first time, and again after
 // the plan's CTA cap changes; it refers only to the plan's own memory.
 static int plan_decode_graph(bs_plan *p, cudaStream_t s) {
-    if (p->kind != kPlanXc || p->n_internal == 0) return plan_decode(p, s, nullptr, nullptr);
+    if (p->kind != kPlanXc || p->n_internal == 0 || p->graph_failed) return plan_decode(p, s, nullptr, nullptr);
     DeviceGuard guard(p->device);
     cudaError_t e = cudaSuccess;
     if (!p->graph || p->graph_ctas != p->max_ctas) {
@@ -383,8 +384,7 @@ static int plan_decode_graph(bs_plan *p, cudaStream_t s) {
         e = xc_decode_attrs(p->coders);
         cudaStream_t cs = nullptr;
         if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&cs, cudaStreamNonBlocking);
-        if (e != cudaSuccess) return cuda_fail(e, "decode graph set-up");
-        e = cudaStreamBeginCapture(cs, cudaStreamCaptureModeThreadLocal);
+        if (e == cudaSuccess) e = cudaStreamBeginCapture(cs, cudaStreamCaptureModeThreadLocal);
         if (e == cudaSuccess) {
             cudaError_t le = launch_xc_prepare(p->d_tens, p->n_internal, p->d_tables, p->d_errs, cs);
             if (le == cudaSuccess)
@@ -396,10 +396,15 @@ static int plan_decode_graph(bs_plan *p, cudaStream_t s) {
             if (e == cudaSuccess) e = cudaGraphInstantiate(&p->graph, g, 0);
             if (g) cudaGraphDestroy(g);
         }
-        cudaStreamDestroy(cs);
+        if (cs) cudaStreamDestroy(cs);
         if (e != cudaSuccess) {
+            // e.g. the calling thread is inside a global-mode stream capture:
+            // the same kernels are launched one by one instead
+            if (p->graph) cudaGraphExecDestroy(p->graph);
             p->graph = nullptr;
-            return cuda_fail(e, "decode graph capture");
+            p->graph_failed = true;
+            cudaGetLastError();
+            return plan_decode(p, s, nullptr, nullptr);
         }
         p->graph_ctas = p->max_ctas;
     }
