@@ -375,12 +375,22 @@ int bs_plan_decode(bs_plan *p, void *stream) { return plan_decode(p, stream, nul
 static int plan_decode_graph(bs_plan *p, cudaStream_t s) {
     if (p->kind != kPlanXc || p->n_internal == 0 || p->graph_failed) return plan_decode(p, s, nullptr, nullptr);
     DeviceGuard guard(p->device);
+    // a caller capturing `s` records the kernels themselves into its graph
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(s, &cap) != cudaSuccess || cap != cudaStreamCaptureStatusNone) {
+        cudaGetLastError();
+        return plan_decode(p, s, nullptr, nullptr);
+    }
     cudaError_t e = cudaSuccess;
     if (!p->graph || p->graph_ctas != p->max_ctas) {
         if (p->graph) {
             cudaGraphExecDestroy(p->graph);
             p->graph = nullptr;
         }
+        // relaxed mode for this thread: creating the private stream must not
+        // invalidate a global-mode capture running elsewhere in the process
+        cudaStreamCaptureMode mode = cudaStreamCaptureModeRelaxed;
+        cudaThreadExchangeStreamCaptureMode(&mode);
         e = xc_decode_attrs(p->coders);
         cudaStream_t cs = nullptr;
         if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&cs, cudaStreamNonBlocking);
@@ -397,6 +407,7 @@ static int plan_decode_graph(bs_plan *p, cudaStream_t s) {
             if (g) cudaGraphDestroy(g);
         }
         if (cs) cudaStreamDestroy(cs);
+        cudaThreadExchangeStreamCaptureMode(&mode);   // the caller's mode back
         if (e != cudaSuccess) {
             // e.g. the calling thread is inside a global-mode stream capture:
             // the same kernels are launched one by one instead

@@ -110,9 +110,10 @@ int bs_plan_decode_timed(bs_plan *plan, void *stream, void *ev_start, void *ev_s
  * decode's kernels run as one CUDA graph launch (about a quarter of the host
  * time of launching them one by one): the graph is captured on a private
  * stream at the plan's first event-chained call and again after
- * bs_plan_set_max_ctas changes the cap; where it cannot be captured (for
- * example while the calling thread is inside a global-mode stream capture)
- * the kernels are launched one by one.  No reference counterpart. */
+ * bs_plan_set_max_ctas changes the cap (in relaxed capture mode for the
+ * calling thread, so a capture running elsewhere is not disturbed).  When
+ * `stream` is itself being captured by the caller, or the graph cannot be
+ * captured, the kernels are launched one by one.  No reference counterpart. */
 int bs_plan_decode_after(bs_plan *plan, void *stream, void *wait_event, void *done_event);
 /* The whole per-layer hand-off of a two-stream prefetch in one call:
  * `release_event` is recorded on `main_stream` (the running layer is done with

@@ -348,3 +348,29 @@ def test_event_chained_decode_runs_as_one_captured_graph():
             assert out.cpu().view(torch.uint8).numpy().tobytes() == raw, (k, cap)
             assert p.launch_count() == 2 * (k + 1)
         p.check()
+
+
+def test_event_chained_decode_inside_a_callers_graph_capture():
+    """A plan's first event-chained decode issued while the caller captures
+    its own CUDA graph (torch.cuda.graph, global capture mode): the library
+    either nests its captured graph or, where it cannot capture, launches the
+    kernels one by one into the caller's capture; replaying the caller's
+    graph decodes exactly either way."""
+    from bigsmall_b200 import gpu
+    n = 300_001
+    raw = _normal(n, 9)
+    blob = _dev(O.xc_encode(raw, 2, 12, 4096))
+    out = torch.empty(n, dtype=torch.bfloat16, device="cuda")
+    with gpu.XcPlan([(blob, out, 4096)], coders="pair") as p:
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            p.decode_after(s)
+        for _ in range(2):
+            out.fill_(0)
+            torch.cuda.synchronize()
+            g.replay()
+            torch.cuda.synchronize()
+            assert out.cpu().view(torch.uint8).numpy().tobytes() == raw
+        p.check()
