@@ -138,3 +138,38 @@ def test_ac_cuda_slot_and_registry(manifest):
     b0, extras0 = enc(raw, chunk_elems=4096, coder="rans")
     assert b0 == O.xc_encode(raw, 0, 12, 4096) and dec(b0, extras0, len(raw) // 2) == raw
     assert "bf16_parallel_v1" in codec_registry.registered_names()
+
+
+def test_empty_tensors_on_every_path():
+    """Zero-element tensors (the reference's codecs return b'' for them,
+    bigsmall/codecs/bf16_parallel.py:270-271): the codec calls, a plan that
+    mixes them with real tensors, a container holding one, and the KV cache."""
+    from bigsmall_b200 import decoder, gpu
+    from bigsmall_b200.codecs import bf16_parallel, exp_chunked
+    from bigsmall_b200.kv_cache import compress_kv_entry, decompress_kv_entry
+    from bigsmall_b200.loader import ContainerImage, DeviceLoader
+    assert exp_chunked.decode(b"", gpu.xc_extras(), 0) == b""
+    assert bf16_parallel.decode(b"", {"n_streams": 32}, 0) == b""
+    blob, extras = exp_chunked.encode(b"")
+    assert blob == b"" and extras["chunk_elems"] == gpu.DEFAULT_CHUNK_ELEMS
+    x = (torch.randn(70_001) * 0.02).to(torch.bfloat16).cuda()
+    b = gpu.encode_xc(x)
+    empty_blob = torch.empty(0, dtype=torch.uint8, device="cuda")
+    out, none = torch.empty_like(x), torch.empty(0, dtype=torch.bfloat16, device="cuda")
+    with gpu.XcPlan([(empty_blob, none, 4096), (b, out, gpu.DEFAULT_CHUNK_ELEMS), (empty_blob, none, 256)]) as p:
+        p.run()
+        assert p.check() == [0, 0, 0]
+    assert torch.equal(out.view(torch.int16), x.view(torch.int16))
+    w = {"a.weight": x.cpu().reshape(70_001), "empty.weight": torch.empty(0, dtype=torch.bfloat16),
+         "b.weight": torch.empty(0, 4, dtype=torch.bfloat16)}
+    img = ContainerImage.from_bytes(decoder.compress_tensors(w, with_md5=False))
+    ld = DeviceLoader(img, device=0)
+    try:
+        got = ld.run()
+    finally:
+        ld.close()
+    assert torch.equal(got["a.weight"].cpu().view(torch.int16), w["a.weight"].view(torch.int16))
+    assert got["empty.weight"].numel() == 0 and tuple(got["b.weight"].shape) == (0, 4)
+    k = torch.empty(1, 8, 0, 64, dtype=torch.bfloat16)
+    k2, v2 = decompress_kv_entry(compress_kv_entry(k, k), device="cuda")
+    assert tuple(k2.shape) == (1, 8, 0, 64) and tuple(v2.shape) == (1, 8, 0, 64)
