@@ -36,21 +36,32 @@ import torch
 from .streaming import StreamingLoader
 
 
-def _get_module(root, dotted: str):
+def _get_dotted_module(root, dotted: str):
+    """Walk a dotted module path, indexing ModuleLists by integer parts
+    (BigSmall bigsmall/streaming_inference.py:350-358)."""
     obj = root
     for p in dotted.split("."):
         obj = obj[int(p)] if p.isdigit() else getattr(obj, p)
     return obj
 
 
-def _set_param(root, dotted: str, tensor: torch.Tensor) -> None:
+def _set_param_data(root, dotted: str, tensor: torch.Tensor) -> None:
+    """Swap the tensor behind a parameter (or buffer) by dotted name, whether
+    it lives on ``meta`` or a real device; parameters stay ``nn.Parameter``
+    (BigSmall bigsmall/streaming_inference.py:49-70)."""
     parts = dotted.split(".")
-    mod = _get_module(root, ".".join(parts[:-1])) if len(parts) > 1 else root
+    mod = _get_dotted_module(root, ".".join(parts[:-1])) if len(parts) > 1 else root
     leaf = parts[-1]
     if isinstance(getattr(mod, leaf, None), torch.nn.Parameter) or leaf in dict(mod.named_parameters(recurse=False)):
         setattr(mod, leaf, torch.nn.Parameter(tensor, requires_grad=False))
     else:
         setattr(mod, leaf, tensor)
+
+
+def _layer_prefix(layer_idx: int, layer_template: str = "model.layers.{}") -> str:
+    """Dotted name prefix of one layer's tensors in the container
+    (BigSmall bigsmall/streaming_inference.py:73-74)."""
+    return layer_template.format(layer_idx) + "."
 
 
 def _materialize_meta_buffers(model, config, device) -> None:
@@ -66,7 +77,7 @@ def _materialize_meta_buffers(model, config, device) -> None:
             except TypeError:
                 new = type(mod)(config, device=device)
             parent_name, _, leaf = name.rpartition(".")
-            parent = _get_module(model, parent_name) if parent_name else model
+            parent = _get_dotted_module(model, parent_name) if parent_name else model
             setattr(parent, leaf, new)
         else:
             for bname, b in list(mod.named_buffers(recurse=False)):
@@ -97,13 +108,13 @@ class BigSmallStreamingModel:
         # non-layer weights: decoded once, resident
         non_layer = self.loader.load_non_layer_tensors()
         for name, t in non_layer.items():
-            _set_param(self.model, name, t)
+            _set_param_data(self.model, name, t)
         if getattr(self.config, "tie_word_embeddings", False) and "lm_head.weight" not in non_layer:
             emb = self.model.get_input_embeddings().weight
             self.model.get_output_embeddings().weight = emb
         _materialize_meta_buffers(self.model, self.config, self.device)
         # layer slots: one set of device buffers per slot, shaped like layer 0
-        self._prefix = [layer_template.format(i) + "." for i in range(self.n_layers)]
+        self._prefix = [_layer_prefix(i, layer_template) for i in range(self.n_layers)]
         self._local = []
         for i in range(self.n_layers):
             names = self.loader.layer_tensor_names(i)
@@ -161,9 +172,9 @@ class BigSmallStreamingModel:
 
     # ------------------------------------------------------------------
     def _bind(self, layer: int, slot: int) -> None:
-        mod = _get_module(self.model, self.layer_template.format(layer))
+        mod = _get_dotted_module(self.model, self.layer_template.format(layer))
         for k, t in self._slots[slot].items():
-            _set_param(mod, k, t)
+            _set_param_data(mod, k, t)
         self._bound[layer] = slot
 
     def _prime(self, first_layer: int = 0) -> None:
@@ -178,7 +189,7 @@ class BigSmallStreamingModel:
         self._primed = True
 
     def _patch_layer(self, layer_idx: int) -> None:
-        mod = _get_module(self.model, self.layer_template.format(layer_idx))
+        mod = _get_dotted_module(self.model, self.layer_template.format(layer_idx))
         original = mod.forward
         outer = self
 

@@ -37,12 +37,12 @@ def random_weights(config, seed: int = 0, device="cuda", model_cls=None) -> dict
 def resident_model(config, weights: dict, device="cuda", model_cls=None):
     """An eval-mode model whose parameters are exactly `weights` (no copies)."""
     from transformers import AutoModelForCausalLM
-    from .streaming_inference import _materialize_meta_buffers, _set_param
+    from .streaming_inference import _materialize_meta_buffers, _set_param_data
     ctor = model_cls or AutoModelForCausalLM.from_config
     with torch.device("meta"):
         m = ctor(config)
     for n, t in weights.items():
-        _set_param(m, n, t)
+        _set_param_data(m, n, t)
     if getattr(config, "tie_word_embeddings", False) and "lm_head.weight" not in weights:
         m.get_output_embeddings().weight = m.get_input_embeddings().weight
     _materialize_meta_buffers(m, config, torch.device(device))
