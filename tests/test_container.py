@@ -115,3 +115,23 @@ def test_owned_for_header_mixed_chunk_sizes():
         assert all(name != "tied" for r in owned for name, _, _ in r)
     with pytest.raises(ValueError):
         owned_for(hdr, 2, 2)
+
+
+def test_version_error_messages_follow_the_reference():
+    """Message shape of BigSmallVersionError for a future container version, an
+    unknown codec and direct construction (reference tests/test_version_errors.py:12-71)."""
+    import bigsmall_b200
+    from bigsmall_b200.decoder import _decode_blob
+    assert issubclass(bigsmall_b200.BigSmallVersionError, Exception)
+    hb = b"{}"
+    with pytest.raises(BigSmallVersionError) as ei:
+        C.parse_header(b"BGSM" + struct.pack("<H", 99) + struct.pack("<I", len(hb)) + hb)
+    assert "pip install --upgrade bigsmall" in str(ei.value) and "requires bigsmall >= 2.4.0" in str(ei.value)
+    meta = {"name": "x", "shape": [4], "dtype": "BF16", "codec": "future_codec_v9", "special": None,
+            "compressed_bytes": 8, "offset": 0, "md5": "0" * 32, "extra": None}
+    with pytest.raises(BigSmallVersionError) as ei:
+        _decode_blob(meta, b"\x00" * 8)
+    assert "pip install --upgrade bigsmall" in str(ei.value) and "future_codec_v9" in str(ei.value)
+    msg = str(BigSmallVersionError(required="3.0.0", installed="2.4.0", detail="hypothetical"))
+    for part in ("requires bigsmall >= 3.0.0", "you have 2.4.0", "pip install --upgrade bigsmall", "hypothetical"):
+        assert part in msg
