@@ -266,7 +266,7 @@ def main():
     ap.add_argument("--stream-priority", default="1",
                     help="config 4: comma list of 0/1: run the model on a high-priority stream (1) or not")
     ap.add_argument("--kv-layers", type=int, default=32, help="config kv: layers of K and V (32 = config 5)")
-    ap.add_argument("--enc-streams", type=int, default=3,
+    ap.add_argument("--enc-streams", type=int, default=4,
                     help="config kv: encoders (each with its own workspace) on as many streams, tensors "
                          "assigned round-robin, so consecutive tensors' encodes overlap")
     ap.add_argument("--prefill-timeline", action="store_true",

@@ -6,8 +6,11 @@
 // leaves HBM:
 //   1. xc_enc_hist_kernel    exponent histogram (per-warp shared-memory bins)
 //                            and the sign|mantissa byte plane, one pass.
-//      (pair coder: xc_enc_window_kernel picks the 15-exponent window, then
-//      xc_enc_pair_hist_kernel counts the pair symbols)
+//      Pair coder: xc_enc_expo_hist_kernel counts exponents only, over one
+//      eighth of a large tensor; xc_enc_window_kernel picks the 15-exponent
+//      window and derives the pair-symbol counts from that histogram, as
+//      products of the two window-index marginals; the chunk encoder writes
+//      the plane.  The input is then read once in full, by the chunk encoder.
 //   2. xc_enc_setup_kernel   deterministic frequency quantisation (the same
 //                            rule as the CPU reference encoder, one symbol per
 //                            thread), blob header, per-symbol encode table.
@@ -113,6 +116,50 @@ __global__ void __launch_bounds__(256) xc_enc_hist_kernel(const uint16_t *__rest
 #pragma unroll
     for (int k = 0; k < 8; k++) s += h[k][threadIdx.x];
     if (s) atomicAdd(&counts[threadIdx.x], static_cast<unsigned long long>(s));
+}
+
+// 1b. pair coder: exponent histogram only (its chunk encoder writes the plane).
+// A tensor of at least kSampleMin values is sampled: the values of the
+// 2048-value blocks whose index is a multiple of 8, one eighth of the input
+// (2048 values are 256 16-byte vectors, so vector q is sampled when
+// q mod 2048 < 256).  The pair coder's escapes keep its alphabet closed (16
+// window indices), so a sampled histogram can never leave a coded symbol
+// without a frequency once every window index gets one (the window kernel).
+constexpr uint64_t kSampleMin = 1ull << 20;
+
+__host__ __device__ inline uint64_t sampled_vectors(uint64_t n8) {
+    return (n8 >> 11) * 256 + (((n8 & 2047) < 256) ? (n8 & 2047) : 256);
+}
+
+__global__ void __launch_bounds__(256) xc_enc_expo_hist_kernel(const uint16_t *__restrict__ in, uint64_t n,
+                                                               unsigned long long *counts) {
+    __shared__ uint32_t h[8][256];
+    const uint32_t w = threadIdx.x >> 5;
+    for (int i = threadIdx.x; i < 8 * 256; i += 256) (&h[0][0])[i] = 0;
+    __syncthreads();
+    const bool sample = n >= kSampleMin;
+    const uint64_t n8 = n / 8;
+    const uint64_t nv = sample ? sampled_vectors(n8) : n8;
+    const uint64_t stride = static_cast<uint64_t>(gridDim.x) * blockDim.x;
+    for (uint64_t k = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; k < nv; k += stride) {
+        const uint64_t q = sample ? ((k >> 8) << 11) | (k & 255) : k;
+        const uint4 v = ld_stream16(reinterpret_cast<const uint4 *>(in) + q);
+        const uint32_t wv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            atomicAdd(&h[w][(wv[j] >> 7) & 0xFF], 1u);
+            atomicAdd(&h[w][(wv[j] >> 23) & 0xFF], 1u);
+        }
+    }
+    if (blockIdx.x == 0) {
+        for (uint64_t i = n8 * 8 + threadIdx.x; i < n; i += blockDim.x)
+            if (!sample || ((i >> 11) & 7) == 0) atomicAdd(&h[w][(in[i] >> 7) & 0xFF], 1u);
+    }
+    __syncthreads();
+    uint32_t t = 0;
+#pragma unroll
+    for (int k = 0; k < 8; k++) t += h[k][threadIdx.x];
+    if (t) atomicAdd(&counts[threadIdx.x], static_cast<unsigned long long>(t));
 }
 
 // 2. quantise + header -----------------------------------------------------
@@ -274,18 +321,32 @@ __global__ void __launch_bounds__(256) xc_enc_setup_kernel(const unsigned long l
     }
 }
 
-// 2b. pair coder: exponent window and pair-symbol histogram ------------------
+// 2b. pair coder: exponent window and pair-symbol counts ---------------------
 __device__ __forceinline__ uint32_t pair_a(uint32_t v, uint32_t e_lo) {
     const uint32_t d = ((v >> 7) & 0xFF) - e_lo;   // wraps to a large value below e_lo
     return min(d, 15u);
 }
 
-// the 15-wide exponent window holding the most values (lowest base on ties):
-// thread w sums window w, then a max reduction keeps the lowest w among equals
-__global__ void __launch_bounds__(256) xc_enc_window_kernel(const unsigned long long *counts, uint32_t *aux) {
+// The 15-wide exponent window holding the most values (lowest base on ties):
+// thread w sums window w, then a max reduction keeps the lowest w among equals.
+// Then the pair-symbol counts the frequencies are quantised from (a product
+// model: a pair codes two neighbouring values, whose exponents are close to
+// independent, so this costs about 0.001-0.007 bits per value against the
+// pairs' own histogram and saves a pass over the input):
+//   s     values the histogram counted (n, or the sample of xc_enc_expo_hist_kernel),
+//   c(a)  counted values with window index a (a = 15: outside the window),
+//   m(a)  = max(1, c(a) * 2^16 / s) if c(a) > 0; else 1 for a sampled
+//         histogram (the rest of the tensor may hold such values), 0 otherwise,
+//   pc(a*16 + b) = m(a) * m(b), plus 1 at (a of the last value, 0) when n is
+//   odd (that value's pair has the phantom b = 0, so its symbol needs f > 0).
+__global__ void __launch_bounds__(256) xc_enc_window_kernel(const unsigned long long *counts,
+                                                            const uint16_t *__restrict__ in, uint64_t n,
+                                                            uint32_t *aux, unsigned long long *pcounts) {
     __shared__ unsigned long long c[256];
     __shared__ unsigned long long s_m[8];
     __shared__ uint32_t s_w[8];
+    __shared__ unsigned long long s_marg[16];
+    __shared__ uint32_t s_elo;
     const uint32_t t = threadIdx.x, lane = t & 31;
     c[t] = counts[t];
     __syncthreads();
@@ -309,45 +370,29 @@ __global__ void __launch_bounds__(256) xc_enc_window_kernel(const unsigned long 
         for (int k = 1; k < 8; k++)
             if (better(s_m[k], s_w[k], m, w)) { m = s_m[k]; w = s_w[k]; }
         *aux = w;
-    }
-}
-
-// pairs (2k, 2k+1) of the tensor; an odd tail value pairs with b = 0
-__global__ void __launch_bounds__(256) xc_enc_pair_hist_kernel(const uint16_t *__restrict__ in, uint64_t n,
-                                                               const uint32_t *aux,
-                                                               unsigned long long *pcounts) {
-    __shared__ uint32_t h[8][256];
-    const uint32_t w = threadIdx.x >> 5;
-    for (int i = threadIdx.x; i < 8 * 256; i += 256) (&h[0][0])[i] = 0;
-    __syncthreads();
-    const uint32_t e_lo = *aux;
-    const uint64_t n8 = n / 8;
-    const uint64_t stride = static_cast<uint64_t>(gridDim.x) * blockDim.x;
-    for (uint64_t q = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; q < n8; q += stride) {
-        const uint4 v = ld_stream16(reinterpret_cast<const uint4 *>(in) + q);
-        const uint32_t wv[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-        for (int k = 0; k < 4; k++)
-            atomicAdd(&h[w][pair_a(wv[k] & 0xFFFF, e_lo) * 16 + pair_a(wv[k] >> 16, e_lo)], 1u);
-    }
-    if (blockIdx.x == 0) {
-        for (uint64_t i = n8 * 8 + 2 * threadIdx.x; i < n; i += 2 * blockDim.x) {
-            const uint32_t b = i + 1 < n ? pair_a(in[i + 1], e_lo) : 0u;
-            atomicAdd(&h[w][pair_a(in[i], e_lo) * 16 + b], 1u);
-        }
+        s_elo = w;
     }
     __syncthreads();
-    uint32_t t = 0;
-#pragma unroll
-    for (int k = 0; k < 8; k++) t += h[k][threadIdx.x];
-    if (t) atomicAdd(&pcounts[threadIdx.x], static_cast<unsigned long long>(t));
+    const uint32_t e_lo = s_elo;
+    if (t < 16) {
+        unsigned long long counted = 0, inside = 0;
+        for (int k = 0; k < 256; k++) counted += c[k];
+        for (int k = 0; k < 15; k++) inside += c[e_lo + k];
+        const unsigned long long ca = t < 15 ? c[e_lo + t] : counted - inside;
+        const unsigned long long q = (ca << 16) / counted;
+        s_marg[t] = ca ? (q ? q : 1ull) : (n >= kSampleMin ? 1ull : 0ull);
+    }
+    __syncthreads();
+    unsigned long long pc = s_marg[t >> 4] * s_marg[t & 15];
+    if ((n & 1) && t == pair_a(in[n - 1], e_lo) * 16) pc += 1;
+    pcounts[t] = pc;
 }
 
 // 3c. per-chunk reverse rANS over exponent pairs, with the escape list -------
 __global__ void __launch_bounds__(kEncWarps * 32) xc_enc_chunks_pair_kernel(
     const uint16_t *__restrict__ in, uint64_t n, uint32_t ce, uint32_t nc, int prec,
     const uint4 *__restrict__ rcp_tab, const uint32_t *aux, uint8_t *__restrict__ slots, uint64_t slot_b,
-    uint32_t *__restrict__ rec_words, uint32_t *__restrict__ rec_esc) {
+    uint32_t *__restrict__ rec_words, uint32_t *__restrict__ rec_esc, uint8_t *__restrict__ plane) {
     __shared__ uint4 s_tab[256];
     for (uint32_t i = threadIdx.x; i < 256; i += blockDim.x) s_tab[i] = rcp_tab[i];
     __syncthreads();
@@ -402,15 +447,21 @@ __global__ void __launch_bounds__(kEncWarps * 32) xc_enc_chunks_pair_kernel(
             x = x + (t.z >> 16) + q * t.w;
         }
     };
+    uint8_t *pl = plane + e0;
     if (rem) {
         const uint32_t eb = G * 256 + lane * 8;
         for (int jj = 3; jj >= 0; jj--) {
             const uint32_t e = lane * 8 + 2 * jj;
             const bool act = e < rem, has_b = e + 1 < rem;
-            enc((act ? static_cast<uint32_t>(src[eb + 2 * jj]) : 0u) |
-                    (has_b ? static_cast<uint32_t>(src[eb + 2 * jj + 1]) << 16 : 0u), act, has_b);
+            const uint32_t va = act ? static_cast<uint32_t>(src[eb + 2 * jj]) : 0u;
+            const uint32_t vb = has_b ? static_cast<uint32_t>(src[eb + 2 * jj + 1]) : 0u;
+            if (act) pl[eb + 2 * jj] = static_cast<uint8_t>(((va >> 8) & 0x80) | (va & 0x7F));
+            if (has_b) pl[eb + 2 * jj + 1] = static_cast<uint8_t>(((vb >> 8) & 0x80) | (vb & 0x7F));
+            enc(va | (vb << 16), act, has_b);
         }
     }
+    // sign|mantissa bytes of a word's two values at bits 0-7 and 16-23
+    auto sm2 = [](uint32_t w) { return (w & 0x007F007Fu) | ((w >> 8) & 0x00800080u); };
     // groups run backwards; the next two groups' values are in flight
     auto grp = [&](int g) { return reinterpret_cast<const uint4 *>(src + g * 256 + lane * 8)[0]; };
     uint4 n1 = make_uint4(0, 0, 0, 0), n2 = n1;
@@ -420,6 +471,8 @@ __global__ void __launch_bounds__(kEncWarps * 32) xc_enc_chunks_pair_kernel(
         const uint4 v = n1;
         n1 = n2;
         if (g >= 2) n2 = grp(g - 2);
+        reinterpret_cast<uint2 *>(pl + g * 256 + lane * 8)[0] =
+            make_uint2(__byte_perm(sm2(v.x), sm2(v.y), 0x6420), __byte_perm(sm2(v.z), sm2(v.w), 0x6420));
         enc(v.w, true, true);
         enc(v.z, true, true);
         enc(v.y, true, true);
@@ -729,24 +782,26 @@ cudaError_t launch_xc_encode(const uint16_t *d_in, uint64_t n, int coder, int pr
     int dev = 0, sms = 148;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    uint64_t want = (n / 8 + 255) / 256;
+    const bool pair = coder == BS_CODER_RANS_PAIR;
+    const uint64_t vecs = pair && n >= kSampleMin ? sampled_vectors(n / 8) : n / 8;
+    uint64_t want = (vecs + 255) / 256;
     int grid = static_cast<int>(want < static_cast<uint64_t>(sms) * 8 ? (want ? want : 1) : static_cast<uint64_t>(sms) * 8);
-    xc_enc_hist_kernel<<<grid, 256, 0, s>>>(d_in, n, counts, d_out + plane_off);
     uint16_t *slot_list = reinterpret_cast<uint16_t *>(d_ws + slotlist_off(nc));
     const unsigned long long *qcounts = counts;
-    if (coder == BS_CODER_RANS_PAIR) {
-        e = cudaMemsetAsync(pcounts, 0, 2048, s);
-        if (e != cudaSuccess) return e;
-        xc_enc_window_kernel<<<1, 256, 0, s>>>(counts, aux);
-        xc_enc_pair_hist_kernel<<<grid, 256, 0, s>>>(d_in, n, aux, pcounts);
+    if (pair) {
+        xc_enc_expo_hist_kernel<<<grid, 256, 0, s>>>(d_in, n, counts);
+        xc_enc_window_kernel<<<1, 256, 0, s>>>(counts, d_in, n, aux, pcounts);
         qcounts = pcounts;
+    } else {
+        xc_enc_hist_kernel<<<grid, 256, 0, s>>>(d_in, n, counts, d_out + plane_off);
     }
     xc_enc_setup_kernel<<<1, 256, 0, s>>>(qcounts, n, coder, prec, ce, static_cast<uint32_t>(nc), groups, d_out,
                                           tab, slot_list, aux);
     const unsigned enc_blocks = static_cast<unsigned>((nc + kEncWarps - 1) / kEncWarps);
     if (coder == BS_CODER_RANS_PAIR) {
         xc_enc_chunks_pair_kernel<<<enc_blocks, kEncWarps * 32, 0, s>>>(d_in, n, ce, static_cast<uint32_t>(nc), prec,
-                                                                       rcp, aux, slots, sb, recw, rece);
+                                                                       rcp, aux, slots, sb, recw, rece,
+                                                                       d_out + plane_off);
     } else if (coder == BS_CODER_TANS) {
         auto *scr = reinterpret_cast<uint32_t *>(d_ws + tans_scratch_off(nc, ce));
         xc_enc_chunks_tans_kernel<<<enc_blocks, kEncWarps * 32, 0, s>>>(d_in, n, ce, static_cast<uint32_t>(nc), prec,

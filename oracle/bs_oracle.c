@@ -1062,6 +1062,7 @@ static int64_t xc_encode_chunk(const uint8_t *ex, int64_t cn, int coder, int P, 
 }
 
 /* ---- coder 2: rANS over exponent pairs ---------------------------------- */
+#define XC2_SAMPLE_MIN (1ll << 20)
 static int xc2_window(const int64_t *hist) {
     int best = 0;
     int64_t bm = -1;
@@ -1194,21 +1195,34 @@ int64_t bso_xc_encode_groups(const uint16_t *w, int64_t n, int coder, int prec, 
     int64_t counts[256] = {0};
     uint8_t *ex = (uint8_t *)malloc((size_t)n);
     if (!ex) return BSO_E_NOMEM;
-    for (int64_t i = 0; i < n; i++) { ex[i] = (uint8_t)((w[i] >> 7) & 0xFF); counts[ex[i]]++; }
+    /* coder 2 on a tensor of at least XC2_SAMPLE_MIN values counts only the */
+    /* 2048-value blocks whose index is a multiple of 8                      */
+    const int sampled = coder == 2 && n >= XC2_SAMPLE_MIN;
+    for (int64_t i = 0; i < n; i++) {
+        ex[i] = (uint8_t)((w[i] >> 7) & 0xFF);
+        if (!sampled || ((i >> 11) & 7) == 0) counts[ex[i]]++;
+    }
     uint16_t freq[256];
     int e_lo = 0;
     if (coder == 2) {
-        /* pair-symbol histogram over every chunk (a missing second element is b = 0) */
+        /* pair-symbol counts of the product model: window-index marginals   */
+        /* c(a) of the s counted values (a = 15 outside the window), m(a) =  */
+        /* max(1, c(a) * 2^16 / s) for c(a) > 0, else 1 when sampled and 0   */
+        /* when not; pc(a*16+b) = m(a) * m(b), plus 1 at (a_last, 0) for odd */
+        /* n (the last value's pair has the phantom b = 0)                   */
         e_lo = xc2_window(counts);
-        int64_t pc[256] = {0};
-        for (uint32_t k = 0; k < nc; k++) {
-            int64_t e0 = (int64_t)k * chunk_elems;
-            int64_t cn = n - e0 < chunk_elems ? n - e0 : chunk_elems;
-            for (int64_t e = 0; e < cn; e += 2) {
-                uint32_t a = xc2_a(ex[e0 + e], e_lo), b = e + 1 < cn ? xc2_a(ex[e0 + e + 1], e_lo) : 0u;
-                pc[a * 16 + b]++;
-            }
+        uint64_t marg[16];
+        uint64_t inside = 0, counted = 0;
+        for (int s = 0; s < 256; s++) counted += (uint64_t)counts[s];
+        for (int a = 0; a < 15; a++) inside += (uint64_t)counts[e_lo + a];
+        for (int a = 0; a < 16; a++) {
+            uint64_t ca = a < 15 ? (uint64_t)counts[e_lo + a] : counted - inside;
+            uint64_t q = (ca << 16) / counted;
+            marg[a] = ca ? (q ? q : 1u) : (sampled ? 1u : 0u);
         }
+        int64_t pc[256];
+        for (int s = 0; s < 256; s++) pc[s] = (int64_t)(marg[s >> 4] * marg[s & 15]);
+        if (n & 1) pc[xc2_a(ex[n - 1], e_lo) * 16] += 1;
         bso_xc_quantise(pc, prec, freq);
     } else {
         bso_xc_quantise(counts, prec, freq);

@@ -173,3 +173,31 @@ def test_empty_tensors_on_every_path():
     k = torch.empty(1, 8, 0, 64, dtype=torch.bfloat16)
     k2, v2 = decompress_kv_entry(compress_kv_entry(k, k), device="cuda")
     assert tuple(k2.shape) == (1, 8, 0, 64) and tuple(v2.shape) == (1, 8, 0, 64)
+
+
+def test_tiny_tensors_stored_raw_at_the_reference_threshold(tmp_path):
+    """Tensors under 512 bytes go raw, stored at their exact byte count; a bf16
+    tensor of exactly 512 bytes takes the codec (reference
+    tests/test_raw_tiny.py:30-110, bigsmall/encoder.py:57, :386-388)."""
+    from bigsmall_b200 import decoder
+    from bigsmall_b200.container import parse_header
+    g = torch.Generator().manual_seed(0)
+    w = {"tiny.bias": torch.randn(128, generator=g).to(torch.bfloat16),
+         "very_tiny.scale": torch.tensor([1.5, -0.25], dtype=torch.float32),
+         "norm.weight": torch.randn(2048, generator=g).to(torch.bfloat16),
+         "matrix.weight": torch.randn(512, 512, generator=g).to(torch.bfloat16),
+         "at_threshold.weight": torch.zeros(256, dtype=torch.bfloat16),
+         "below_threshold.weight": torch.zeros(255, dtype=torch.bfloat16)}
+    data = decoder.compress_tensors(w, tmp_path / "t.bs")
+    header = parse_header(data)[0]
+    codec = {t["name"]: t["codec"] for t in header["tensors"]}
+    size = {t["name"]: int(t["compressed_bytes"]) for t in header["tensors"]}
+    assert codec["tiny.bias"] == "raw" and size["tiny.bias"] == 256
+    assert codec["very_tiny.scale"] == "raw" and size["very_tiny.scale"] == 8
+    assert codec["below_threshold.weight"] == "raw"
+    for n in ("norm.weight", "matrix.weight", "at_threshold.weight"):
+        assert codec[n] == "bf16_exp_chunked_v1", n
+    out = decoder.load(tmp_path / "t.bs", device="cuda")
+    for k, v in w.items():
+        got = out[k].cpu().contiguous().view(torch.uint8).numpy().tobytes()
+        assert hashlib.md5(got).hexdigest() == hashlib.md5(v.view(torch.uint8).numpy().tobytes()).hexdigest(), k

@@ -207,3 +207,46 @@ def test_xc_groups_header_checked(coder):
         O.xc_encode(raw, coder, 12, 4096, 32)
     with pytest.raises(O.OracleError):       # chunk not a multiple of groups
         O.xc_encode(raw, coder, 12, 65536, 3)
+
+
+def _product_model_freqs(raw: np.ndarray, prec: int = 12) -> tuple[int, np.ndarray]:
+    """The pair coder's frequency rule restated in numpy: the exponent
+    histogram counts every value, or for n >= 2^20 the 2048-value blocks whose
+    index is a multiple of 8; window = first maximal 15-exponent window;
+    window-index marginals c(a) of the s counted values; m(a) =
+    max(1, c(a) * 2^16 // s) for c(a) > 0, else 1 if sampled, 0 if not;
+    counts m(a) * m(b), plus 1 at (a of the last value, 0) for odd n; then the
+    format's quantisation."""
+    n = raw.size
+    ex = (raw >> 7) & 0xFF
+    sampled = n >= 1 << 20
+    counted = ex[((np.arange(n) >> 11) & 7) == 0] if sampled else ex
+    hist = np.bincount(counted, minlength=256).astype(np.int64)
+    e_lo = int(np.argmax([hist[w:w + 15].sum() for w in range(242)]))
+    c = np.zeros(16, np.int64)
+    c[:15] = hist[e_lo:e_lo + 15]
+    c[15] = counted.size - c[:15].sum()
+    m = np.where(c > 0, np.maximum(1, (c << 16) // counted.size), 1 if sampled else 0)
+    pc = np.outer(m, m).reshape(-1)
+    if n % 2:
+        d = int(ex[-1]) - e_lo
+        pc[(d if 0 <= d <= 14 else 15) * 16] += 1
+    return e_lo, O.xc_quantise(pc, prec)
+
+
+@pytest.mark.parametrize("seed,n", [(0, 50_000), (1, 50_001), (2, 1), (3, 255), (4, 70_001),
+                                    (5, (1 << 20) - 1), (6, 1 << 20), (7, (1 << 20) + 12_345), (8, 3 << 20)])
+def test_xc_pair_coder_frequencies_follow_the_product_model(seed, n):
+    """Coder 2 quantises m(a) * m(b) from the exponent histogram alone (no pass
+    over the pairs; an eighth of the blocks from 2^20 values on); its header's
+    window and frequency table match a numpy restatement of that rule, for
+    normal, wide-range and odd-length inputs on both sides of the threshold."""
+    rng = np.random.default_rng(seed)
+    w = (rng.standard_normal(n) * np.exp(rng.standard_normal(n) * (3 if seed % 2 else 0.3))).astype(np.float32)
+    raw = (w.view(np.uint32) >> 16).astype(np.uint16)
+    for prec in (10, 12):
+        blob = O.xc_encode(raw.tobytes(), 2, prec, 4096)
+        e_lo, want = _product_model_freqs(raw, prec)
+        assert struct.unpack_from("<I", blob, 28)[0] == e_lo
+        assert np.array_equal(np.frombuffer(blob, dtype="<u2", count=256, offset=64), want), (seed, n, prec)
+        assert O.xc_decode(blob, n) == raw.tobytes()
