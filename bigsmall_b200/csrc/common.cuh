@@ -63,31 +63,34 @@ struct XcTensorDev {
     uint32_t rec_lim16;       // end of the chunk-record area in 16-byte units from chunks_off
 };
 
-// Exact unsigned division by an invariant divisor (Granlund & Montgomery,
-// "Division by Invariant Integers using Multiplication", PLDI 1994, Fig. 4.1,
-// N = 32): with l = ceil(log2 d) and m' = floor(2^32 (2^l - d) / d) + 1,
-// q = (t + ((n - t) >> min(l, 1))) >> max(l - 1, 0), t = mulhi(m', n), equals
-// floor(n / d) for every 32-bit n and 1 <= d < 2^32.  The rANS encoders divide
-// the state by a symbol frequency once per value; this replaces that divide.
-struct RcpDiv {
-    uint32_t m;
-    uint32_t sh1, sh2;
-};
-
-__host__ __device__ inline RcpDiv rcp_div_make(uint32_t d) {
-    uint32_t l = 0;
-    while ((1ull << l) < d) l++;
-    const uint64_t m = ((1ull << 32) * ((1ull << l) - d)) / d + 1;
-    return RcpDiv{static_cast<uint32_t>(m), l ? 1u : 0u, l ? l - 1 : 0u};
+// rANS encode step with the division by the symbol frequency done as a
+// multiplication.  The step maps the 32-bit state x (already renormalised, so
+// 1 <= x < f * 2^(32-P)) to (x / f) * M + (x mod f) + cum, written as
+// x + cum + q * (M - f) with q = floor(x / f).  q = floor(x * m / 2^64) for
+// m = ceil(2^64 / f) = floor((2^64 - 1) / f) + 1 (f >= 2): m / 2^64 exceeds
+// 1 / f by less than 2^-64, so x * m / 2^64 exceeds x / f by less than 2^-32 <
+// 1 / f, which never carries past the next integer.  The 64 x 32 product is two
+// 32-bit multiplies, mulhi(x, m_lo) and x * m_hi + that (a 64-bit result whose
+// high word is q).  For f = 1, m = 2^64 - 1 gives q = x - 1, and the entry adds
+// M - 1 to cum to make up for it.  An entry is {m_lo, m_hi, f << (32 - P)
+// (the renorm threshold), cum' | (M - f) << 16}.
+__host__ __device__ inline uint4 rans_enc_entry(uint32_t f, uint32_t cum, uint32_t P) {
+    const uint32_t M = 1u << P;
+    const uint64_t m = f <= 1 ? ~0ull : ~0ull / f + 1;
+    const uint32_t fe = f ? f : 1u;
+    const uint32_t cw = (cum + (fe == 1 ? M - 1 : 0u)) | ((M - fe) << 16);
+    return make_uint4(static_cast<uint32_t>(m), static_cast<uint32_t>(m >> 32), fe << (32 - P), cw);
 }
 
-__host__ __device__ inline uint32_t rcp_div(uint32_t n, uint32_t m, uint32_t sh1, uint32_t sh2) {
+// (x / f) * M + (x mod f) + cum for 1 <= x < f * 2^(32-P), from the entry above
+__host__ __device__ inline uint32_t rans_enc_update(uint32_t x, const uint4 &t) {
 #ifdef __CUDA_ARCH__
-    const uint32_t t = __umulhi(m, n);
+    const uint32_t lo = __umulhi(x, t.x);
 #else
-    const uint32_t t = static_cast<uint32_t>((static_cast<uint64_t>(m) * n) >> 32);
+    const uint32_t lo = static_cast<uint32_t>((static_cast<uint64_t>(x) * t.x) >> 32);
 #endif
-    return (t + ((n - t) >> sh1)) >> sh2;
+    const uint32_t q = static_cast<uint32_t>((static_cast<uint64_t>(x) * t.y + lo) >> 32);
+    return x + (t.w & 0xFFFFu) + q * (t.w >> 16);
 }
 
 // A work item: up to 16 consecutive chunks of one tensor (xc_warps_per_cta), one CTA.

@@ -40,7 +40,7 @@ constexpr uint64_t kWsTab = 2048;       // u32[256]: freq | cum << 16
 constexpr uint64_t kWsFlags = 3072;     // u32 flags
 constexpr uint64_t kWsAux = 3076;       // u32 pair coder: window base e_lo
 constexpr uint64_t kWsPairCounts = 4096;   // u64[256] pair-symbol histogram
-constexpr uint64_t kWsRcp = 6144;       // uint4[256]: {m', sh1 | sh2 << 8, freq | cum << 16, M - freq}
+constexpr uint64_t kWsRcp = 6144;       // uint4[256]: rANS encode-step entries (rans_enc_entry)
 constexpr uint64_t kWsRec = 10240;      // u32[n_chunks] words per record, then u32[n_chunks] escapes
 
 inline uint64_t rup(uint64_t x, uint64_t a) { return (x + a - 1) / a * a; }
@@ -284,13 +284,10 @@ __global__ void __launch_bounds__(256) xc_enc_setup_kernel(const unsigned long l
     if (tab_end + tid < plane_off) out[tab_end + tid] = 0;
     if (plane_off + n + tid < chunks_off) out[plane_off + n + tid] = 0;
     enc_tab[tid] = static_cast<uint32_t>(f[tid]) | (s_cum[tid] << 16);
-    {
-        // per-symbol divide-by-frequency constants for the rANS encoders
-        const uint32_t fs = static_cast<uint32_t>(f[tid]);
-        const RcpDiv r = rcp_div_make(fs ? fs : 1u);
-        reinterpret_cast<uint4 *>(enc_tab + (kWsRcp - kWsTab) / 4)[tid] =
-            make_uint4(r.m, r.sh1 | (r.sh2 << 8), fs | (s_cum[tid] << 16), static_cast<uint32_t>(M) - fs);
-    }
+    // per-symbol encode-step entries of the rANS encoders (renorm threshold,
+    // divide-by-frequency as a multiplication, cum and M - f)
+    reinterpret_cast<uint4 *>(enc_tab + (kWsRcp - kWsTab) / 4)[tid] =
+        rans_enc_entry(static_cast<uint32_t>(f[tid]), s_cum[tid], static_cast<uint32_t>(prec));
     if (coder != BS_CODER_TANS) return;
     // tANS: spread the symbols over the 2^P states with Collet's step (the k-th
     // placement in symbol order lands on (k * step) mod M), then list each
@@ -390,7 +387,7 @@ __global__ void __launch_bounds__(256) xc_enc_window_kernel(const unsigned long 
 
 // 3c. per-chunk reverse rANS over exponent pairs, with the escape list -------
 __global__ void __launch_bounds__(kEncWarps * 32) xc_enc_chunks_pair_kernel(
-    const uint16_t *__restrict__ in, uint64_t n, uint32_t ce, uint32_t nc, int prec,
+    const uint16_t *__restrict__ in, uint64_t n, uint32_t ce, uint32_t nc,
     const uint4 *__restrict__ rcp_tab, const uint32_t *aux, uint8_t *__restrict__ slots, uint64_t slot_b,
     uint32_t *__restrict__ rec_words, uint32_t *__restrict__ rec_esc, uint8_t *__restrict__ plane) {
     __shared__ uint4 s_tab[256];
@@ -400,7 +397,6 @@ __global__ void __launch_bounds__(kEncWarps * 32) xc_enc_chunks_pair_kernel(
     const uint32_t lane = threadIdx.x & 31;
     const uint32_t c = blockIdx.x * kEncWarps + (threadIdx.x >> 5);
     if (c >= nc) return;
-    const uint32_t P = static_cast<uint32_t>(prec);
     const uint64_t e0 = static_cast<uint64_t>(c) * ce;
     const uint32_t cn = (n - e0) < ce ? static_cast<uint32_t>(n - e0) : ce;
     const uint16_t *src = in + e0;
@@ -418,7 +414,6 @@ __global__ void __launch_bounds__(kEncWarps * 32) xc_enc_chunks_pair_kernel(
     // keeps the words (<= ce bytes, downwards from the slot end) above eend.
     uint8_t *eend = slot + kXcPairRecHdr + ce;
     uint32_t ecur = 0;
-    const uint32_t thr_shift = 32 - P;
 
     // x <- (x / f) << P | (x mod f) + cum  ==  x + cum + (x / f) (M - f)
     uint16_t *wtop = wend - 1;   // the next word goes to wtop[-cur - (emitting lanes below)]
@@ -437,15 +432,12 @@ __global__ void __launch_bounds__(kEncWarps * 32) xc_enc_chunks_pair_kernel(
             ecur = static_cast<uint32_t>(k);
         }
         const uint4 t = s_tab[a * 16 + b];
-        const bool emit = act && x >= ((t.z & 0xFFFF) << thr_shift);   // f < 2^P: fits 32 bits
+        const bool emit = act && x >= t.z;   // t.z = f << (32 - P)
         const uint32_t m = __ballot_sync(kFull, emit);
         if (emit) wtop[-static_cast<int32_t>(cur + __popc(m & gt))] = static_cast<uint16_t>(x);
         x = emit ? x >> 16 : x;
         cur += __popc(m);
-        if (act) {
-            const uint32_t q = rcp_div(x, t.x, t.y & 0xFF, t.y >> 8);
-            x = x + (t.z >> 16) + q * t.w;
-        }
+        if (act) x = rans_enc_update(x, t);
     };
     uint8_t *pl = plane + e0;
     if (rem) {
@@ -487,7 +479,7 @@ __global__ void __launch_bounds__(kEncWarps * 32) xc_enc_chunks_pair_kernel(
 
 // 3. per-chunk reverse rANS ---------------------------------------------------
 __global__ void __launch_bounds__(kEncWarps * 32) xc_enc_chunks_kernel(
-    const uint16_t *__restrict__ in, uint64_t n, uint32_t ce, uint32_t nc, int prec,
+    const uint16_t *__restrict__ in, uint64_t n, uint32_t ce, uint32_t nc,
     const uint4 *__restrict__ rcp_tab, uint8_t *__restrict__ slots, uint64_t slot_b,
     uint32_t *__restrict__ rec_words) {
     __shared__ uint4 s_tab[256];
@@ -496,7 +488,6 @@ __global__ void __launch_bounds__(kEncWarps * 32) xc_enc_chunks_kernel(
     const uint32_t lane = threadIdx.x & 31;
     const uint32_t c = blockIdx.x * kEncWarps + (threadIdx.x >> 5);
     if (c >= nc) return;
-    const uint32_t P = static_cast<uint32_t>(prec);
     const uint64_t e0 = static_cast<uint64_t>(c) * ce;
     const uint32_t cn = (n - e0) < ce ? static_cast<uint32_t>(n - e0) : ce;
     const uint16_t *src = in + e0;
@@ -511,18 +502,14 @@ __global__ void __launch_bounds__(kEncWarps * 32) xc_enc_chunks_kernel(
     auto enc = [&](uint32_t v, bool active) {
         const uint32_t sym = (v >> 7) & 0xFF;
         const uint4 t = s_tab[sym];
-        const uint32_t f = t.z & 0xFFFF, cf = t.z >> 16;
-        const bool emit = active && x >= (f << (32 - P));   // f < 2^P: the threshold fits 32 bits
+        const bool emit = active && x >= t.z;   // t.z = f << (32 - P)
         const uint32_t m = __ballot_sync(kFull, emit);
         if (emit) {
             wend[-1 - static_cast<int64_t>(cur + __popc(m & gt))] = static_cast<uint16_t>(x & 0xFFFF);
             x >>= 16;
         }
         cur += __popc(m);
-        if (active) {
-            const uint32_t q = rcp_div(x, t.x, t.y & 0xFF, t.y >> 8);
-            x = x + cf + q * t.w;
-        }
+        if (active) x = rans_enc_update(x, t);
     };
 
     if (rem) {
@@ -799,7 +786,7 @@ cudaError_t launch_xc_encode(const uint16_t *d_in, uint64_t n, int coder, int pr
                                           tab, slot_list, aux);
     const unsigned enc_blocks = static_cast<unsigned>((nc + kEncWarps - 1) / kEncWarps);
     if (coder == BS_CODER_RANS_PAIR) {
-        xc_enc_chunks_pair_kernel<<<enc_blocks, kEncWarps * 32, 0, s>>>(d_in, n, ce, static_cast<uint32_t>(nc), prec,
+        xc_enc_chunks_pair_kernel<<<enc_blocks, kEncWarps * 32, 0, s>>>(d_in, n, ce, static_cast<uint32_t>(nc),
                                                                        rcp, aux, slots, sb, recw, rece,
                                                                        d_out + plane_off);
     } else if (coder == BS_CODER_TANS) {
@@ -807,7 +794,7 @@ cudaError_t launch_xc_encode(const uint16_t *d_in, uint64_t n, int coder, int pr
         xc_enc_chunks_tans_kernel<<<enc_blocks, kEncWarps * 32, 0, s>>>(d_in, n, ce, static_cast<uint32_t>(nc), prec,
                                                                        tab, slot_list, slots, sb, scr, recw);
     } else {
-        xc_enc_chunks_kernel<<<enc_blocks, kEncWarps * 32, 0, s>>>(d_in, n, ce, static_cast<uint32_t>(nc), prec,
+        xc_enc_chunks_kernel<<<enc_blocks, kEncWarps * 32, 0, s>>>(d_in, n, ce, static_cast<uint32_t>(nc),
                                                                   rcp, slots, sb, recw);
     }
     xc_enc_scan_kernel<<<1, 1024, 0, s>>>(recw, rece, coder, static_cast<uint32_t>(nc), d_out, chunks_off, out_cap,
