@@ -418,12 +418,13 @@ __global__ void __launch_bounds__(kEncWarps * 32) xc_enc_chunks_pair_kernel(
     // x <- (x / f) << P | (x mod f) + cum  ==  x + cum + (x / f) (M - f)
     uint16_t *wtop = wend - 1;   // the next word goes to wtop[-cur - (emitting lanes below)]
     // one pair-step: w holds the lane's two values (first in the low half)
-    auto enc = [&](uint32_t w, bool act, bool has_b) {
+    // `chk` false: the caller has seen that no lane's values escape the window
+    auto enc = [&](uint32_t w, bool act, bool has_b, bool chk = true) {
         // window index: exponent - e_lo, 15 (escape) outside the window
         const uint32_t da = ((w >> 7) & 0xFF) - e_lo, db = ((w >> 23) & 0xFF) - e_lo;
         const bool ea = act && da > 14, eb = has_b && db > 14;
         const uint32_t a = act ? min(da, 15u) : 0u, b = has_b ? min(db, 15u) : 0u;
-        if (__ballot_sync(kFull, ea || eb)) {   // rare: only then the per-value ballots
+        if (chk && __ballot_sync(kFull, ea || eb)) {   // rare: only then the per-value ballots
             const uint32_t ba = __ballot_sync(kFull, ea), bb = __ballot_sync(kFull, eb);
             const int64_t k = static_cast<int64_t>(ecur) + __popc(ba) + __popc(bb);
             const int64_t pa = static_cast<int64_t>(__popc(ba & lt) + __popc(bb & lt)) - k;
@@ -465,10 +466,20 @@ __global__ void __launch_bounds__(kEncWarps * 32) xc_enc_chunks_pair_kernel(
         if (g >= 2) n2 = grp(g - 2);
         reinterpret_cast<uint2 *>(pl + g * 256 + lane * 8)[0] =
             make_uint2(__byte_perm(sm2(v.x), sm2(v.y), 0x6420), __byte_perm(sm2(v.z), sm2(v.w), 0x6420));
-        enc(v.w, true, true);
-        enc(v.z, true, true);
-        enc(v.y, true, true);
-        enc(v.x, true, true);
+        // one vote per group on escapes (window index > 14 among the lane's 8
+        // values); the four pair-steps vote again only when one is there
+        auto dmax = [&](uint32_t w) { return max(((w >> 7) & 0xFF) - e_lo, ((w >> 23) & 0xFF) - e_lo); };
+        if (__any_sync(kFull, max(max(dmax(v.x), dmax(v.y)), max(dmax(v.z), dmax(v.w))) > 14)) {
+            enc(v.w, true, true);
+            enc(v.z, true, true);
+            enc(v.y, true, true);
+            enc(v.x, true, true);
+        } else {
+            enc(v.w, true, true, false);
+            enc(v.z, true, true, false);
+            enc(v.y, true, true, false);
+            enc(v.x, true, true, false);
+        }
     }
     reinterpret_cast<uint32_t *>(slot)[lane] = x;
     if (lane == 0) {
