@@ -224,7 +224,10 @@ int bs_xc_encode_workspace(uint64_t n_elems, uint32_t chunk_elems, uint32_t grou
  * cut into `groups` state groups (chunk_elems / groups must be a multiple of
  * 256; groups > 1 writes format version 2).  The exact blob length is written
  * to the device u64 at d_out_len.  Deterministic: the bytes equal the CPU
- * reference encoder's.  Asynchronous on `stream`.
+ * reference encoder's.  Coder 2 quantises a product of its two window-index
+ * marginals, counted over every value, or for n_elems >= 2^20 over the
+ * 2048-value blocks whose index is a multiple of 8; coders 0 and 1 count every
+ * value.  Asynchronous on `stream`.
  * Replaces: bigsmall/codecs/kv_cache.py:41-83 compress_kv_entry's CPU encode. */
 int bs_xc_encode(const void *d_in, uint64_t n_elems, int coder, int prec,
                  uint32_t chunk_elems, uint32_t groups, void *d_out, uint64_t out_cap,
