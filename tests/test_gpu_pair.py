@@ -374,3 +374,21 @@ def test_event_chained_decode_inside_a_callers_graph_capture():
             torch.cuda.synchronize()
             assert out.cpu().view(torch.uint8).numpy().tobytes() == raw
         p.check()
+
+
+def test_device_encoder_when_the_sample_is_unlike_the_rest():
+    """The pair coder's statistics come from every eighth 2048-value block of a
+    tensor of 2^20 values or more; with those blocks all zeros the device
+    encoder still equals the oracle's bytes and decodes exactly."""
+    from bigsmall_b200 import gpu
+    n = (1 << 20) + 4097
+    g = torch.Generator(device="cuda").manual_seed(11)
+    x = (torch.randn(n, generator=g, device="cuda") * 0.02).to(torch.bfloat16)
+    idx = torch.arange(n, device="cuda")
+    x[((idx >> 11) & 7) == 0] = 0
+    blob = gpu.encode_xc(x, coder=2, chunk_elems=32768)
+    raw = x.cpu().view(torch.uint8).numpy().tobytes()
+    assert blob.cpu().numpy().tobytes() == O.xc_encode(raw, 2, 12, 32768)
+    out = torch.empty_like(x)
+    gpu.decode_xc_into(blob, out, 32768)
+    assert torch.equal(out.view(torch.int16), x.view(torch.int16))

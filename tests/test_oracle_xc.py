@@ -250,3 +250,19 @@ def test_xc_pair_coder_frequencies_follow_the_product_model(seed, n):
         assert struct.unpack_from("<I", blob, 28)[0] == e_lo
         assert np.array_equal(np.frombuffer(blob, dtype="<u2", count=256, offset=64), want), (seed, n, prec)
         assert O.xc_decode(blob, n) == raw.tobytes()
+
+
+def test_xc_pair_coder_sample_unlike_the_rest_still_round_trips():
+    """From 2^20 values on the pair coder's statistics come from every eighth
+    2048-value block.  When those blocks are all zeros and the rest are normal
+    weights, every other value escapes the window: the ratio suffers, the round
+    trip does not."""
+    n = (1 << 20) + 4097
+    rng = np.random.default_rng(11)
+    w = (rng.standard_normal(n) * 0.02).astype(np.float32)
+    raw = (w.view(np.uint32) >> 16).astype(np.uint16)
+    raw[((np.arange(n) >> 11) & 7) == 0] = 0
+    blob = O.xc_encode(raw.tobytes(), 2, 12, 32768)
+    assert struct.unpack_from("<I", blob, 28)[0] == 0            # window at the zeros' exponent
+    assert O.xc_decode(blob, n) == raw.tobytes()
+    assert len(blob) > 2 * n                                      # most exponents escaped
