@@ -266,9 +266,11 @@ def main():
     ap.add_argument("--stream-priority", default="1",
                     help="config 4: comma list of 0/1: run the model on a high-priority stream (1) or not")
     ap.add_argument("--kv-layers", type=int, default=32, help="config kv: layers of K and V (32 = config 5)")
-    ap.add_argument("--enc-streams", type=int, default=4,
+    ap.add_argument("--enc-streams", type=int, default=0,
                     help="config kv: encoders (each with its own workspace) on as many streams, tensors "
-                         "assigned round-robin, so consecutive tensors' encodes overlap")
+                         "assigned round-robin, so consecutive tensors' encodes overlap; 0 = enough "
+                         "tensors in flight for about three waves of chunk warps (4 for a config-5 "
+                         "tensor on one GPU, up to 16 for the smaller batch slices of 8 GPUs)")
     ap.add_argument("--prefill-timeline", action="store_true",
                     help="config stream: also record one prefill of each model with the CUDA profiler (CUPTI "
                          "kernel records) and report GPU busy time, decode/model overlap and the launch "
@@ -620,6 +622,10 @@ def bench_kv(a, torch, dev, world, rank, dist, local):
     lens = torch.zeros(len(kv), 2, dtype=torch.int64, device=dev)
     stream = torch.cuda.current_stream(dev)
 
+    if a.enc_streams <= 0:
+        # one warp per chunk; about 36 chunk warps fit an SM (56 registers, 4-warp CTAs)
+        resident = torch.cuda.get_device_properties(dev).multi_processor_count * 36
+        a.enc_streams = max(1, min(16, math.ceil(3 * resident / max(1, -(-n // ce)))))
     encs = [enc] + [gpu.XcEncoder(n, ce, a.coder, a.prec, device=local) for _ in range(a.enc_streams - 1)]
     streams = [stream] + [torch.cuda.Stream(dev) for _ in range(a.enc_streams - 1)]
 
