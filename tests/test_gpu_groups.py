@@ -162,3 +162,15 @@ def test_noalloc_entry_point_takes_grouped_tensors():
     rc = _lib.load().bs_xc_decode_noalloc(arr, 1, ctypes.c_void_p(torch.cuda.current_stream().cuda_stream), st)
     assert rc == 0 and st[0] == 0
     assert out.cpu().numpy().tobytes() == raw
+
+
+@pytest.mark.parametrize("n,ce,groups", [((1 << 21) + 513, 65536, 8), (3 << 20, 1 << 20, 32)])
+def test_device_encoder_matches_oracle_on_sampled_tensors(n, ce, groups):
+    """From 2^20 values on the pair coder counts an eighth of the tensor; with
+    state groups the device encoder still writes the oracle's bytes."""
+    from bigsmall_b200 import gpu
+    raw = _wide(n, 21) if n % 2 else _normal(n, 21)
+    x = torch.from_numpy(np.frombuffer(raw, dtype=np.int16).copy()).cuda()
+    dev_blob = gpu.encode_xc(x, coder=2, chunk_elems=ce, groups=groups)
+    assert dev_blob.cpu().numpy().tobytes() == O.xc_encode(raw, 2, 12, ce, groups)
+    assert _decode(dev_blob.cpu().numpy().tobytes(), n, ce, groups) == raw
