@@ -7,7 +7,7 @@
 //   1. xc_enc_hist_kernel    exponent histogram (per-warp shared-memory bins)
 //                            and the sign|mantissa byte plane, one pass.
 //      Pair coder: xc_enc_expo_hist_kernel counts exponents only, over one
-//      eighth of a large tensor; xc_enc_window_kernel picks the 15-exponent
+//      eighth of a large tensor; the setup kernel picks the 15-exponent
 //      window and derives the pair-symbol counts from that histogram, as
 //      products of the two window-index marginals; the chunk encoder writes
 //      the plane.  The input is then read once in full, by the chunk encoder.
@@ -39,7 +39,6 @@ constexpr uint64_t kWsCounts = 0;       // u64[256] exponent histogram
 constexpr uint64_t kWsTab = 2048;       // u32[256]: freq | cum << 16
 constexpr uint64_t kWsFlags = 3072;     // u32 flags
 constexpr uint64_t kWsAux = 3076;       // u32 pair coder: window base e_lo
-constexpr uint64_t kWsPairCounts = 4096;   // u64[256] pair-symbol histogram
 constexpr uint64_t kWsRcp = 6144;       // uint4[256]: rANS encode-step entries (rans_enc_entry)
 constexpr uint64_t kWsRec = 10240;      // u32[n_chunks] words per record, then u32[n_chunks] escapes
 
@@ -162,6 +161,74 @@ __global__ void __launch_bounds__(256) xc_enc_expo_hist_kernel(const uint16_t *_
     if (t) atomicAdd(&counts[threadIdx.x], static_cast<unsigned long long>(t));
 }
 
+// 2a. pair coder: exponent window and pair-symbol counts (in the setup block) -
+__device__ __forceinline__ uint32_t pair_a(uint32_t v, uint32_t e_lo) {
+    const uint32_t d = ((v >> 7) & 0xFF) - e_lo;   // wraps to a large value below e_lo
+    return min(d, 15u);
+}
+
+// The 15-wide exponent window holding the most values (lowest base on ties):
+// thread w sums window w, then a max reduction keeps the lowest w among equals.
+// Then the pair-symbol counts the frequencies are quantised from (a product
+// model: a pair codes two neighbouring values, whose exponents are close to
+// independent, so this costs about 0.001-0.007 bits per value against the
+// pairs' own histogram and saves a pass over the input):
+//   s     values the histogram counted (n, or the sample of xc_enc_expo_hist_kernel),
+//   c(a)  counted values with window index a (a = 15: outside the window),
+//   m(a)  = max(1, c(a) * 2^16 / s) if c(a) > 0; else 1 for a sampled
+//         histogram (the rest of the tensor may hold such values), 0 otherwise,
+//   pc(a*16 + b) = m(a) * m(b), plus 1 at (a of the last value, 0) when n is
+//   odd (that value's pair has the phantom b = 0, so its symbol needs f > 0).
+// Run by all 256 threads of the setup block; returns pc(threadIdx.x) and
+// stores e_lo at *aux.
+__device__ unsigned long long pair_counts_block(const unsigned long long *counts,
+                                                const uint16_t *__restrict__ in, uint64_t n, uint32_t *aux) {
+    __shared__ unsigned long long c[256];
+    __shared__ unsigned long long s_m[8];
+    __shared__ uint32_t s_w[8];
+    __shared__ unsigned long long s_marg[16];
+    __shared__ uint32_t s_elo;
+    const uint32_t t = threadIdx.x, lane = t & 31;
+    c[t] = counts[t];
+    __syncthreads();
+    unsigned long long m = 0;
+    uint32_t w = 0xFFFFu;                         // not a window: loses every comparison
+    if (t + 14 < 256) {
+        for (int k = 0; k < 15; k++) m += c[t + k];
+        w = t;
+    }
+    auto better = [](unsigned long long m1, uint32_t w1, unsigned long long m0, uint32_t w0) {
+        return m1 > m0 || (m1 == m0 && w1 < w0);
+    };
+    for (int off = 16; off; off >>= 1) {
+        const unsigned long long om = __shfl_down_sync(kFull, m, off);
+        const uint32_t ow = __shfl_down_sync(kFull, w, off);
+        if (better(om, ow, m, w)) { m = om; w = ow; }
+    }
+    if (lane == 0) { s_m[t >> 5] = m; s_w[t >> 5] = w; }
+    __syncthreads();
+    if (t == 0) {
+        for (int k = 1; k < 8; k++)
+            if (better(s_m[k], s_w[k], m, w)) { m = s_m[k]; w = s_w[k]; }
+        *aux = w;
+        s_elo = w;
+    }
+    __syncthreads();
+    const uint32_t e_lo = s_elo;
+    if (t < 16) {
+        unsigned long long counted = 0, inside = 0;
+        for (int k = 0; k < 256; k++) counted += c[k];
+        for (int k = 0; k < 15; k++) inside += c[e_lo + k];
+        const unsigned long long ca = t < 15 ? c[e_lo + t] : counted - inside;
+        const unsigned long long q = (ca << 16) / counted;
+        s_marg[t] = ca ? (q ? q : 1ull) : (n >= kSampleMin ? 1ull : 0ull);
+    }
+    __syncthreads();
+    unsigned long long pc = s_marg[t >> 4] * s_marg[t & 15];
+    if ((n & 1) && t == pair_a(in[n - 1], e_lo) * 16) pc += 1;
+    return pc;
+}
+
 // 2. quantise + header -----------------------------------------------------
 // Same rule as the CPU reference encoder of the format: f = max(1, c*M/total)
 // for present symbols; a positive remainder goes to the most frequent symbol
@@ -169,10 +236,11 @@ __global__ void __launch_bounds__(256) xc_enc_expo_hist_kernel(const uint16_t *_
 // never below 1; a single present symbol gets M-1 plus a phantom neighbour.
 // `ce` / `nc` are the values per state group and the group count (the coded
 // units); the header names chunks of ce * groups values.
-__global__ void __launch_bounds__(256) xc_enc_setup_kernel(const unsigned long long *counts, uint64_t n,
+__global__ void __launch_bounds__(256) xc_enc_setup_kernel(const unsigned long long *counts,
+                                                           const uint16_t *__restrict__ in, uint64_t n,
                                                            int coder, int prec, uint32_t ce, uint32_t nc,
                                                            uint32_t groups, uint8_t *out, uint32_t *enc_tab,
-                                                           uint16_t *slot_list, const uint32_t *aux) {
+                                                           uint16_t *slot_list, uint32_t *aux) {
     __shared__ int64_t f[256];
     __shared__ uint32_t s_cum[256];
     __shared__ uint8_t s_spread[kXcMaxTable];
@@ -205,7 +273,9 @@ __global__ void __launch_bounds__(256) xc_enc_setup_kernel(const unsigned long l
         for (int w = 0; w < 8; w++) r += s_red[w];
         return r;
     };
-    const unsigned long long c = counts[tid];
+    // the pair coder quantises its pair-symbol counts (window and product
+    // model above); the others the exponent histogram itself
+    const unsigned long long c = coder == BS_CODER_RANS_PAIR ? pair_counts_block(counts, in, n, aux) : counts[tid];
     unsigned long long tot = c;
 #pragma unroll
     for (int d = 16; d > 0; d >>= 1) tot += __shfl_xor_sync(0xFFFFFFFFu, tot, d);
@@ -316,73 +386,6 @@ __global__ void __launch_bounds__(256) xc_enc_setup_kernel(const unsigned long l
             __syncwarp();
         }
     }
-}
-
-// 2b. pair coder: exponent window and pair-symbol counts ---------------------
-__device__ __forceinline__ uint32_t pair_a(uint32_t v, uint32_t e_lo) {
-    const uint32_t d = ((v >> 7) & 0xFF) - e_lo;   // wraps to a large value below e_lo
-    return min(d, 15u);
-}
-
-// The 15-wide exponent window holding the most values (lowest base on ties):
-// thread w sums window w, then a max reduction keeps the lowest w among equals.
-// Then the pair-symbol counts the frequencies are quantised from (a product
-// model: a pair codes two neighbouring values, whose exponents are close to
-// independent, so this costs about 0.001-0.007 bits per value against the
-// pairs' own histogram and saves a pass over the input):
-//   s     values the histogram counted (n, or the sample of xc_enc_expo_hist_kernel),
-//   c(a)  counted values with window index a (a = 15: outside the window),
-//   m(a)  = max(1, c(a) * 2^16 / s) if c(a) > 0; else 1 for a sampled
-//         histogram (the rest of the tensor may hold such values), 0 otherwise,
-//   pc(a*16 + b) = m(a) * m(b), plus 1 at (a of the last value, 0) when n is
-//   odd (that value's pair has the phantom b = 0, so its symbol needs f > 0).
-__global__ void __launch_bounds__(256) xc_enc_window_kernel(const unsigned long long *counts,
-                                                            const uint16_t *__restrict__ in, uint64_t n,
-                                                            uint32_t *aux, unsigned long long *pcounts) {
-    __shared__ unsigned long long c[256];
-    __shared__ unsigned long long s_m[8];
-    __shared__ uint32_t s_w[8];
-    __shared__ unsigned long long s_marg[16];
-    __shared__ uint32_t s_elo;
-    const uint32_t t = threadIdx.x, lane = t & 31;
-    c[t] = counts[t];
-    __syncthreads();
-    unsigned long long m = 0;
-    uint32_t w = 0xFFFFu;                         // not a window: loses every comparison
-    if (t + 14 < 256) {
-        for (int k = 0; k < 15; k++) m += c[t + k];
-        w = t;
-    }
-    auto better = [](unsigned long long m1, uint32_t w1, unsigned long long m0, uint32_t w0) {
-        return m1 > m0 || (m1 == m0 && w1 < w0);
-    };
-    for (int off = 16; off; off >>= 1) {
-        const unsigned long long om = __shfl_down_sync(kFull, m, off);
-        const uint32_t ow = __shfl_down_sync(kFull, w, off);
-        if (better(om, ow, m, w)) { m = om; w = ow; }
-    }
-    if (lane == 0) { s_m[t >> 5] = m; s_w[t >> 5] = w; }
-    __syncthreads();
-    if (t == 0) {
-        for (int k = 1; k < 8; k++)
-            if (better(s_m[k], s_w[k], m, w)) { m = s_m[k]; w = s_w[k]; }
-        *aux = w;
-        s_elo = w;
-    }
-    __syncthreads();
-    const uint32_t e_lo = s_elo;
-    if (t < 16) {
-        unsigned long long counted = 0, inside = 0;
-        for (int k = 0; k < 256; k++) counted += c[k];
-        for (int k = 0; k < 15; k++) inside += c[e_lo + k];
-        const unsigned long long ca = t < 15 ? c[e_lo + t] : counted - inside;
-        const unsigned long long q = (ca << 16) / counted;
-        s_marg[t] = ca ? (q ? q : 1ull) : (n >= kSampleMin ? 1ull : 0ull);
-    }
-    __syncthreads();
-    unsigned long long pc = s_marg[t >> 4] * s_marg[t & 15];
-    if ((n & 1) && t == pair_a(in[n - 1], e_lo) * 16) pc += 1;
-    pcounts[t] = pc;
 }
 
 // 3c. per-chunk reverse rANS over exponent pairs, with the escape list -------
@@ -768,7 +771,6 @@ cudaError_t launch_xc_encode(const uint16_t *d_in, uint64_t n, int coder, int pr
     auto *rcp = reinterpret_cast<const uint4 *>(d_ws + kWsRcp);
     auto *flags = reinterpret_cast<uint32_t *>(d_ws + kWsFlags);
     auto *aux = reinterpret_cast<uint32_t *>(d_ws + kWsAux);
-    auto *pcounts = reinterpret_cast<unsigned long long *>(d_ws + kWsPairCounts);
     auto *recw = reinterpret_cast<uint32_t *>(d_ws + kWsRec);
     auto *rece = recw + nc;
     uint8_t *slots = d_ws + slots_off(nc);
@@ -785,15 +787,11 @@ cudaError_t launch_xc_encode(const uint16_t *d_in, uint64_t n, int coder, int pr
     uint64_t want = (vecs + 255) / 256;
     int grid = static_cast<int>(want < static_cast<uint64_t>(sms) * 8 ? (want ? want : 1) : static_cast<uint64_t>(sms) * 8);
     uint16_t *slot_list = reinterpret_cast<uint16_t *>(d_ws + slotlist_off(nc));
-    const unsigned long long *qcounts = counts;
-    if (pair) {
+    if (pair)
         xc_enc_expo_hist_kernel<<<grid, 256, 0, s>>>(d_in, n, counts);
-        xc_enc_window_kernel<<<1, 256, 0, s>>>(counts, d_in, n, aux, pcounts);
-        qcounts = pcounts;
-    } else {
+    else
         xc_enc_hist_kernel<<<grid, 256, 0, s>>>(d_in, n, counts, d_out + plane_off);
-    }
-    xc_enc_setup_kernel<<<1, 256, 0, s>>>(qcounts, n, coder, prec, ce, static_cast<uint32_t>(nc), groups, d_out,
+    xc_enc_setup_kernel<<<1, 256, 0, s>>>(counts, d_in, n, coder, prec, ce, static_cast<uint32_t>(nc), groups, d_out,
                                           tab, slot_list, aux);
     const unsigned enc_blocks = static_cast<unsigned>((nc + kEncWarps - 1) / kEncWarps);
     if (coder == BS_CODER_RANS_PAIR) {
