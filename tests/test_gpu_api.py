@@ -124,12 +124,16 @@ def test_unknown_codec_raises_version_error():
 def test_ac_cuda_slot_and_registry(manifest):
     from bigsmall_b200 import codec_registry, kernels
     from bigsmall_b200.kernels import ac_cuda
-    assert kernels.use_gpu() and kernels.backend_name() == "cuda_c"
+    kernels._GPU_BACKEND = None          # re-probe, as the reference's tests do
+    kernels._GPU_DECODE_FN = None
+    assert kernels.use_gpu() is True and kernels.backend_name() == "cuda_c"
     c = manifest["cases"]["edge"]
     blob = golden_bytes(c["blobs"]["par128"]["file"])
     out = ac_cuda.decode(blob, {"n_streams": 128}, c["n"])
     assert hashlib.md5(out).hexdigest() == c["raw_md5"]
     assert kernels.decode_bf16_parallel(blob, {}, c["n"]) == out
+    dev = ac_cuda.decode_to_device(blob, {"n_streams": 128}, c["n"])
+    assert dev.is_cuda and dev.cpu().numpy().tobytes() == out
     enc, dec = codec_registry.get_codec("bf16_exp_chunked_v1")
     raw = golden_bytes("c1_head_16k.raw")
     b, extras = enc(raw, chunk_elems=4096)
