@@ -271,6 +271,8 @@ def main():
                          "assigned round-robin, so consecutive tensors' encodes overlap; 0 = enough "
                          "tensors in flight for about three waves of chunk warps (4 for a config-5 "
                          "tensor on one GPU, up to 16 for the smaller batch slices of 8 GPUs)")
+    ap.add_argument("--enc-graph", type=int, default=1,
+                    help="config kv: replay the step's encode launches as one CUDA graph (1) or launch them (0)")
     ap.add_argument("--prefill-timeline", action="store_true",
                     help="config stream: also record one prefill of each model with the CUDA profiler (CUPTI "
                          "kernel records) and report GPU busy time, decode/model overlap and the launch "
@@ -630,15 +632,35 @@ def bench_kv(a, torch, dev, world, rank, dist, local):
     streams = [stream] + [torch.cuda.Stream(dev) for _ in range(a.enc_streams - 1)]
 
     def encode_all():
+        s0 = torch.cuda.current_stream(dev)
         for s in streams[1:]:
-            s.wait_stream(stream)
+            s.wait_stream(s0)
         for i, x in enumerate(kv):
             k = i % len(encs)
-            encs[k].encode_into(x, outs[i], lens[i], streams[k])
+            encs[k].encode_into(x, outs[i], lens[i], s0 if k == 0 else streams[k])
         for s in streams[1:]:
-            stream.wait_stream(s)
+            s0.wait_stream(s)
 
-    enc_ms = _timed(torch, encode_all, a.steps, a.warmup, stream)
+    # The step's launches (five kernels per tensor, 64 tensors) replay as one
+    # CUDA graph: with small per-rank tensors the host would otherwise set the
+    # pace.  Each replay runs every encode in full.
+    enc_fn, enc_graph = encode_all, None
+    if a.enc_graph:
+        try:
+            encode_all()
+            torch.cuda.synchronize(dev)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, capture_error_mode="relaxed"):
+                encode_all()
+            enc_fn, enc_graph = graph.replay, graph
+        except RuntimeError as exc:   # capture refused: time the eager launches instead
+            print(f"encode graph capture failed, eager launches: {exc}", file=sys.stderr)
+            torch.cuda.synchronize(dev)
+    enc_ms = _timed(torch, enc_fn, a.steps, a.warmup, stream)
+    used_graph = enc_graph is not None
+    if enc_graph is not None:
+        enc_graph.reset()
+        enc_graph = None
     ln = lens[:, 0].tolist()
     blobs = [o[:int(l)] for o, l in zip(outs, ln)]
     dec = [torch.empty_like(x) for x in kv]
@@ -672,7 +694,8 @@ def bench_kv(a, torch, dev, world, rank, dist, local):
             "config": {"workload": f"{L} layers x {{K,V}} [16,8,8192,128] bf16, N(0,1) x log-normal per-channel "
                                    "scale, seed 0; batch sharded across ranks"
                                    + ("" if L == 32 else " (reduced case; config 5 is 32 layers)"),
-                       "chunk_elems": ce, "coder": a.coder, "encode_streams": a.enc_streams},
+                       "chunk_elems": ce, "coder": a.coder, "encode_streams": a.enc_streams,
+                       "encode_graph": used_graph},
             "verified": "bitwise equal" if bad == 0 else f"MISMATCH on {int(bad)} ranks"}), flush=True)
     plan.close()
     if dist:
