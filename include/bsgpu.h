@@ -227,7 +227,9 @@ int bs_xc_encode_workspace(uint64_t n_elems, uint32_t chunk_elems, uint32_t grou
  * reference encoder's.  Coder 2 quantises a product of its two window-index
  * marginals, counted over every value, or for n_elems >= 2^20 over the
  * 2048-value blocks whose index is a multiple of 8; coders 0 and 1 count every
- * value.  Asynchronous on `stream`.
+ * value.  Asynchronous on `stream`: one memset and five kernels, so a run of
+ * encodes can be captured into a CUDA graph (relaxed capture mode; the KV
+ * benchmark replays a whole step of 64 encodes that way).
  * Replaces: bigsmall/codecs/kv_cache.py:41-83 compress_kv_entry's CPU encode. */
 int bs_xc_encode(const void *d_in, uint64_t n_elems, int coder, int prec,
                  uint32_t chunk_elems, uint32_t groups, void *d_out, uint64_t out_cap,
