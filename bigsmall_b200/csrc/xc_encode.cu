@@ -707,6 +707,25 @@ __device__ __forceinline__ uint32_t ld_u32_any(const uint8_t *p) {
     return __funnelshift_r(base[0], base[1], 8 * k);
 }
 
+// 16 bytes from any address: the two aligned 16-byte blocks holding them,
+// funnel-shifted (nothing outside those blocks is read).  The misalignment is
+// the same for every piece of a record's region, so the switch is uniform.
+__device__ __forceinline__ uint4 ld_u128_any(const uint8_t *p) {
+    const uintptr_t a = reinterpret_cast<uintptr_t>(p);
+    const uint4 *b = reinterpret_cast<const uint4 *>(a & ~static_cast<uintptr_t>(15));
+    const uint32_t k = static_cast<uint32_t>(a & 15);
+    if (k == 0) return b[0];
+    const uint4 lo = b[0], hi = b[1];
+    const uint32_t s = 8 * (k & 3);
+    auto f = [s](uint32_t x, uint32_t y) { return __funnelshift_r(x, y, s); };
+    switch (k >> 2) {
+        case 0: return make_uint4(f(lo.x, lo.y), f(lo.y, lo.z), f(lo.z, lo.w), f(lo.w, hi.x));
+        case 1: return make_uint4(f(lo.y, lo.z), f(lo.z, lo.w), f(lo.w, hi.x), f(hi.x, hi.y));
+        case 2: return make_uint4(f(lo.z, lo.w), f(lo.w, hi.x), f(hi.x, hi.y), f(hi.y, hi.z));
+        default: return make_uint4(f(lo.w, hi.x), f(hi.x, hi.y), f(hi.y, hi.z), f(hi.z, hi.w));
+    }
+}
+
 __global__ void __launch_bounds__(256) xc_enc_compact_kernel(const uint8_t *__restrict__ slots, uint64_t slot_b,
                                                              const uint32_t *__restrict__ rec_words,
                                                              const uint32_t *__restrict__ rec_esc,
@@ -733,13 +752,23 @@ __global__ void __launch_bounds__(256) xc_enc_compact_kernel(const uint8_t *__re
     }
     const uint8_t *ws = coder == BS_CODER_TANS ? slot + 128 : slot + slot_b - 2ull * W;
     const uint8_t *es = slot + hdr + ce - E;
-    // body = words, escapes, zero pad: 16 bytes per thread and pass, each
-    // 32-bit piece funnel-shifted from aligned loads of the source region it
-    // lies in (words start 2-byte aligned, escapes anywhere)
+    // body = words, escapes, zero pad: 16 bytes per thread and pass, shifted
+    // from aligned 16-byte loads of the source region they lie in (words start
+    // 2-byte aligned, escapes anywhere); the piece across the words/escapes
+    // edge and the pad go 32 bits, then bytes, at a time
     const uint32_t wb = 2u * W, eb = wb + E;
     const uint32_t body = ((hdr + eb + 15u) & ~15u) - hdr;
     uint4 *bd = reinterpret_cast<uint4 *>(dst + hdr);
     for (uint32_t v = threadIdx.x; v < body / 16; v += blockDim.x) {
+        const uint32_t j0 = 16 * v;
+        if (j0 + 16 <= wb) {
+            bd[v] = ld_u128_any(ws + j0);
+            continue;
+        }
+        if (j0 >= wb && j0 + 16 <= eb) {
+            bd[v] = ld_u128_any(es + (j0 - wb));
+            continue;
+        }
         uint32_t o[4];
 #pragma unroll
         for (int k = 0; k < 4; k++) {
