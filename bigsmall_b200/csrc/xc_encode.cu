@@ -661,28 +661,40 @@ __global__ void __launch_bounds__(1024) xc_enc_scan_kernel(const uint32_t *__res
                                                            const uint32_t *__restrict__ rec_esc, int coder, uint32_t nc,
                                                            uint8_t *out, uint64_t chunks_off, uint64_t out_cap,
                                                            unsigned long long *out_len, uint32_t *flags) {
-    __shared__ uint64_t s_part[1024];
-    const uint32_t tid = threadIdx.x;
+    __shared__ uint64_t s_warp[32];
+    const uint32_t tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const uint32_t per = (nc + 1023) / 1024;
     const uint32_t lo = tid * per, hi = min(nc, lo + per);
     uint64_t sum = 0;
     for (uint32_t c = lo; c < hi; c++) sum += rec16(rec_words, rec_esc, c, coder);
-    s_part[tid] = sum;
-    __syncthreads();
-    for (uint32_t d = 1; d < 1024; d <<= 1) {
-        uint64_t v = tid >= d ? s_part[tid - d] : 0;
-        __syncthreads();
-        s_part[tid] += v;
-        __syncthreads();
+    // block-wide inclusive scan of the per-thread sums: within each warp by
+    // shuffles, then over the 32 warp totals by the first warp
+    uint64_t inc = sum;
+#pragma unroll
+    for (uint32_t d = 1; d < 32; d <<= 1) {
+        const uint64_t v = __shfl_up_sync(kFull, inc, d);
+        if (lane >= d) inc += v;
     }
-    uint64_t run = s_part[tid] - sum;   // exclusive
+    if (lane == 31) s_warp[warp] = inc;
+    __syncthreads();
+    if (warp == 0) {
+        uint64_t t = s_warp[lane];
+#pragma unroll
+        for (uint32_t d = 1; d < 32; d <<= 1) {
+            const uint64_t v = __shfl_up_sync(kFull, t, d);
+            if (lane >= d) t += v;
+        }
+        s_warp[lane] = t;
+    }
+    __syncthreads();
+    uint64_t run = (warp ? s_warp[warp - 1] : 0ull) + inc - sum;   // exclusive
     uint32_t *tab = reinterpret_cast<uint32_t *>(out + kXcTabOff);
     for (uint32_t c = lo; c < hi; c++) {
         tab[c] = static_cast<uint32_t>(run);
         run += rec16(rec_words, rec_esc, c, coder);
     }
     if (tid == 1023) {
-        const uint64_t total16 = s_part[1023];
+        const uint64_t total16 = s_warp[31];
         tab[nc] = static_cast<uint32_t>(total16);
         const uint64_t total = chunks_off + 16 * total16;
         if (total > out_cap) {
